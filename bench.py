@@ -1,0 +1,413 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 fp16 -> fp32 GEMM (BASELINE.json metric: TFLOP/s and % of B200
+dense FP16 peak, 8192^3 fp16 -> fp32 GEMM, 1/2/4/8 GPU).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+One step = one 8192 x 8192 x 8192 GEMM per GPU.  With N > 1 (one
+process per GPU under torchrun) rank r owns rows [8192 r, 8192 (r+1)) of an
+(8192 N) x 8192 x 8192 GEMM: M-row slabs, B broadcast once from rank 0 over NCCL at
+set-up, C written locally with no reduction (weak scaling: per-GPU work fixed).
+
+Prints one JSON line (rank 0).  value = all ranks' FLOPs / max-over-ranks device time of K
+steps with inputs resident in HBM.  e2e = the same metric through the public C ABI with
+host buffers: each step copies A and B from pinned host memory and reads C back.
+--impl reference times the reference's arithmetic on the host CPU (the oracle's blocked
+port of GEMM_Naive, mmm.cpp:52-62; the HIP reference cannot run here).
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SPEC_TFLOPS = 2250.0   # B200 dense fp16 tensor peak (spec)
+M_PER_GPU = N_DIM = K_DIM = 8192
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+
+
+def load_b2g():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "b2g", os.path.join(ROOT, "rdna4-gemm-wmma_b200", "b2g.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.load()
+    return mod
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the top kernel from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "gemm_tc_kernel_8192.md")
+    try:
+        for line in open(p):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        time.sleep(0.3)
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=5)
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm, mx, pw = float(parts[1]), float(parts[2]), float(parts[3])
+            except ValueError:
+                continue
+            if pw < 200:  # not under load (before the first / after the last launch)
+                continue
+            sms.append(sm)
+            maxs.append(mx)
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def cpu_baseline(seconds, threads=None):
+    """The oracle's blocked multithreaded GEMM (GEMM_Naive arithmetic, bit-exact) on a row
+    sample of the 8192^3 problem; returns TFLOP/s, rows done, seconds, threads."""
+    from oracle import orc
+    A = orc.uniform_f16((M_PER_GPU, K_DIM), 1)
+    B = orc.uniform_f16((K_DIM, N_DIM), 2)
+    thr = threads or orc.nthreads()
+    t0 = time.perf_counter()
+    Bf = orc.widen_b(B, threads=thr)
+    t_widen = time.perf_counter() - t0
+    rows_done, t_rows = 0, 0.0
+    chunk = 48
+    while t_rows < seconds and rows_done + chunk <= M_PER_GPU:
+        t0 = time.perf_counter()
+        orc.gemm_f32_blocked(A, B, rows=(rows_done, rows_done + chunk), threads=thr, Bf=Bf)
+        dt = time.perf_counter() - t0
+        t_rows += dt
+        rows_done += chunk
+        if dt < 0.5:
+            chunk = min(chunk * 2, 768)
+    # the one-time widening of B is charged pro rata to the rows computed
+    t = t_rows + t_widen * rows_done / M_PER_GPU
+    flops = 2.0 * rows_done * N_DIM * K_DIM
+    return flops / t / 1e12, rows_done, t, thr
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import orc
+    thr = orc.nthreads()
+    A = orc.uniform_f16((M_PER_GPU, K_DIM), 1)
+    B = orc.uniform_f16((K_DIM, N_DIM), 2)
+    t0 = time.perf_counter()
+    Bf = orc.widen_b(B, threads=thr)
+    t_widen = time.perf_counter() - t0
+    # size each step so the whole run takes about a minute
+    t0 = time.perf_counter()
+    orc.gemm_f32_blocked(A, B, rows=(0, 48), threads=thr, Bf=Bf)
+    per_row = (time.perf_counter() - t0) / 48
+    budget = 60.0 / max(1, args.steps + args.warmup)
+    rows = int(max(6, min(M_PER_GPU, budget / per_row)) // 6 * 6)
+    r0 = 0
+    for _ in range(args.warmup):
+        orc.gemm_f32_blocked(A, B, rows=(r0, r0 + rows), threads=thr, Bf=Bf)
+    times = []
+    for s in range(args.steps):
+        r0 = (s * rows) % max(1, M_PER_GPU - rows)
+        t0 = time.perf_counter()
+        orc.gemm_f32_blocked(A, B, rows=(r0, r0 + rows), threads=thr, Bf=Bf)
+        times.append(time.perf_counter() - t0 + t_widen * rows / M_PER_GPU)
+    tot = sum(times)
+    val = 2.0 * rows * N_DIM * K_DIM * args.steps / tot / 1e12
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    line = {
+        "impl": "reference",
+        "metric": "gemm_tflops_8192cubed_fp16_fp32",
+        "value": val,
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": tot / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 in, f32 accumulate/out",
+        "data": "synthetic: seeded U[-1,1] fp16",
+        "config": {"workload": "gemm 8192x8192x8192 row-major fp16->fp32 (BASELINE configs[1])",
+                   "sample": "%d rows x 8192 x 8192 per step" % rows, "world_size": ws},
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": thr, "kind": "port",
+                         "sample": "%d of 8192 rows per step; blocked AVX2 port of GEMM_Naive "
+                                   "(mmm.cpp:52-62), bit-exact; B widening charged pro rata" % rows},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is HIP/rocBLAS for AMD gfx12 and cannot run on this box; this "
+                "arm is the CPU port of its arithmetic",
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b2g", choices=["b2g", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=12)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    b2g = load_b2g()
+
+    M, N, K = M_PER_GPU, N_DIM, K_DIM
+    flops = 2.0 * M * N * K
+    stream = torch.cuda.current_stream()
+    dA = torch.empty((M, K), dtype=torch.float16, device=dev)
+    dB = torch.empty((K, N), dtype=torch.float16, device=dev)
+    dC = torch.empty((M, N), dtype=torch.float32, device=dev)
+    # rank r's slab of the (M*ws) x K matrix A; B generated on rank 0 and broadcast once
+    b2g.fill_uniform(dA, M * K, 1, rank * M * K, stream)
+    if rank == 0:
+        b2g.fill_uniform(dB, K * N, 2, 0, stream)
+    if ws > 1:
+        dist.broadcast(dB, src=0)
+    torch.cuda.synchronize()
+
+    def step():
+        b2g.gemm(dA, dB, dC, M, N, K, K, N, N, stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if b2g.device_status() != 0:
+        raise SystemExit("device-side wait timed out during warm-up")
+
+    # per-launch events (roofline of the kernel), total events (value)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    if ws > 1:
+        dist.barrier()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    launch_ms = [a.elapsed_time(b) for a, b in ev]
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    path = b2g.PATH_NAMES.get(b2g.last_path(), "?")
+    if b2g.device_status() != 0:
+        raise SystemExit("device-side wait timed out during the timed region")
+
+    value = flops * ws * args.steps / (elapsed_ms * 1e-3) / 1e12
+    avg_launch_ms = statistics.mean(launch_ms)
+    achieved = flops / (avg_launch_ms * 1e-3) / 1e12
+
+    # ---- end to end through the C ABI with host buffers (pipelined over 3 streams)
+    e2e = e2e_run(torch, b2g, dev, M, N, K, rank, ws, args.e2e_steps, dist if ws > 1 else None)
+
+    peaks, peaks_src = measured_peaks()
+    sustained = elapsed_ms > 1000.0
+    peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        v, rows, secs, thr = cpu_baseline(args.cpu_seconds)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": thr, "kind": "port",
+               "sample": "%d of 8192 rows of the 8192^3 GEMM (%.1f s); blocked AVX2 port of "
+                         "GEMM_Naive (mmm.cpp:52-62), bit-exact; B widening charged pro rata"
+                         % (rows, secs)}
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {
+        "metric": "gemm_tflops_8192cubed_fp16_fp32",
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16 in, f32 accumulate/out",
+        "data": "synthetic: seeded U[-1,1] fp16 generated on the device (b2g_fill_uniform_f16)",
+        "config": {
+            "workload": "gemm 8192x8192x8192 row-major fp16->fp32 per GPU (BASELINE configs[1]);"
+                        " N>1: M-row slabs of a (8192N)x8192x8192 GEMM, B broadcast once",
+            "M": M, "N": N, "K": K, "world_size": ws, "path": path,
+            "l2": "inputs+output 512 MiB per GPU > 126 MB L2 (no flush needed)",
+            "frac_of_spec_2250": value / ws / SPEC_TFLOPS,
+        },
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": profiled_traffic(),
+                     "peak_source": "%s %s" % (peaks_src, "bf16_tflops_sustained" if sustained
+                                               else "bf16_tflops"),
+                     "kernel": "gemm_tc_kernel", "flops_per_launch": flops,
+                     "avg_launch_ms": avg_launch_ms},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def e2e_run(torch, b2g, dev, M, N, K, rank, ws, steps, dist):
+    """Pinned host A, B -> device, GEMM, C -> pinned host, every step.  Two buffer sets and
+    three streams (H2D, compute, D2H) let step i+1's upload overlap step i's download."""
+    import numpy as np
+    from oracle import orc  # input generation only (the seeded host sequence)
+    hA = torch.from_numpy(orc.uniform_f16((M, K), 1, rank * M * K).view(np.int16)).view(
+        torch.float16).pin_memory()
+    hB = torch.from_numpy(orc.uniform_f16((K, N), 2).view(np.int16)).view(torch.float16).pin_memory()
+    hC = [torch.empty((M, N), dtype=torch.float32).pin_memory() for _ in range(2)]
+    bufs = [(torch.empty((M, K), dtype=torch.float16, device=dev),
+             torch.empty((K, N), dtype=torch.float16, device=dev),
+             torch.empty((M, N), dtype=torch.float32, device=dev)) for _ in range(2)]
+    s_in, s_mm, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+    up = [torch.cuda.Event() for _ in range(2)]
+    mm = [torch.cuda.Event() for _ in range(2)]
+    down = [torch.cuda.Event() for _ in range(2)]
+
+    def run(n):
+        for i in range(n):
+            b = i & 1
+            a_, b_, c_ = bufs[b]
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(mm[b]) if i >= 2 else None
+                a_.copy_(hA, non_blocking=True)
+                b_.copy_(hB, non_blocking=True)
+                up[b].record(s_in)
+            s_mm.wait_event(up[b])
+            if i >= 2:
+                s_mm.wait_event(down[b])
+            b2g.gemm(a_, b_, c_, M, N, K, K, N, N, s_mm)
+            mm[b].record(s_mm)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(mm[b])
+                hC[b].copy_(c_, non_blocking=True)
+                down[b].record(s_out)
+
+    run(2)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record(s_in)
+    run(steps)
+    s_in.wait_stream(s_out)
+    t1.record(s_in)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # spot-check the result that came back (first row of the last step)
+    ref = orc.gemm_f64(orc.uniform_f16((1, K), 1, rank * M * K), orc.uniform_f16((K, N), 2))
+    bad = orc.check(hC[(steps - 1) & 1][:1].numpy(), ref, K, 1.0, 1.0)[0]
+    return {"value": 2.0 * M * N * K * ws * steps / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": (M * K + K * N) * 2, "d2h_bytes_per_step": M * N * 4,
+            "steps": steps, "ms_per_step": ms / steps, "row0_out_of_tolerance": bad,
+            "pipeline": "2 buffer sets, H2D / compute / D2H streams"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

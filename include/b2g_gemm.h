@@ -1,0 +1,138 @@
+/*
+ * b2g_gemm.h - C ABI of the B200 (sm_100a) GEMM and 5-D contraction library
+ * (libb2g_gemm.so).  Plain pointers and sizes only; no CUDA or framework types.
+ *
+ * Reference: thrasos-g/RDNA4-GEMM-WMMA.  The reference is two benchmark programs whose
+ * de-facto drop-in boundary is a kernel launch on the default stream with compile-time
+ * sizes; every entry point below cites the reference interface it replaces.
+ *
+ * Conventions (all entry points):
+ *   - Device pointers are owned by the caller.  A, B are IEEE fp16 (2-byte elements);
+ *     C is fp32.  C is overwritten (beta = 0), as the reference kernel does
+ *     (mmm.cpp:1372, mmmTensor.cpp:251).
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream, which is what the
+ *     reference launches on, mmm.cpp:1496).  Calls are asynchronous on that stream.
+ *   - Return 0 (B2G_OK) on success, else a B2G_ERR_* code; b2g_last_error_string()
+ *     returns a message for the calling thread's last failure.  (The reference aborts
+ *     the process from HIP_CHECK / ROCBLAS_CHECK, mmm.cpp:33-49.)
+ *   - Strides are in elements.  Any shape and stride set is accepted; layouts the
+ *     tensor-memory kernel cannot address through TMA (unaligned bases or strides,
+ *     no unit-stride K/N/M mode, ...) run on a generic CUDA kernel instead
+ *     (b2g_last_path() tells which).
+ *   - Numerics: fp32 accumulation of exact fp16 products.  Results agree with an FP64
+ *     reference within |err| <= 1e-3*sqrt(K)*max|a|*max|b| + 1e-3*|ref|.
+ *   - Thread-safe; calls from several host threads may run concurrently.
+ */
+#ifndef B2G_GEMM_H
+#define B2G_GEMM_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  B2G_OK = 0,
+  B2G_ERR_INVALID_ARG = 1, /* bad shape, stride or null pointer */
+  B2G_ERR_UNSUPPORTED = 2, /* valid request this build cannot run (e.g. no sm_100 device) */
+  B2G_ERR_CUDA = 3,        /* a CUDA runtime/driver call failed */
+  B2G_ERR_TIMEOUT = 4,     /* a bounded device-side wait gave up (see b2g_device_status) */
+  B2G_ERR_NCCL = 5,        /* collective failure in the sharded path */
+};
+
+/* Which kernel the calling thread's last successful compute call ran. */
+enum {
+  B2G_PATH_NONE = 0,
+  B2G_PATH_TC_1CTA = 1,   /* tcgen05 kernel, one CTA per 128x256 tile */
+  B2G_PATH_TC_2CTA = 2,   /* tcgen05 kernel, CTA pair per 256x256 tile (cta_group::2) */
+  B2G_PATH_GENERIC = 3,   /* generic CUDA kernel (layouts outside TMA's rules) */
+  B2G_PATH_ZERO = 4,      /* K == 0: C filled with zeros */
+  B2G_PATH_EMPTY = 5,     /* M == 0 or N == 0: nothing to do */
+};
+
+/*
+ * C[M,N] = A[M,K] . B[K,N], all row-major: A[m*lda + k], B[k*ldb + n], C[m*ldc + n].
+ * Replaces the launch of WMMA_Swizzled_Full<2,2,4,4> (mmm.cpp:1214-1215 signature,
+ * 1462-1472 launch configuration, 1496 launch), whose sizes are the compile-time globals
+ * DIM_I/DIM_J/DIM_K (mmm.cpp:13-15) with lda = K, ldb = N, ldc = N; here they are
+ * arguments.
+ */
+int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K,
+                     int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+
+/*
+ * The reference's drop-in form: contiguous row-major operands, lda = K, ldb = N, ldc = N,
+ * default stream.  Same as GEMM_Naive's contract (mmm.cpp:52-62).
+ */
+int b2g_gemm(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K);
+
+/*
+ * 5-D contraction C[a,b,i,n] = sum_{j,k} A[a,b,i,j,k] * B[j,k,n].
+ *   a_shape = (a,b,i,j,k), b_shape = (j,k,n), c_shape = (a,b,i,n); *_stride in elements.
+ * Read in place through TMA tensor maps on these strides: no packed copy is made.
+ * Replaces mmmTensor.cpp: the host pack of G into A (329-340) plus the contraction
+ * kernel launch (44-45 signature, 345-355 launch configuration, 364-369 launch) with its
+ * K-major Input read (168) and remapped Output store (246-252).  The reference's own
+ * form Out[m,b,r] = sum_{n,k} G[r,n,m,k] * In[b,n,k] is this call with
+ *   a_shape = (mt, 1, rt, nt, rt_l), a_stride = (rt_l, 0, nt*mt*rt_l, mt*rt_l, 1),
+ *   b_shape = (nt, rt_l, bt),        b_stride = (rt_l, 1, nt*rt_l),
+ *   c_shape = (mt, 1, rt, bt),       c_stride = (bt*rt, 0, 1, rt).
+ */
+int b2g_contract5d_f16_f32(const void* A, const int64_t a_shape[5], const int64_t a_stride[5],
+                           const void* B, const int64_t b_shape[3], const int64_t b_stride[3],
+                           float* C, const int64_t c_shape[4], const int64_t c_stride[4],
+                           void* stream);
+
+/*
+ * Fill n fp16 elements with the seeded uniform [-1,1] sequence: element e of the logical
+ * stream is f(seed, offset + e).  Bit-identical to the host oracle, so a row slab of a
+ * large matrix can be generated on the GPU that owns it.  Replaces randomMatrix
+ * (mmm.cpp:1409-1414, mmmTensor.cpp:271-276: rand()/RAND_MAX, U[0,1], unseeded).
+ */
+int b2g_fill_uniform_f16(void* dst, int64_t n, uint64_t seed, uint64_t offset, void* stream);
+
+/* Message for the calling thread's last failed call ("" if none). */
+const char* b2g_last_error_string(void);
+
+/* Path taken by the calling thread's last successful compute call (B2G_PATH_*). */
+int b2g_last_path(void);
+
+/*
+ * Device-side error word of the current device: 0 if every bounded wait completed, else
+ * the code of the first wait that gave up.  Synchronises the device.  clear != 0 resets
+ * the word.  Returns -1 if the word could not be read.  (No reference counterpart: the
+ * reference has no device-side failure detection.)
+ */
+int b2g_device_status(int clear);
+
+/*
+ * Tuning / test options (no reference counterpart; the reference selects kernels by
+ * editing source, mmm.cpp:1489,1494).  Keys:
+ *   "cta_group"    0 = choose by shape (default), 1 = one CTA per tile, 2 = CTA pairs
+ *   "raster_group" strip height of the persistent tile order (0 = default)
+ *   "timeout_ns"   limit of every bounded device-side wait (default 2e9)
+ *   "force_generic" 1 = run the generic kernel for every call (testing)
+ *   "fault_flags"  test-only fault injection: bit 0 = the TMA producer issues no loads,
+ *                  so the MMA wait runs out and the call reports B2G_ERR_TIMEOUT
+ * Returns B2G_OK or B2G_ERR_INVALID_ARG for an unknown key.  Options are process-wide.
+ */
+int b2g_set_option(const char* key, int64_t value);
+int64_t b2g_get_option(const char* key);
+
+/*
+ * Host mirror of the persistent kernel's tile order: tile index t of a num_m x num_n
+ * tile grid visited in strips of `group` M-tiles -> (tm, tn).  A bijection for every
+ * shape (the reference's strip remap, mmm.cpp:1219-1236, is not when the grid width is
+ * not a multiple of 32).  Exposed for host-side tests.
+ */
+void b2g_tile_coord(int t, int num_m, int num_n, int group, int* tm, int* tn);
+
+/* Library version string. */
+const char* b2g_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* B2G_GEMM_H */

@@ -1,0 +1,169 @@
+"""ctypes binding of libb2g_gemm.so, the C ABI declared in include/b2g_gemm.h.
+
+This is the Python mirror of the reference's drop-in surface: GEMM(A, B, C, M, N, K) for
+the kernel launch of mmm.cpp:1496 and contract5d(...) for the G pack + contraction launch
+of mmmTensor.cpp:329-369.  Operands are device pointers (ints) or objects exposing
+``data_ptr()`` (e.g. torch CUDA tensors, used only as device-memory plumbing).
+
+The binding never computes anything itself: if the shared library is missing it raises,
+and every call goes to the CUDA kernels.
+"""
+import ctypes
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "libb2g_gemm.so")
+HEADER = os.path.join(ROOT, "include", "b2g_gemm.h")
+
+OK = 0
+ERR_INVALID_ARG = 1
+ERR_UNSUPPORTED = 2
+ERR_CUDA = 3
+ERR_TIMEOUT = 4
+ERR_NCCL = 5
+
+PATH_NONE, PATH_TC_1CTA, PATH_TC_2CTA, PATH_GENERIC, PATH_ZERO, PATH_EMPTY = range(6)
+PATH_NAMES = {0: "none", 1: "tc_1cta", 2: "tc_2cta", 3: "generic", 4: "zero", 5: "empty"}
+
+
+class B2GError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__("b2g error %d: %s" % (code, msg))
+        self.code = code
+
+
+_lib = None
+
+
+def load(path=None):
+    """Load libb2g_gemm.so (built by build.py).  Raises if it is missing."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise FileNotFoundError(
+            "libb2g_gemm.so not found at %s; build it with python rdna4-gemm-wmma_b200/build.py" % p)
+    L = ctypes.CDLL(p)
+    i64, vp = ctypes.c_int64, ctypes.c_void_p
+    i64p = ctypes.POINTER(ctypes.c_int64)
+    L.b2g_gemm_f16_f32.restype = ctypes.c_int
+    L.b2g_gemm_f16_f32.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
+    L.b2g_gemm.restype = ctypes.c_int
+    L.b2g_gemm.argtypes = [vp, vp, vp, i64, i64, i64]
+    L.b2g_contract5d_f16_f32.restype = ctypes.c_int
+    L.b2g_contract5d_f16_f32.argtypes = [vp, i64p, i64p, vp, i64p, i64p, vp, i64p, i64p, vp]
+    L.b2g_fill_uniform_f16.restype = ctypes.c_int
+    L.b2g_fill_uniform_f16.argtypes = [vp, i64, ctypes.c_uint64, ctypes.c_uint64, vp]
+    L.b2g_last_error_string.restype = ctypes.c_char_p
+    L.b2g_last_error_string.argtypes = []
+    L.b2g_last_path.restype = ctypes.c_int
+    L.b2g_device_status.restype = ctypes.c_int
+    L.b2g_device_status.argtypes = [ctypes.c_int]
+    L.b2g_set_option.restype = ctypes.c_int
+    L.b2g_set_option.argtypes = [ctypes.c_char_p, i64]
+    L.b2g_get_option.restype = i64
+    L.b2g_get_option.argtypes = [ctypes.c_char_p]
+    L.b2g_tile_coord.restype = None
+    L.b2g_tile_coord.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int)] * 2
+    L.b2g_version.restype = ctypes.c_char_p
+    if path is None:
+        _lib = L
+    return L
+
+
+def declared_symbols(header=HEADER):
+    """Names of the functions include/b2g_gemm.h declares."""
+    txt = open(header).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(b2g_[a-z0-9_]+)\s*\(", txt)))
+
+
+def _ptr(x):
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    raise TypeError("expected a device pointer (int) or an object with data_ptr()")
+
+
+def _stream(s):
+    if s is None:
+        try:
+            import torch  # plumbing only: the caller's current stream
+            if torch.cuda.is_available():
+                return torch.cuda.current_stream().cuda_stream
+        except ImportError:
+            pass
+        return None
+    if isinstance(s, int):
+        return s
+    return s.cuda_stream
+
+
+def _check(rc):
+    if rc != OK:
+        raise B2GError(rc, load().b2g_last_error_string().decode())
+
+
+def gemm(A, B, C, M, N, K, lda=None, ldb=None, ldc=None, stream=None):
+    """C[M,N] = A[M,K] . B[K,N] (fp16 in, fp32 out, row-major)."""
+    L = load()
+    _check(L.b2g_gemm_f16_f32(_ptr(A), _ptr(B), _ptr(C), M, N, K,
+                              K if lda is None else lda, N if ldb is None else ldb,
+                              N if ldc is None else ldc, _stream(stream)))
+
+
+def GEMM(A, B, C, M, N, K):
+    """The reference's drop-in form (contiguous, default stream)."""
+    _check(load().b2g_gemm(_ptr(A), _ptr(B), _ptr(C), M, N, K))
+
+
+def _arr(vals, n):
+    vals = [int(v) for v in vals]
+    assert len(vals) == n
+    return (ctypes.c_int64 * n)(*vals)
+
+
+def contract5d(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, stream=None):
+    """C[a,b,i,n] = sum_{j,k} A[a,b,i,j,k] B[j,k,n]; shapes/strides in elements."""
+    L = load()
+    _check(L.b2g_contract5d_f16_f32(_ptr(A), _arr(a_shape, 5), _arr(a_stride, 5), _ptr(B),
+                                    _arr(b_shape, 3), _arr(b_stride, 3), _ptr(C), _arr(c_shape, 4),
+                                    _arr(c_stride, 4), _stream(stream)))
+
+
+def fill_uniform(dst, n, seed, offset=0, stream=None):
+    _check(load().b2g_fill_uniform_f16(_ptr(dst), n, seed, offset, _stream(stream)))
+
+
+def last_path():
+    return load().b2g_last_path()
+
+
+def device_status(clear=True):
+    return load().b2g_device_status(1 if clear else 0)
+
+
+def set_option(key, value):
+    rc = load().b2g_set_option(key.encode(), int(value))
+    if rc != OK:
+        raise B2GError(rc, "bad option %s=%r" % (key, value))
+
+
+def get_option(key):
+    return load().b2g_get_option(key.encode())
+
+
+def tile_coord(t, num_m, num_n, group):
+    tm, tn = ctypes.c_int(), ctypes.c_int()
+    load().b2g_tile_coord(t, num_m, num_n, group, ctypes.byref(tm), ctypes.byref(tn))
+    return tm.value, tn.value
+
+
+def version():
+    return load().b2g_version().decode()

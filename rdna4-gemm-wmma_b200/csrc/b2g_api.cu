@@ -1,0 +1,578 @@
+// Host side of libb2g_gemm.so: the C ABI declared in include/b2g_gemm.h.
+//
+// Per call: validate shapes/strides, coalesce contraction modes whose strides allow it,
+// classify the layout (K-major A; N- or K-contiguous B; N- or M-contiguous C), encode the
+// TMA tensor maps directly on the caller's strides, pick one CTA or a CTA pair per tile,
+// and launch the persistent tcgen05 kernel (gemm_sm100.cuh) on the caller's stream.
+// Layouts outside TMA's addressing rules run on gemm_generic_kernel below, which computes
+// exactly GEMM_Naive's arithmetic (mmm.cpp:52-62).  There is no host/CPU compute path.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/b2g_gemm.h"
+#include "gemm_sm100.cuh"
+
+namespace b2g {
+
+// ------------------------------------------------------------------ errors / options
+static thread_local std::string t_err;
+static thread_local int t_path = B2G_PATH_NONE;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+static int cuda_fail(cudaError_t e, const char* what) {
+  return fail(B2G_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+static std::atomic<int64_t> opt_cta_group{0};
+static std::atomic<int64_t> opt_raster_group{0};
+static std::atomic<int64_t> opt_timeout_ns{2000000000LL};
+static std::atomic<int64_t> opt_force_generic{0};
+static std::atomic<int64_t> opt_fault_flags{0};
+
+// ------------------------------------------------------------------ driver entry point
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// ------------------------------------------------------------------ per-device state
+struct DevState {
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  bool attr_set[2][2][2] = {};  // [cg-1][b_kmajor][c_mcontig]
+  int max_clusters[2][2] = {};  // CG=2 only: [b_kmajor][c_mcontig]
+};
+static std::mutex g_dev_mu;
+static DevState g_dev[64];
+
+static int device_state(int dev, DevState** out) {
+  if (dev < 0 || dev >= 64) return fail(B2G_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DevState& d = g_dev[dev];
+  if (d.sm_count == 0) {
+    cudaError_t e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev);
+  }
+  *out = &d;
+  return B2G_OK;
+}
+
+// ------------------------------------------------------------------ generic kernel
+// Any shape, any strides: one thread per C element, fp32 accumulator, K visited in
+// ascending flattened (j, k) order -- GEMM_Naive's arithmetic (mmm.cpp:52-62).  With K == 0
+// it writes zeros.  Used when TMA cannot address the operands.
+struct Geo {
+  int64_t as[5], ast[5];  // a,b,i,j,k
+  int64_t bst[3];         // j,k,n strides
+  int64_t n;              // N
+  int64_t cst[4];         // a,b,i,n strides
+};
+
+__global__ void gemm_generic_kernel(const __half* __restrict__ A, const __half* __restrict__ B,
+                                    float* __restrict__ C, const Geo g) {
+  const int64_t rows = g.as[0] * g.as[1] * g.as[2];
+  const int64_t total = rows * g.n;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = idx / g.n, col = idx - row * g.n;
+    const int64_t ii = row % g.as[2];
+    const int64_t ib = (row / g.as[2]) % g.as[1];
+    const int64_t ia = row / (g.as[2] * g.as[1]);
+    const __half* ar = A + ia * g.ast[0] + ib * g.ast[1] + ii * g.ast[2];
+    const __half* bc = B + col * g.bst[2];
+    float acc = 0.0f;
+    for (int64_t j = 0; j < g.as[3]; ++j)
+      for (int64_t k = 0; k < g.as[4]; ++k)
+        acc += __half2float(ar[j * g.ast[3] + k * g.ast[4]]) *
+               __half2float(bc[j * g.bst[0] + k * g.bst[1]]);
+    C[ia * g.cst[0] + ib * g.cst[1] + ii * g.cst[2] + col * g.cst[3]] = acc;
+  }
+}
+
+// ------------------------------------------------------------------ RNG kernel
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void fill_uniform_kernel(__half* __restrict__ dst, int64_t n, uint64_t seed,
+                                    uint64_t offset) {
+  const uint64_t key = mix64(seed);
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const uint64_t h = mix64(key + offset + (uint64_t)e);
+    const int32_t r = (int32_t)(h >> 40) - 8388608;
+    dst[e] = __float2half_rn((float)r * (1.0f / 8388608.0f));
+  }
+}
+
+// ------------------------------------------------------------------ planning
+struct Mode {
+  int64_t size, sa, sc;  // extent, stride in the first operand, stride in the second
+};
+
+// Merge adjacent modes (outer first) whose strides in both operands are "outer = inner *
+// size_inner"; drop size-1 modes.  Returns the number of modes kept, innermost last.
+static int coalesce(Mode* m, int n) {
+  Mode out[5];
+  int k = 0;
+  for (int t = 0; t < n; ++t)
+    if (m[t].size != 1) out[k++] = m[t];
+  bool merged = true;
+  while (merged) {
+    merged = false;
+    for (int t = k - 1; t > 0; --t) {
+      const Mode& ot = out[t - 1];
+      Mode& in = out[t];
+      if (ot.sa == in.sa * in.size && ot.sc == in.sc * in.size) {
+        in.size *= ot.size;  // the merged mode keeps the inner strides
+        for (int u = t - 1; u < k - 1; ++u) out[u] = out[u + 1];
+        --k;
+        merged = true;
+        break;
+      }
+    }
+  }
+  for (int t = 0; t < k; ++t) m[t] = out[t];
+  return k;
+}
+
+static inline bool al16(int64_t bytes) { return (bytes & 15) == 0; }
+
+// ------------------------------------------------------------------ core dispatch
+static int run(const void* A, const int64_t as[5], const int64_t ast[5], const void* B,
+               const int64_t bs[3], const int64_t bst[3], float* Cp, const int64_t cs[4],
+               const int64_t cst[4], cudaStream_t stream) {
+  // ---- validation
+  for (int t = 0; t < 5; ++t)
+    if (as[t] < 0) return fail(B2G_ERR_INVALID_ARG, "negative A extent");
+  for (int t = 0; t < 3; ++t)
+    if (bs[t] < 0) return fail(B2G_ERR_INVALID_ARG, "negative B extent");
+  if (bs[0] != as[3] || bs[1] != as[4])
+    return fail(B2G_ERR_INVALID_ARG, "contracted modes differ: A (j,k)=(%lld,%lld) B=(%lld,%lld)",
+                (long long)as[3], (long long)as[4], (long long)bs[0], (long long)bs[1]);
+  if (cs[0] != as[0] || cs[1] != as[1] || cs[2] != as[2] || cs[3] != bs[2])
+    return fail(B2G_ERR_INVALID_ARG, "C shape does not match A/B free modes");
+  const int64_t M = as[0] * as[1] * as[2], N = bs[2], K = as[3] * as[4];
+  if (M == 0 || N == 0) {
+    t_path = B2G_PATH_EMPTY;
+    return B2G_OK;
+  }
+  if (!Cp) return fail(B2G_ERR_INVALID_ARG, "C is null");
+  if (K > 0 && (!A || !B)) return fail(B2G_ERR_INVALID_ARG, "A or B is null");
+
+  int dev = 0;
+  cudaError_t ce = cudaGetDevice(&dev);
+  if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
+  DevState* ds = nullptr;
+  int rc = device_state(dev, &ds);
+  if (rc) return rc;
+
+  auto launch_generic = [&](int path) -> int {
+    Geo g;
+    for (int t = 0; t < 5; ++t) {
+      g.as[t] = as[t];
+      g.ast[t] = ast[t];
+    }
+    for (int t = 0; t < 3; ++t) g.bst[t] = bst[t];
+    for (int t = 0; t < 4; ++t) g.cst[t] = cst[t];
+    g.n = N;
+    const int64_t total = M * N;
+    const int threads = 256;
+    int64_t blocks = (total + threads - 1) / threads;
+    blocks = std::min<int64_t>(blocks, (int64_t)ds->sm_count * 32);
+    gemm_generic_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
+        static_cast<const __half*>(A), static_cast<const __half*>(B), Cp, g);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "generic kernel launch");
+    t_path = path;
+    return B2G_OK;
+  };
+
+  if (K == 0) return launch_generic(B2G_PATH_ZERO);
+  if (opt_force_generic.load()) return launch_generic(B2G_PATH_GENERIC);
+  if (ds->cc_major != 10) return launch_generic(B2G_PATH_GENERIC);
+
+  // ---- coalesce modes
+  Mode mm[3] = {{as[0], ast[0], cst[0]}, {as[1], ast[1], cst[1]}, {as[2], ast[2], cst[2]}};
+  int nm = coalesce(mm, 3);
+  Mode km[2] = {{as[3], ast[3], bst[0]}, {as[4], ast[4], bst[1]}};
+  int nk = coalesce(km, 2);
+  // pad to fixed arity: M -> (a, b, i), K -> (j, k); padded modes have size 1
+  Mode M3[3], K2[2];
+  for (int t = 0; t < 3; ++t) M3[t] = {1, 0, 0};
+  for (int t = 0; t < 2; ++t) K2[t] = {1, 0, 0};
+  if (nm > 3 || nk > 2) return launch_generic(B2G_PATH_GENERIC);
+  for (int t = 0; t < nm; ++t) M3[3 - nm + t] = mm[t];
+  for (int t = 0; t < nk; ++t) K2[2 - nk + t] = km[t];
+  if (nm == 0) M3[2] = {1, 1, 1};
+  if (nk == 0) K2[1] = {1, 1, 1};
+  const int64_t b_sn = bst[2], c_sn = cst[3];
+
+  // ---- layout classes
+  const bool a_ok = K2[1].sa == 1;                  // K-major A
+  const bool b_mn = (b_sn == 1) || N == 1;          // N contiguous
+  const bool b_k = !b_mn && K2[1].sc == 1;          // K contiguous
+  const bool c_n = (c_sn == 1) || N == 1;           // N contiguous
+  const bool c_m = !c_n && M3[2].sc == 1;           // innermost M mode contiguous
+  if (!a_ok || !(b_mn || b_k) || !(c_n || c_m)) return launch_generic(B2G_PATH_GENERIC);
+
+  // ---- M decomposition: 128-row load box over (i, b, a)
+  const int64_t isz = M3[2].size, bsz = M3[1].size, asz = M3[0].size;
+  const int64_t jsz = K2[0].size, ksz = K2[1].size;
+  if (isz > INT32_MAX / 2 || bsz > INT32_MAX / 2 || asz > INT32_MAX / 2 || N > INT32_MAX / 2 ||
+      jsz > INT32_MAX / 2 || ksz > INT32_MAX / 2)
+    return launch_generic(B2G_PATH_GENERIC);
+  int bi, bb, ba;
+  if (isz >= 128 || (128 % isz) != 0 || bsz * asz == 1) {
+    bi = 128; bb = 1; ba = 1;
+  } else {
+    bi = (int)isz;
+    const int rem = 128 / bi;
+    if (bsz >= rem || (rem % bsz) != 0) {
+      bb = rem; ba = 1;
+    } else {
+      bb = (int)bsz; ba = rem / bb;
+    }
+  }
+  const int si = std::min(bi, 32);
+  const int sb = std::min(bb, 32 / si);
+  const int sa = 32 / (si * sb);
+  if (c_m && si < 4) return launch_generic(B2G_PATH_GENERIC);  // TMA inner box >= 16 bytes
+
+  // ---- TMA legality: 16-byte aligned bases and strides (size-1 modes do not matter)
+  auto stride_ok = [](const Mode& m, bool first, int esz) {
+    return m.size == 1 || al16((first ? m.sa : m.sc) * esz);
+  };
+  bool tma_ok = al16((int64_t)(uintptr_t)A) && al16((int64_t)(uintptr_t)B) &&
+                al16((int64_t)(uintptr_t)Cp);
+  // every M mode is an outer dimension of A; of C too, except the innermost one when C is
+  // M-contiguous (it is then the map's unit-stride dimension 0)
+  for (int t = 0; t < 3; ++t)
+    tma_ok = tma_ok && stride_ok(M3[t], true, 2) && ((c_m && t == 2) || stride_ok(M3[t], false, 4));
+  tma_ok = tma_ok && stride_ok(K2[0], true, 2) && stride_ok(K2[0], false, 2);
+  if (b_mn) tma_ok = tma_ok && stride_ok(K2[1], false, 2);
+  if (b_k) tma_ok = tma_ok && (N == 1 || al16(b_sn * 2));
+  if (c_m) tma_ok = tma_ok && (N == 1 || al16(c_sn * 4));
+  if (!tma_ok) return launch_generic(B2G_PATH_GENERIC);
+
+  auto encode = get_encode();
+  if (!encode) return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+
+  // filler stride for size-1 modes: anything 16-byte aligned works (coordinate is always 0)
+  auto fill = [](int64_t s, int64_t size, int64_t prev_extent_bytes) -> cuuint64_t {
+    if (size == 1) return (cuuint64_t)((std::max<int64_t>(prev_extent_bytes, 16) + 15) & ~15LL);
+    return (cuuint64_t)s;
+  };
+
+  CUtensorMap tmA, tmB, tmC;
+  // A: dims (k, j, i, b, a)
+  {
+    cuuint64_t dims[5] = {(cuuint64_t)ksz, (cuuint64_t)jsz, (cuuint64_t)isz, (cuuint64_t)bsz,
+                          (cuuint64_t)asz};
+    cuuint64_t st[4];
+    st[0] = fill(K2[0].sa * 2, jsz, ksz * 2);
+    st[1] = fill(M3[2].sa * 2, isz, (int64_t)st[0] * jsz);
+    st[2] = fill(M3[1].sa * 2, bsz, (int64_t)st[1] * isz);
+    st[3] = fill(M3[0].sa * 2, asz, (int64_t)st[2] * bsz);
+    cuuint32_t box[5] = {64, 1, (cuuint32_t)bi, (cuuint32_t)bb, (cuuint32_t)ba};
+    cuuint32_t es[5] = {1, 1, 1, 1, 1};
+    CUresult r = encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(A), dims, st, box,
+                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map A not encodable
+  }
+  // choose CTA grouping
+  const int num_m_tiles_i = (int)((isz + bi - 1) / bi);
+  const int num_m_tiles_b = (int)((bsz + bb - 1) / bb);
+  const int num_m_tiles_a = (int)((asz + ba - 1) / ba);
+  const int64_t nmt64 = (int64_t)num_m_tiles_i * num_m_tiles_b * num_m_tiles_a;
+  const int64_t nnt64 = (N + kBN - 1) / kBN;
+  if (nmt64 * nnt64 > INT32_MAX / 4) return launch_generic(B2G_PATH_GENERIC);
+  int cg = (int)opt_cta_group.load();
+  if (cg != 1 && cg != 2) cg = (nmt64 >= 2) ? 2 : 1;
+  const int bn_cta = kBN / cg;
+  // B
+  if (b_mn) {  // dims (n, k, j)
+    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)ksz, (cuuint64_t)jsz};
+    cuuint64_t st[2];
+    st[0] = fill(K2[1].sc * 2, ksz, N * 2);
+    st[1] = fill(K2[0].sc * 2, jsz, (int64_t)st[0] * ksz);
+    cuuint32_t box[3] = {64, 64, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B), dims, st, box,
+                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map B (N-major) not encodable
+  } else {  // dims (k, j, n)
+    cuuint64_t dims[3] = {(cuuint64_t)ksz, (cuuint64_t)jsz, (cuuint64_t)N};
+    cuuint64_t st[2];
+    st[0] = fill(K2[0].sc * 2, jsz, ksz * 2);
+    st[1] = fill(b_sn * 2, N, (int64_t)st[0] * jsz);
+    cuuint32_t box[3] = {64, 1, (cuuint32_t)bn_cta};
+    cuuint32_t es[3] = {1, 1, 1};
+    CUresult r = encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B), dims, st, box,
+                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map B (K-major) not encodable
+  }
+  // C
+  if (c_n) {  // dims (n, i, b, a), 128-byte swizzled 32x32 boxes
+    cuuint64_t dims[4] = {(cuuint64_t)N, (cuuint64_t)isz, (cuuint64_t)bsz, (cuuint64_t)asz};
+    cuuint64_t st[3];
+    st[0] = fill(M3[2].sc * 4, isz, N * 4);
+    st[1] = fill(M3[1].sc * 4, bsz, (int64_t)st[0] * isz);
+    st[2] = fill(M3[0].sc * 4, asz, (int64_t)st[1] * bsz);
+    cuuint32_t box[4] = {32, (cuuint32_t)si, (cuuint32_t)sb, (cuuint32_t)sa};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = encode(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, dims, st, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map C (N-major) not encodable
+  } else {  // dims (i, n, b, a), unswizzled si x 32 boxes
+    cuuint64_t dims[4] = {(cuuint64_t)isz, (cuuint64_t)N, (cuuint64_t)bsz, (cuuint64_t)asz};
+    cuuint64_t st[3];
+    st[0] = fill(c_sn * 4, N, isz * 4);
+    st[1] = fill(M3[1].sc * 4, bsz, (int64_t)st[0] * N);
+    st[2] = fill(M3[0].sc * 4, asz, (int64_t)st[1] * bsz);
+    cuuint32_t box[4] = {(cuuint32_t)si, 32, (cuuint32_t)sb, (cuuint32_t)sa};
+    cuuint32_t es[4] = {1, 1, 1, 1};
+    CUresult r = encode(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, dims, st, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map C (M-major) not encodable
+  }
+
+  GemmParams p{};
+  p.i_size = (int)isz;
+  p.b_size = (int)bsz;
+  p.a_size = (int)asz;
+  p.bi = bi; p.bb = bb; p.ba = ba;
+  p.ti = num_m_tiles_i;
+  p.tb = num_m_tiles_b;
+  p.si = si; p.sb = sb; p.sa = sa;
+  p.num_m_tiles = (int)nmt64;
+  p.num_pm_tiles = (int)((nmt64 + cg - 1) / cg);
+  p.n_size = (int)N;
+  p.num_n_tiles = (int)nnt64;
+  p.k_blocks_per_j = (int)((ksz + kBK - 1) / kBK);
+  p.k_iters = (int)(jsz * p.k_blocks_per_j);
+  p.num_tiles = p.num_pm_tiles * p.num_n_tiles;
+  int rg = (int)opt_raster_group.load();
+  p.raster_group = rg > 0 ? rg : (cg == 2 ? 8 : 16);
+  p.timeout_ns = (unsigned long long)opt_timeout_ns.load();
+  p.fault_flags = (int)opt_fault_flags.load();
+
+  // ---- launch
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams) = nullptr;
+  const int bk = b_k ? 1 : 0, cm = c_m ? 1 : 0;
+  if (cg == 1) {
+    kern = bk ? (cm ? gemm_tc_kernel<1, true, true> : gemm_tc_kernel<1, true, false>)
+              : (cm ? gemm_tc_kernel<1, false, true> : gemm_tc_kernel<1, false, false>);
+  } else {
+    kern = bk ? (cm ? gemm_tc_kernel<2, true, true> : gemm_tc_kernel<2, true, false>)
+              : (cm ? gemm_tc_kernel<2, false, true> : gemm_tc_kernel<2, false, false>);
+  }
+  const uint32_t smem = cg == 1 ? Cfg<1>::SMEM_BYTES : Cfg<2>::SMEM_BYTES;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (!ds->attr_set[cg - 1][bk][cm]) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
+      if (cg == 2) {
+        cudaLaunchConfig_t qc = {};
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = 2;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        qc.gridDim = dim3(2 * (ds->sm_count / 2), 1, 1);
+        qc.blockDim = dim3(kThreads, 1, 1);
+        qc.dynamicSmemBytes = smem;
+        qc.attrs = qa;
+        qc.numAttrs = 1;
+        int nclu = 0;
+        e = cudaOccupancyMaxActiveClusters(&nclu, (void*)kern, &qc);
+        if (e != cudaSuccess || nclu <= 0) nclu = ds->sm_count / 2;
+        ds->max_clusters[bk][cm] = nclu;
+      }
+      ds->attr_set[cg - 1][bk][cm] = true;
+    }
+  }
+  int groups;
+  if (cg == 1)
+    groups = std::min(ds->sm_count, p.num_tiles);
+  else
+    groups = std::min(ds->max_clusters[bk][cm], p.num_tiles);
+  if (groups < 1) groups = 1;
+
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3((unsigned)(groups * cg), 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  if (cg == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
+  if (e != cudaSuccess) return cuda_fail(e, "tcgen05 kernel launch");
+  t_path = cg == 1 ? B2G_PATH_TC_1CTA : B2G_PATH_TC_2CTA;
+  return B2G_OK;
+}
+
+}  // namespace b2g
+
+// ==================================================================== C ABI
+using namespace b2g;
+
+extern "C" int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t M, int64_t N,
+                                int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  t_err.clear();
+  if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
+  if (lda < std::max<int64_t>(K, 1) || ldb < std::max<int64_t>(N, 1) || ldc < std::max<int64_t>(N, 1))
+    return fail(B2G_ERR_INVALID_ARG, "leading dimension smaller than the row length");
+  const int64_t as[5] = {1, 1, M, 1, K}, ast[5] = {0, 0, lda, 0, 1};
+  const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
+  const int64_t cs[4] = {1, 1, M, N}, cst[4] = {0, 0, ldc, 1};
+  return run(A, as, ast, B, bs, bst, C, cs, cst, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2g_gemm(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K) {
+  return b2g_gemm_f16_f32(A, B, C, M, N, K, std::max<int64_t>(K, 1), std::max<int64_t>(N, 1),
+                          std::max<int64_t>(N, 1), nullptr);
+}
+
+extern "C" int b2g_contract5d_f16_f32(const void* A, const int64_t a_shape[5],
+                                      const int64_t a_stride[5], const void* B,
+                                      const int64_t b_shape[3], const int64_t b_stride[3], float* C,
+                                      const int64_t c_shape[4], const int64_t c_stride[4],
+                                      void* stream) {
+  t_err.clear();
+  if (!a_shape || !a_stride || !b_shape || !b_stride || !c_shape || !c_stride)
+    return fail(B2G_ERR_INVALID_ARG, "null shape/stride array");
+  return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride,
+             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2g_fill_uniform_f16(void* dst, int64_t n, uint64_t seed, uint64_t offset,
+                                    void* stream) {
+  t_err.clear();
+  if (n < 0) return fail(B2G_ERR_INVALID_ARG, "negative length");
+  if (n == 0) return B2G_OK;
+  if (!dst) return fail(B2G_ERR_INVALID_ARG, "dst is null");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DevState* ds = nullptr;
+  int rc = device_state(dev, &ds);
+  if (rc) return rc;
+  const int threads = 256;
+  int64_t blocks = std::min<int64_t>((n + threads - 1) / threads, (int64_t)ds->sm_count * 16);
+  fill_uniform_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__half*>(dst), n, seed, offset);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "fill kernel launch");
+  return B2G_OK;
+}
+
+extern "C" const char* b2g_last_error_string(void) { return t_err.c_str(); }
+
+extern "C" int b2g_last_path(void) { return t_path; }
+
+extern "C" int b2g_device_status(int clear) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    fail(B2G_ERR_CUDA, "cudaDeviceSynchronize: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (e != cudaSuccess) {
+    fail(B2G_ERR_CUDA, "read device error word: %s", cudaGetErrorString(e));
+    return -1;
+  }
+  if (clear) {
+    const int z = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &z, sizeof(int));
+    if (e != cudaSuccess) {
+      fail(B2G_ERR_CUDA, "clear device error word: %s", cudaGetErrorString(e));
+      return -1;
+    }
+  }
+  return v;
+}
+
+extern "C" int b2g_set_option(const char* key, int64_t value) {
+  if (!key) return B2G_ERR_INVALID_ARG;
+  if (!strcmp(key, "cta_group")) {
+    if (value < 0 || value > 2) return B2G_ERR_INVALID_ARG;
+    opt_cta_group = value;
+  } else if (!strcmp(key, "raster_group")) {
+    if (value < 0) return B2G_ERR_INVALID_ARG;
+    opt_raster_group = value;
+  } else if (!strcmp(key, "timeout_ns")) {
+    if (value <= 0) return B2G_ERR_INVALID_ARG;
+    opt_timeout_ns = value;
+  } else if (!strcmp(key, "force_generic")) {
+    opt_force_generic = value ? 1 : 0;
+  } else if (!strcmp(key, "fault_flags")) {
+    opt_fault_flags = value;
+  } else {
+    return B2G_ERR_INVALID_ARG;
+  }
+  return B2G_OK;
+}
+
+extern "C" int64_t b2g_get_option(const char* key) {
+  if (!key) return -1;
+  if (!strcmp(key, "cta_group")) return opt_cta_group;
+  if (!strcmp(key, "raster_group")) return opt_raster_group;
+  if (!strcmp(key, "timeout_ns")) return opt_timeout_ns;
+  if (!strcmp(key, "force_generic")) return opt_force_generic;
+  if (!strcmp(key, "fault_flags")) return opt_fault_flags;
+  return -1;
+}
+
+extern "C" void b2g_tile_coord(int t, int num_m, int num_n, int group, int* tm, int* tn) {
+  b2g_sched_tile(t, num_m, num_n, group, tm, tn);
+}
+
+extern "C" const char* b2g_version(void) { return "b2g_gemm 0.1 (sm_100a tcgen05)"; }

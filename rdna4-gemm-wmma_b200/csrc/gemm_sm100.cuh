@@ -1,0 +1,348 @@
+// sm_100a GEMM / contraction kernel: C (fp32) = A (fp16) x B (fp16), fp32 accumulation in
+// tensor memory.
+//
+// Replaces the reference's WMMA_Swizzled_Full (mmm.cpp:1214-1374) and its tensor variant
+// (mmmTensor.cpp:44-257).  Same result definition (GEMM_Naive, mmm.cpp:52-62: every C element
+// is the fp32-accumulated dot product of an A row and a B column, C overwritten), different
+// machine: the gfx12 WMMA ladder, LDS XOR swizzles and register-blocking templates give way to
+//   * TMA tensor-map loads into 128-byte-swizzled shared memory (the tensor maps carry the
+//     operand strides, so the 5-D contraction is read in place, with no packing pass),
+//   * a STAGES-deep mbarrier ring between one TMA producer thread and one MMA thread,
+//   * tcgen05.mma (kind::f16) with the fp32 accumulator in TMEM, double-buffered so the
+//     epilogue of tile t overlaps the main loop of tile t+1,
+//   * CG = 2: a CTA pair (cluster of 2) shares one 256x256 tile: each CTA loads its own 128
+//     A rows and half of the B columns, the even CTA issues cta_group::2 MMAs over both
+//     halves.  No TMA load uses cluster multicast.
+//   * an epilogue of 4 warps: TMEM -> registers -> swizzled shared memory -> TMA store,
+//     which also clips ragged M/N edges (TMA zero-fill covers ragged K on the load side),
+//   * a persistent grid walking the tiles in grouped order (sched.h).
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer,
+// warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31).
+#pragma once
+#include <cuda.h>
+#include <cstdint>
+
+#include "ptx.cuh"
+#include "sched.h"
+
+namespace b2g {
+
+// Device-side error word: 0 = fine, otherwise the code of the first bounded wait that gave up.
+// Read and cleared by b2g_device_status().
+__device__ int g_device_error;
+
+enum : int {
+  ERR_WAIT_EMPTY = 1,   // producer waiting for a free pipeline stage
+  ERR_WAIT_FULL = 2,    // MMA waiting for operands
+  ERR_WAIT_TEMPTY = 3,  // MMA waiting for the epilogue to release an accumulator
+  ERR_WAIT_TFULL = 4,   // epilogue waiting for an accumulator
+  ERR_WAIT_DRAIN = 5,   // teardown waiting for copies / MMAs in flight
+};
+
+// Problem description computed on the host (b2g_api.cu) and passed by value.
+//
+// Rows of C are the flattened M-modes (a, b, i), i innermost; the K axis is the flattened
+// (j, k), k innermost.  A 128-row CTA tile is one TMA box of bi x bb x ba rows over (i, b, a),
+// bi*bb*ba == 128; each epilogue warp stores a 32-row sub-box si x sb x sa.
+struct GemmParams {
+  int i_size, b_size, a_size;  // M-mode extents
+  int bi, bb, ba;              // load box per M-mode
+  int ti, tb;                  // tiles along i and b (tiles along a = num_m_tiles/(ti*tb))
+  int si, sb, sa;              // per-warp store sub-box
+  int num_m_tiles;             // 128-row tiles
+  int num_pm_tiles;            // tiles of 128*CG rows (one per CTA group)
+  int n_size;                  // N extent
+  int num_n_tiles;             // 256-column tiles
+  int k_blocks_per_j;          // ceil(k / 64)
+  int k_iters;                 // j * k_blocks_per_j
+  int num_tiles;               // num_pm_tiles * num_n_tiles
+  int raster_group;            // strip height of the tile order, in CTA-group tiles
+  unsigned long long timeout_ns;
+  int fault_flags;             // test-only: bit 0 = producer issues no loads (forces a timeout)
+};
+
+constexpr int kBM = 128;  // rows per CTA (UMMA M per CTA)
+constexpr int kBN = 256;  // columns per CTA group (UMMA N)
+constexpr int kBK = 64;   // K per stage: one 128-byte swizzle row of fp16
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;  // two 256-column fp32 accumulators
+constexpr uint32_t kCBuf = 32 * 32 * 4;  // one 32x32 fp32 staging buffer
+
+template <int CG>
+struct Cfg {
+  static constexpr int BN_CTA = kBN / CG;                          // B columns loaded per CTA
+  static constexpr uint32_t A_BYTES = kBM * kBK * 2;               // 16 KiB
+  static constexpr uint32_t B_BYTES = BN_CTA * kBK * 2;            // 32 or 16 KiB
+  static constexpr int STAGES = CG == 1 ? 4 : 6;
+  static constexpr uint32_t OFF_B = STAGES * A_BYTES;
+  static constexpr uint32_t OFF_C = OFF_B + STAGES * B_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_C + kEpiWarps * 2 * kCBuf;
+  static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
+  static constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
+  static constexpr uint32_t TX_BYTES = CG * (A_BYTES + B_BYTES);  // bytes per stage per group
+};
+
+static_assert(Cfg<1>::SMEM_BYTES <= 232448, "shared memory budget (CG=1)");
+static_assert(Cfg<2>::SMEM_BYTES <= 232448, "shared memory budget (CG=2)");
+
+// Instruction descriptor, kind::f16: D fp32 (bit 4), A/B fp16 (format 0), A K-major,
+// B major per template, N>>3 at bit 17, M>>4 at bit 24.
+__host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool b_mn_major) {
+  return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void m_tile_origin(const GemmParams& p, int mt, int& i0, int& b0,
+                                              int& a0) {
+  const int ii = mt % p.ti;
+  const int r = mt / p.ti;
+  const int ib = r % p.tb;
+  const int ia = r / p.tb;
+  i0 = ii * p.bi;
+  b0 = ib * p.bb;
+  a0 = ia * p.ba;
+}
+
+template <int CG, bool B_KMAJOR, bool C_MCONTIG>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+  using C = Cfg<CG>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint32_t base = ptx::smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
+  base += pad;
+  uint8_t* smem = smem_raw + pad;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta_rank = (CG == 2) ? ptx::cluster_ctarank() : 0u;
+  const bool leader = (cta_rank == 0);
+
+  auto full_bar = [&](int s) { return base + C::OFF_BAR + 8u * s; };
+  auto empty_bar = [&](int s) { return base + C::OFF_BAR + 8u * (C::STAGES + s); };
+  auto tfull_bar = [&](int a) { return base + C::OFF_BAR + 8u * (2 * C::STAGES + a); };
+  auto tempty_bar = [&](int a) { return base + C::OFF_BAR + 8u * (2 * C::STAGES + 2 + a); };
+  const uint32_t mma_done_bar = base + C::OFF_BAR + 8u * (2 * C::STAGES + 4);
+  const uint32_t tmem_slot = base + C::OFF_MISC;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  int* err = &g_device_error;
+  const unsigned long long lim = p.timeout_ns;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      ptx::mbar_init(full_bar(s), 1);
+      ptx::mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(tfull_bar(a), 1);
+      ptx::mbar_init(tempty_bar(a), kEpiWarps * CG);
+    }
+    ptx::mbar_init(mma_done_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::tma_prefetch_desc(&tmA);
+    ptx::tma_prefetch_desc(&tmB);
+    ptx::tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc<CG>(tmem_slot, kTmemCols);
+    ptx::tmem_relinquish<CG>();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if constexpr (CG == 2) ptx::cluster_sync();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(smem + C::OFF_MISC);
+
+  const int group_id = blockIdx.x / CG;
+  const int num_groups = gridDim.x / CG;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int t = group_id; t < p.num_tiles && ok; t += num_groups) {
+        int pm, tn;
+        b2g_sched_tile(t, p.num_pm_tiles, p.num_n_tiles, p.raster_group, &pm, &tn);
+        const int mt = pm * CG + (int)cta_rank;
+        int i0, b0, a0;
+        m_tile_origin(p, mt, i0, b0, a0);
+        const int nb = tn * kBN + (int)cta_rank * C::BN_CTA;
+        for (int kb = 0; kb < p.k_iters; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+          if (!ptx::mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, err, ERR_WAIT_EMPTY, lim)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = (CG == 1) ? full_bar(s) : ptx::mapa(full_bar(s), 0);
+          if (leader) ptx::mbar_arrive_expect_tx(full_bar(s), C::TX_BYTES);
+          if (p.fault_flags & 1) continue;
+          const int jj = kb / p.k_blocks_per_j;
+          const int kc = (kb - jj * p.k_blocks_per_j) * kBK;
+          const uint32_t sa = base + s * C::A_BYTES;
+          const uint32_t sb = base + C::OFF_B + s * C::B_BYTES;
+          ptx::tma_load_5d<CG>(sa, &tmA, fb, kc, jj, i0, b0, a0);
+          if constexpr (B_KMAJOR) {
+            ptx::tma_load_3d<CG>(sb, &tmB, fb, kc, jj, nb);
+          } else {
+#pragma unroll
+            for (int c = 0; c < C::BN_CTA / 64; ++c)
+              ptx::tma_load_3d<CG>(sb + c * 8192u, &tmB, fb, nb + 64 * c, kc, jj);
+          }
+        }
+      }
+      // Teardown: every load this thread issued must land before the CTA can exit.  With
+      // CG == 1 the last min(it, STAGES) loads each completed (or will complete) a phase of
+      // their stage's full barrier; wait for those phases.  (With CG == 2 in a normal exit the
+      // leader's MMA thread consumed every stage before the final cluster barrier.)
+      if (CG == 1 && !(p.fault_flags & 1)) {
+        const int pending = it < C::STAGES ? it : C::STAGES;
+        for (int q = 0; q < pending; ++q) {
+          const int i2 = it - 1 - q;
+          ptx::mbar_wait_drain(full_bar(i2 % C::STAGES), (uint32_t)(i2 / C::STAGES) & 1u, err,
+                               ERR_WAIT_DRAIN, lim);
+        }
+      }
+      if (!ok || *abort_flag) ptx::spin_ns(200000ull);  // abnormal exit: grace period for copies
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = make_idesc(kBM * CG, kBN, !B_KMAJOR);
+      int it = 0, tc = 0;
+      bool ok = true;
+      for (int t = group_id; t < p.num_tiles && ok; t += num_groups, ++tc) {
+        const int acc = tc & 1;
+        const uint32_t aph = (uint32_t)(tc >> 1) & 1u;
+        if (!ptx::mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag, err, ERR_WAIT_TEMPTY, lim)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)acc * kBN;
+        for (int kb = 0; kb < p.k_iters; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
+          if (!ptx::mbar_wait(full_bar(s), ph, abort_flag, err, ERR_WAIT_FULL, lim)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t sa = base + s * C::A_BYTES;
+          const uint32_t sb = base + C::OFF_B + s * C::B_BYTES;
+#pragma unroll
+          for (int k16 = 0; k16 < kBK / 16; ++k16) {
+            const uint64_t ad = ptx::smem_desc_sw128(sa + 32u * k16, 16u, 1024u);
+            const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(sb + 32u * k16, 16u, 1024u)
+                                         : ptx::smem_desc_sw128(sb + 2048u * k16, 8192u, 1024u);
+            ptx::umma_f16<CG>(d, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
+          }
+          ptx::umma_commit<CG>(empty_bar(s), (uint16_t)0x3);
+        }
+        if (!ok) break;
+        ptx::umma_commit<CG>(tfull_bar(acc), (uint16_t)0x3);
+      }
+      // Teardown: all MMAs issued by this thread must finish before TMEM/shared memory go away.
+      ptx::umma_commit<CG>(mma_done_bar, (uint16_t)0x1);
+      ptx::mbar_wait_drain(mma_done_bar, 0u, err, ERR_WAIT_DRAIN, lim);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;                  // TMEM lane quarter
+    const uint32_t cbuf = base + C::OFF_C + (uint32_t)(warp - 2) * 2u * kCBuf;
+    // This warp's 32-row sub-box inside the 128-row tile (flattened (a, b, i) order).
+    const int r0 = 32 * q;
+    const int a_l = r0 / (p.bi * p.bb);
+    const int b_l = (r0 / p.bi) % p.bb;
+    const int i_l = r0 % p.bi;
+    int tc = 0, nstore = 0;
+    for (int t = group_id; t < p.num_tiles; t += num_groups, ++tc) {
+      int pm, tn;
+      b2g_sched_tile(t, p.num_pm_tiles, p.num_n_tiles, p.raster_group, &pm, &tn);
+      const int mt = pm * CG + (int)cta_rank;
+      int i0, b0, a0;
+      m_tile_origin(p, mt, i0, b0, a0);
+      const int ci = i0 + i_l, cb = b0 + b_l, ca = a0 + a_l;
+      const bool rows_valid = mt < p.num_m_tiles && ci < p.i_size && cb < p.b_size && ca < p.a_size;
+      const int acc = tc & 1;
+      const uint32_t aph = (uint32_t)(tc >> 1) & 1u;
+      const bool got = ptx::mbar_wait(tfull_bar(acc), aph, abort_flag, err, ERR_WAIT_TFULL, lim);
+      if (!__all_sync(0xffffffffu, got)) break;
+      ptx::tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)acc * kBN;
+      const int n0 = tn * kBN;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(tbase + 32u * c, v);
+        ptx::tmem_ld_wait();
+        if (c == kBN / 32 - 1) {
+          // Accumulator fully read: hand it back to the MMA warp.
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 1)
+              ptx::mbar_arrive(tempty_bar(acc));
+            else
+              ptx::mbar_arrive_cluster(tempty_bar(acc), 0);
+          }
+        }
+        if (!rows_valid || n0 + 32 * c >= p.n_size) continue;
+        const uint32_t buf = cbuf + (uint32_t)(nstore & 1) * kCBuf;
+        if (lane == 0) ptx::bulk_wait_read<1>();
+        __syncwarp();
+        if constexpr (!C_MCONTIG) {
+          // Row `lane` as 8 16-byte chunks, 128-byte swizzle: chunk j -> j ^ (row % 8).
+          const uint32_t row = buf + (uint32_t)lane * 128u;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            ptx::st_shared_v4(row + (uint32_t)((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1],
+                              v[4 * j + 2], v[4 * j + 3]);
+        } else {
+          // Box order (i, n, b, a): element (row, col) at ((row / si) * 32 + col) * si + row % si.
+          const int blk = lane / p.si, il = lane - blk * p.si;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            ptx::st_shared_b32(buf + 4u * (uint32_t)((blk * 32 + j) * p.si + il), v[j]);
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (!C_MCONTIG)
+            ptx::tma_store_4d(&tmC, buf, n0 + 32 * c, ci, cb, ca);
+          else
+            ptx::tma_store_4d(&tmC, buf, ci, n0 + 32 * c, cb, ca);
+          ptx::bulk_commit();
+        }
+        ++nstore;
+      }
+    }
+    if (lane == 0) ptx::bulk_wait_all();
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------ teardown
+  __syncwarp();
+  ptx::tc_fence_before();
+  __syncthreads();
+  if constexpr (CG == 2) {
+    __syncwarp();
+    ptx::cluster_sync();
+  }
+  ptx::tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    ptx::tmem_dealloc<CG>(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace b2g

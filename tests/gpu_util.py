@@ -1,0 +1,40 @@
+"""Helpers shared by the GPU parity tests: seeded inputs (host oracle generator, copied to
+the device), the oracle comparison, and option scoping.  torch is used only to hold device
+memory; every product computation goes through the C ABI."""
+import contextlib
+
+import numpy as np
+
+
+def to_dev(torch, arr):
+    t = torch.from_numpy(np.ascontiguousarray(arr))
+    return t.cuda()
+
+
+def padded_f16(torch, orc, rows, cols, ld, seed, offset=0):
+    """rows x cols fp16 matrix (row pitch ld) holding the oracle sequence for the logical
+    rows x cols matrix; the pad columns hold a different sequence so a kernel that reads
+    them is caught."""
+    logical = orc.uniform_f16((rows, cols), seed, offset)
+    full = orc.uniform_f16((rows, ld), seed + 1000003, offset)
+    full[:, :cols] = logical
+    return logical, to_dev(torch, full)
+
+
+def assert_close(orc, got, ref, K, max_a=1.0, max_b=1.0, what=""):
+    bad, ma, mr, first = orc.check(got, ref, K, max_a, max_b)
+    assert bad == 0, "%s: %d elements out of tolerance (max abs %.3g, max rel %.3g, first %d: got %r ref %r)" % (
+        what, bad, ma, mr, first, np.asarray(got).ravel()[first], np.asarray(ref).ravel()[first])
+    return ma, mr
+
+
+@contextlib.contextmanager
+def options(b2g, **kw):
+    old = {k: b2g.get_option(k) for k in kw}
+    try:
+        for k, v in kw.items():
+            b2g.set_option(k, v)
+        yield
+    finally:
+        for k, v in old.items():
+            b2g.set_option(k, v)
