@@ -220,6 +220,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=12)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="device-resident GEMM steps only (no e2e, CPU baseline or clock "
+                         "sampling): the command profiled with ncu")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -265,11 +268,12 @@ def main():
           for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local)
+    sampler = ClockSampler(local) if not args.kernel_only else None
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    sampler.start()
+    if sampler:
+        sampler.start()
     t_start.record(stream)
     for i in range(args.steps):
         ev[i][0].record(stream)
@@ -277,7 +281,7 @@ def main():
         ev[i][1].record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
-    clocks = sampler.stop()
+    clocks = sampler.stop() if sampler else None
     if ws > 1:
         dist.barrier()
     elapsed_ms = t_start.elapsed_time(t_end)
@@ -295,13 +299,15 @@ def main():
     achieved = flops / (avg_launch_ms * 1e-3) / 1e12
 
     # ---- end to end through the C ABI with host buffers (pipelined over 3 streams)
-    e2e = e2e_run(torch, b2g, dev, M, N, K, rank, ws, args.e2e_steps, dist if ws > 1 else None)
+    e2e = None
+    if not args.kernel_only:
+        e2e = e2e_run(torch, b2g, dev, M, N, K, rank, ws, args.e2e_steps, dist if ws > 1 else None)
 
     peaks, peaks_src = measured_peaks()
     sustained = elapsed_ms > 1000.0
     peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
     cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not args.kernel_only:
         v, rows, secs, thr = cpu_baseline(args.cpu_seconds)
         cpu = {"value": v, "unit": "TFLOP/s", "cores": thr, "kind": "port",
                "sample": "%d of 8192 rows of the 8192^3 GEMM (%.1f s); blocked AVX2 port of "

@@ -47,6 +47,7 @@ static std::atomic<int64_t> opt_raster_group{0};
 static std::atomic<int64_t> opt_timeout_ns{2000000000LL};
 static std::atomic<int64_t> opt_force_generic{0};
 static std::atomic<int64_t> opt_fault_flags{0};
+static std::atomic<int64_t> opt_tile_n{0};  // 0 = choose by shape, else 256 or 512
 
 // ------------------------------------------------------------------ driver entry point
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -67,8 +68,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 struct DevState {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
-  bool attr_set[2][2][2] = {};  // [cg-1][b_kmajor][c_mcontig]
-  int max_clusters[2][2] = {};  // CG=2 only: [b_kmajor][c_mcontig]
+  bool attr_set[3][2][2] = {};  // [variant][b_kmajor][c_mcontig]
+  int max_clusters[3][2][2] = {};
 };
 static std::mutex g_dev_mu;
 static DevState g_dev[64];
@@ -319,11 +320,14 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   const int num_m_tiles_b = (int)((bsz + bb - 1) / bb);
   const int num_m_tiles_a = (int)((asz + ba - 1) / ba);
   const int64_t nmt64 = (int64_t)num_m_tiles_i * num_m_tiles_b * num_m_tiles_a;
-  const int64_t nnt64 = (N + kBN - 1) / kBN;
-  if (nmt64 * nnt64 > INT32_MAX / 4) return launch_generic(B2G_PATH_GENERIC);
   int cg = (int)opt_cta_group.load();
   if (cg != 1 && cg != 2) cg = (nmt64 >= 2) ? 2 : 1;
-  const int bn_cta = kBN / cg;
+  int bn = (int)opt_tile_n.load();
+  if (bn != 256 && bn != 512) bn = (cg == 2 && N >= 1024) ? 512 : 256;
+  if (cg == 1) bn = 256;  // one CTA: 256 columns (TMEM holds two accumulators)
+  const int64_t nnt64 = (N + bn - 1) / bn;
+  if (nmt64 * nnt64 > INT32_MAX / 4) return launch_generic(B2G_PATH_GENERIC);
+  const int bph = 256 / cg;  // B columns of one N-half held by one CTA
   // B
   if (b_mn) {  // dims (n, k, j)
     cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)ksz, (cuuint64_t)jsz};
@@ -341,7 +345,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     cuuint64_t st[2];
     st[0] = fill(K2[0].sc * 2, jsz, ksz * 2);
     st[1] = fill(b_sn * 2, N, (int64_t)st[0] * jsz);
-    cuuint32_t box[3] = {64, 1, (cuuint32_t)bn_cta};
+    cuuint32_t box[3] = {64, 1, (cuuint32_t)bph};
     cuuint32_t es[3] = {1, 1, 1};
     CUresult r = encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B), dims, st, box,
                         es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -391,24 +395,28 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.k_iters = (int)(jsz * p.k_blocks_per_j);
   p.num_tiles = p.num_pm_tiles * p.num_n_tiles;
   int rg = (int)opt_raster_group.load();
-  p.raster_group = rg > 0 ? rg : (cg == 2 ? 8 : 16);
+  p.raster_group = rg > 0 ? rg : (cg == 2 ? 8 : 16);  // measured best on 8192^3
   p.timeout_ns = (unsigned long long)opt_timeout_ns.load();
   p.fault_flags = (int)opt_fault_flags.load();
 
   // ---- launch
-  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams) = nullptr;
+  using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
   const int bk = b_k ? 1 : 0, cm = c_m ? 1 : 0;
-  if (cg == 1) {
-    kern = bk ? (cm ? gemm_tc_kernel<1, true, true> : gemm_tc_kernel<1, true, false>)
-              : (cm ? gemm_tc_kernel<1, false, true> : gemm_tc_kernel<1, false, false>);
-  } else {
-    kern = bk ? (cm ? gemm_tc_kernel<2, true, true> : gemm_tc_kernel<2, true, false>)
-              : (cm ? gemm_tc_kernel<2, false, true> : gemm_tc_kernel<2, false, false>);
-  }
-  const uint32_t smem = cg == 1 ? Cfg<1>::SMEM_BYTES : Cfg<2>::SMEM_BYTES;
+  const int variant = cg == 1 ? 0 : (bn == 256 ? 1 : 2);
+  static const KernFn table[3][2][2] = {
+      {{gemm_tc_kernel<1, 256, false, false>, gemm_tc_kernel<1, 256, false, true>},
+       {gemm_tc_kernel<1, 256, true, false>, gemm_tc_kernel<1, 256, true, true>}},
+      {{gemm_tc_kernel<2, 256, false, false>, gemm_tc_kernel<2, 256, false, true>},
+       {gemm_tc_kernel<2, 256, true, false>, gemm_tc_kernel<2, 256, true, true>}},
+      {{gemm_tc_kernel<2, 512, false, false>, gemm_tc_kernel<2, 512, false, true>},
+       {gemm_tc_kernel<2, 512, true, false>, gemm_tc_kernel<2, 512, true, true>}}};
+  static const uint32_t smem_of[3] = {Cfg<1, 256>::SMEM_BYTES, Cfg<2, 256>::SMEM_BYTES,
+                                      Cfg<2, 512>::SMEM_BYTES};
+  KernFn kern = table[variant][bk][cm];
+  const uint32_t smem = smem_of[variant];
   {
     std::lock_guard<std::mutex> lk(g_dev_mu);
-    if (!ds->attr_set[cg - 1][bk][cm]) {
+    if (!ds->attr_set[variant][bk][cm]) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
       if (cg == 2) {
@@ -426,16 +434,16 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
         int nclu = 0;
         e = cudaOccupancyMaxActiveClusters(&nclu, (void*)kern, &qc);
         if (e != cudaSuccess || nclu <= 0) nclu = ds->sm_count / 2;
-        ds->max_clusters[bk][cm] = nclu;
+        ds->max_clusters[variant][bk][cm] = nclu;
       }
-      ds->attr_set[cg - 1][bk][cm] = true;
+      ds->attr_set[variant][bk][cm] = true;
     }
   }
   int groups;
   if (cg == 1)
     groups = std::min(ds->sm_count, p.num_tiles);
   else
-    groups = std::min(ds->max_clusters[bk][cm], p.num_tiles);
+    groups = std::min(ds->max_clusters[variant][bk][cm], p.num_tiles);
   if (groups < 1) groups = 1;
 
   cudaLaunchConfig_t cfg = {};
@@ -555,6 +563,9 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_force_generic = value ? 1 : 0;
   } else if (!strcmp(key, "fault_flags")) {
     opt_fault_flags = value;
+  } else if (!strcmp(key, "tile_n")) {
+    if (value != 0 && value != 256 && value != 512) return B2G_ERR_INVALID_ARG;
+    opt_tile_n = value;
   } else {
     return B2G_ERR_INVALID_ARG;
   }
@@ -568,6 +579,7 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "timeout_ns")) return opt_timeout_ns;
   if (!strcmp(key, "force_generic")) return opt_force_generic;
   if (!strcmp(key, "fault_flags")) return opt_fault_flags;
+  if (!strcmp(key, "tile_n")) return opt_tile_n;
   return -1;
 }
 

@@ -63,30 +63,48 @@ struct GemmParams {
 };
 
 constexpr int kBM = 128;  // rows per CTA (UMMA M per CTA)
-constexpr int kBN = 256;  // columns per CTA group (UMMA N)
 constexpr int kBK = 64;   // K per stage: one 128-byte swizzle row of fp16
+constexpr int kUN = 256;  // N of one UMMA instruction
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 512;  // two 256-column fp32 accumulators
+constexpr uint32_t kTmemCols = 512;      // all of TMEM
 constexpr uint32_t kCBuf = 32 * 32 * 4;  // one 32x32 fp32 staging buffer
+constexpr uint32_t kSmemLimit = 232448;  // max dynamic shared memory per CTA on sm_100
 
-template <int CG>
+// CG: CTAs per tile (1, or 2 = cta_group::2 pair).  BN: tile width in columns (256 or 512);
+// a tile is (128*CG) x BN.  BN = 256 keeps two accumulators in TMEM (the epilogue of tile t
+// overlaps the main loop of tile t+1); BN = 512 fills TMEM with one accumulator and cuts the
+// operand bytes each CTA pulls from L2 per FLOP by a quarter.
+template <int CG, int BN>
 struct Cfg {
-  static constexpr int BN_CTA = kBN / CG;                          // B columns loaded per CTA
-  static constexpr uint32_t A_BYTES = kBM * kBK * 2;               // 16 KiB
-  static constexpr uint32_t B_BYTES = BN_CTA * kBK * 2;            // 32 or 16 KiB
-  static constexpr int STAGES = CG == 1 ? 4 : 6;
+  static_assert(CG == 1 || CG == 2, "CTA group");
+  static_assert(BN == 256 || BN == 512, "tile width");
+  static constexpr int NH = BN / kUN;                 // UMMA N-halves per k step
+  static constexpr int ACC_BUFS = BN == 256 ? 2 : 1;  // accumulators held in TMEM
+  static constexpr int BPH = kUN / CG;                // B columns per N-half held by one CTA
+  static constexpr int BN_CTA = BN / CG;              // B columns loaded per CTA
+  static constexpr uint32_t A_BYTES = kBM * kBK * 2;  // 16 KiB
+  static constexpr uint32_t B_BYTES = BN_CTA * kBK * 2;
+  static constexpr uint32_t HALF_BYTES = BPH * kBK * 2;  // one N-half of B in shared memory
+  static constexpr uint32_t EPI_BYTES = kEpiWarps * 2 * kCBuf;
+  static constexpr int NUM_BARS_FIXED = 2 + 2 + 1;
+  static constexpr int STAGES =
+      (int)((kSmemLimit - 1024 - EPI_BYTES - 256) / (A_BYTES + B_BYTES)) > 8
+          ? 8
+          : (int)((kSmemLimit - 1024 - EPI_BYTES - 256) / (A_BYTES + B_BYTES));
   static constexpr uint32_t OFF_B = STAGES * A_BYTES;
   static constexpr uint32_t OFF_C = OFF_B + STAGES * B_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_C + kEpiWarps * 2 * kCBuf;
-  static constexpr int NUM_BARS = 2 * STAGES + 2 + 2 + 1;
+  static constexpr uint32_t OFF_BAR = OFF_C + EPI_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + NUM_BARS_FIXED;
   static constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TX_BYTES = CG * (A_BYTES + B_BYTES);  // bytes per stage per group
+  static constexpr int CHUNKS = BN / 32;  // 32-column epilogue chunks per tile
 };
 
-static_assert(Cfg<1>::SMEM_BYTES <= 232448, "shared memory budget (CG=1)");
-static_assert(Cfg<2>::SMEM_BYTES <= 232448, "shared memory budget (CG=2)");
+static_assert(Cfg<1, 256>::SMEM_BYTES <= kSmemLimit && Cfg<1, 256>::STAGES >= 4, "CG=1 budget");
+static_assert(Cfg<2, 256>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256>::STAGES >= 6, "CG=2 budget");
+static_assert(Cfg<2, 512>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512>::STAGES >= 4, "BN=512 budget");
 
 // Instruction descriptor, kind::f16: D fp32 (bit 4), A/B fp16 (format 0), A K-major,
 // B major per template, N>>3 at bit 17, M>>4 at bit 24.
@@ -106,11 +124,11 @@ __device__ __forceinline__ void m_tile_origin(const GemmParams& p, int mt, int& 
   a0 = ia * p.ba;
 }
 
-template <int CG, bool B_KMAJOR, bool C_MCONTIG>
+template <int CG, int BN, bool B_KMAJOR, bool C_MCONTIG>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using C = Cfg<CG>;
+  using C = Cfg<CG, BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint32_t base = ptx::smem_u32(smem_raw);
   const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
@@ -164,6 +182,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int group_id = blockIdx.x / CG;
   const int num_groups = gridDim.x / CG;
 
+  // B columns of N-half h held by this CTA start at n0 + h*256 + cta_rank*BPH.
+  auto issue_b = [&](uint32_t sb, uint32_t fb, int n0, int kc, int jj) {
+#pragma unroll
+    for (int h = 0; h < C::NH; ++h) {
+      const int nh = n0 + h * kUN + (int)cta_rank * C::BPH;
+      const uint32_t dst = sb + (uint32_t)h * C::HALF_BYTES;
+      if constexpr (B_KMAJOR) {
+        ptx::tma_load_3d<CG>(dst, &tmB, fb, kc, jj, nh);
+      } else {
+#pragma unroll
+        for (int c = 0; c < C::BPH / 64; ++c)
+          ptx::tma_load_3d<CG>(dst + (uint32_t)c * 8192u, &tmB, fb, nh + 64 * c, kc, jj);
+      }
+    }
+  };
+
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -175,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int mt = pm * CG + (int)cta_rank;
         int i0, b0, a0;
         m_tile_origin(p, mt, i0, b0, a0);
-        const int nb = tn * kBN + (int)cta_rank * C::BN_CTA;
+        const int n0 = tn * BN;
         for (int kb = 0; kb < p.k_iters; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
@@ -188,16 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.fault_flags & 1) continue;
           const int jj = kb / p.k_blocks_per_j;
           const int kc = (kb - jj * p.k_blocks_per_j) * kBK;
-          const uint32_t sa = base + s * C::A_BYTES;
-          const uint32_t sb = base + C::OFF_B + s * C::B_BYTES;
-          ptx::tma_load_5d<CG>(sa, &tmA, fb, kc, jj, i0, b0, a0);
-          if constexpr (B_KMAJOR) {
-            ptx::tma_load_3d<CG>(sb, &tmB, fb, kc, jj, nb);
-          } else {
-#pragma unroll
-            for (int c = 0; c < C::BN_CTA / 64; ++c)
-              ptx::tma_load_3d<CG>(sb + c * 8192u, &tmB, fb, nb + 64 * c, kc, jj);
-          }
+          ptx::tma_load_5d<CG>(base + s * C::A_BYTES, &tmA, fb, kc, jj, i0, b0, a0);
+          issue_b(base + C::OFF_B + s * C::B_BYTES, fb, n0, kc, jj);
         }
       }
       // Teardown: every load this thread issued must land before the CTA can exit.  With
@@ -217,18 +243,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = make_idesc(kBM * CG, kBN, !B_KMAJOR);
+      constexpr uint32_t idesc = make_idesc(kBM * CG, kUN, !B_KMAJOR);
       int it = 0, tc = 0;
       bool ok = true;
       for (int t = group_id; t < p.num_tiles && ok; t += num_groups, ++tc) {
-        const int acc = tc & 1;
-        const uint32_t aph = (uint32_t)(tc >> 1) & 1u;
+        const int acc = (C::ACC_BUFS == 2) ? (tc & 1) : 0;
+        const uint32_t aph = (uint32_t)(C::ACC_BUFS == 2 ? (tc >> 1) : tc) & 1u;
         if (!ptx::mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag, err, ERR_WAIT_TEMPTY, lim)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)acc * kBN;
+        const uint32_t d = tmem_base + (uint32_t)acc * kUN;
         for (int kb = 0; kb < p.k_iters; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
@@ -242,9 +268,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k16 = 0; k16 < kBK / 16; ++k16) {
             const uint64_t ad = ptx::smem_desc_sw128(sa + 32u * k16, 16u, 1024u);
-            const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(sb + 32u * k16, 16u, 1024u)
-                                         : ptx::smem_desc_sw128(sb + 2048u * k16, 8192u, 1024u);
-            ptx::umma_f16<CG>(d, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < C::NH; ++h) {
+              const uint32_t bh = sb + (uint32_t)h * C::HALF_BYTES;
+              const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(bh + 32u * k16, 16u, 1024u)
+                                           : ptx::smem_desc_sw128(bh + 2048u * k16, 8192u, 1024u);
+              ptx::umma_f16<CG>(d + (uint32_t)h * kUN, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
+            }
           }
           ptx::umma_commit<CG>(empty_bar(s), (uint16_t)0x3);
         }
@@ -257,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;                  // TMEM lane quarter
+    const int q = warp & 3;  // TMEM lane quarter
     const uint32_t cbuf = base + C::OFF_C + (uint32_t)(warp - 2) * 2u * kCBuf;
     // This warp's 32-row sub-box inside the 128-row tile (flattened (a, b, i) order).
     const int r0 = 32 * q;
@@ -273,30 +303,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       m_tile_origin(p, mt, i0, b0, a0);
       const int ci = i0 + i_l, cb = b0 + b_l, ca = a0 + a_l;
       const bool rows_valid = mt < p.num_m_tiles && ci < p.i_size && cb < p.b_size && ca < p.a_size;
-      const int acc = tc & 1;
-      const uint32_t aph = (uint32_t)(tc >> 1) & 1u;
+      const int acc = (C::ACC_BUFS == 2) ? (tc & 1) : 0;
+      const uint32_t aph = (uint32_t)(C::ACC_BUFS == 2 ? (tc >> 1) : tc) & 1u;
       const bool got = ptx::mbar_wait(tfull_bar(acc), aph, abort_flag, err, ERR_WAIT_TFULL, lim);
       if (!__all_sync(0xffffffffu, got)) break;
       ptx::tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)acc * kBN;
-      const int n0 = tn * kBN;
-#pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t v[32];
-        ptx::tmem_ld_32x32b_x32(tbase + 32u * c, v);
-        ptx::tmem_ld_wait();
-        if (c == kBN / 32 - 1) {
-          // Accumulator fully read: hand it back to the MMA warp.
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if constexpr (CG == 1)
-              ptx::mbar_arrive(tempty_bar(acc));
-            else
-              ptx::mbar_arrive_cluster(tempty_bar(acc), 0);
-          }
-        }
-        if (!rows_valid || n0 + 32 * c >= p.n_size) continue;
+      const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)acc * kUN;
+      const int n0 = tn * BN;
+
+      // Stage chunk `ch` (32 columns of this warp's 32 rows) and TMA-store it.
+      auto store_chunk = [&](const uint32_t (&v)[32], int ch) {
+        const int gcol = n0 + 32 * ch;
+        if (!rows_valid || gcol >= p.n_size) return;
         const uint32_t buf = cbuf + (uint32_t)(nstore & 1) * kCBuf;
         if (lane == 0) ptx::bulk_wait_read<1>();
         __syncwarp();
@@ -318,12 +336,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) {
           if constexpr (!C_MCONTIG)
-            ptx::tma_store_4d(&tmC, buf, n0 + 32 * c, ci, cb, ca);
+            ptx::tma_store_4d(&tmC, buf, gcol, ci, cb, ca);
           else
-            ptx::tma_store_4d(&tmC, buf, ci, n0 + 32 * c, cb, ca);
+            ptx::tma_store_4d(&tmC, buf, ci, gcol, cb, ca);
           ptx::bulk_commit();
         }
         ++nstore;
+      };
+
+      // TMEM loads are software-pipelined: chunk ch+1 is in flight while chunk ch is stored.
+      uint32_t v0[32], v1[32];
+      ptx::tmem_ld_32x32b_x32(tbase, v0);
+#pragma unroll 1
+      for (int ch = 0; ch < C::CHUNKS; ch += 2) {
+        ptx::tmem_ld_wait();
+        ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 1), v1);
+        store_chunk(v0, ch);
+        ptx::tmem_ld_wait();
+        if (ch + 2 < C::CHUNKS) {
+          ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 2), v0);
+        } else {
+          // Accumulator fully read: hand it back to the MMA warp.
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 1)
+              ptx::mbar_arrive(tempty_bar(acc));
+            else
+              ptx::mbar_arrive_cluster(tempty_bar(acc), 0);
+          }
+        }
+        store_chunk(v1, ch + 1);
       }
     }
     if (lane == 0) ptx::bulk_wait_all();

@@ -28,6 +28,11 @@ def assert_close(orc, got, ref, K, max_a=1.0, max_b=1.0, what=""):
     return ma, mr
 
 
+# kernel variants of the tensor-core path: (CTAs per tile, tile width)
+VARIANTS = [(1, 256), (2, 256), (2, 512)]
+VARIANT_IDS = ["cta1_n256", "cta2_n256", "cta2_n512"]
+
+
 @contextlib.contextmanager
 def options(b2g, **kw):
     old = {k: b2g.get_option(k) for k in kw}

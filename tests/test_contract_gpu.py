@@ -12,7 +12,7 @@ Tolerance: |C - R| <= 1e-3*sqrt(K)*max|a|*max|b| + 1e-3*|R| against the FP64 ora
 import numpy as np
 import pytest
 
-from gpu_util import assert_close, options, to_dev
+from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -47,30 +47,30 @@ def _contract(b2g, torch, orc, a_shape, a_order, n, c_order, b_kmajor=False, see
     return path
 
 
-@pytest.mark.parametrize("cg", [1, 2])
-def test_contract_baseline_form_small(b2g, cuda, orc, cg):
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+def test_contract_baseline_form_small(b2g, cuda, orc, cg, tn):
     """BASELINE configs[2] layout at reduced size: coalesces to a plain 2-D GEMM view."""
-    with options(b2g, cta_group=cg):
+    with options(b2g, cta_group=cg, tile_n=tn):
         path = _contract(b2g, cuda, orc, (2, 4, 32, 4, 64), (0, 1, 2, 3, 4), 256, (0, 1, 2, 3))
     assert path in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
 
 
-@pytest.mark.parametrize("cg", [1, 2])
-def test_contract_permuted_memory_not_coalescible(b2g, cuda, orc, cg):
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+def test_contract_permuted_memory_not_coalescible(b2g, cuda, orc, cg, tn):
     """A stored as [b][a][i][j][k] and C as [b][a][i][n]: the M modes cannot be merged, so the
     load box spans (i, b, a) of a rank-5 tensor map and the store box spans three modes."""
-    with options(b2g, cta_group=cg):
+    with options(b2g, cta_group=cg, tile_n=tn):
         path = _contract(b2g, cuda, orc, (2, 4, 16, 2, 64), (1, 0, 2, 3, 4), 192, (1, 0, 2, 3))
     assert path in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
 
 
-@pytest.mark.parametrize("cg", [1, 2])
-def test_contract_ragged_k_mode(b2g, cuda, orc, cg):
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+def test_contract_ragged_k_mode(b2g, cuda, orc, cg, tn):
     """A stored [b][a][j][i][k], so neither the K modes (j, k) nor the M modes (b, i) merge;
     k = 96 is not a multiple of the 64-wide K block: each j visits two K blocks, the second
     half zero-filled by TMA; i = 100 does not divide the 128-row tile (28 rows zero-filled,
     clipped at the store)."""
-    with options(b2g, cta_group=cg):
+    with options(b2g, cta_group=cg, tile_n=tn):
         path = _contract(b2g, cuda, orc, (1, 3, 100, 3, 96), (1, 0, 3, 2, 4), 136, (1, 0, 2, 3))
     assert path in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
 
@@ -97,11 +97,11 @@ def _reference_form(b2g, torch, orc, mt, rt, nt, rt_l, bt, seed=9):
     return path
 
 
-@pytest.mark.parametrize("cg", [1, 2])
-def test_contract_reference_form_small(b2g, cuda, orc, cg):
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+def test_contract_reference_form_small(b2g, cuda, orc, cg, tn):
     """rt=8, mt=16, nt=4, rt_l=64, bt=256: K-major B and an M-contiguous output (8-row
     store boxes)."""
-    with options(b2g, cta_group=cg):
+    with options(b2g, cta_group=cg, tile_n=tn):
         path = _reference_form(b2g, cuda, orc, mt=16, rt=8, nt=4, rt_l=64, bt=256)
     assert path in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
 

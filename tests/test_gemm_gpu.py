@@ -8,7 +8,7 @@ Inputs: seeded U[-1,1] fp16 (max|a| = max|b| = 1).
 import numpy as np
 import pytest
 
-from gpu_util import assert_close, options, padded_f16, to_dev
+from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, padded_f16, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -37,24 +37,24 @@ def test_fill_uniform_matches_oracle(b2g, cuda, orc):
     assert np.array_equal(d.cpu().numpy().view(np.uint16), host.view(np.uint16))
 
 
-@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
 @pytest.mark.parametrize("MNK", [(128, 256, 64), (256, 256, 128), (512, 768, 320), (1024, 1024, 1024)])
-def test_gemm_tile_multiples(b2g, cuda, orc, cg, MNK):
+def test_gemm_tile_multiples(b2g, cuda, orc, cg, tn, MNK):
     M, N, K = MNK
-    with options(b2g, cta_group=cg):
+    with options(b2g, cta_group=cg, tile_n=tn):
         A, B, C, path = _run_gemm(b2g, cuda, orc, M, N, K)
     assert path == (b2g.PATH_TC_1CTA if cg == 1 else b2g.PATH_TC_2CTA)
     assert_close(orc, C, orc.gemm_f64(A, B), K, what="%s cg=%d" % (MNK, cg))
 
 
-@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
 @pytest.mark.parametrize("MNK", [(1, 8, 8), (127, 129, 136), (129, 127, 1000), (1000, 1000, 8),
                                  (300, 40, 72), (8, 520, 64), (385, 264, 4104)])
-def test_gemm_ragged_aligned_pitch(b2g, cuda, orc, cg, MNK):
+def test_gemm_ragged_aligned_pitch(b2g, cuda, orc, cg, tn, MNK):
     """Ragged M/N/K (zero-filled loads, clipped stores) with 16-byte-aligned row pitches."""
     M, N, K = MNK
     r8 = lambda x: (x + 7) // 8 * 8
-    with options(b2g, cta_group=cg):
+    with options(b2g, cta_group=cg, tile_n=tn):
         A, B, C, path = _run_gemm(b2g, cuda, orc, M, N, K, lda=r8(K), ldb=r8(N), ldc=r8(N) + 4)
     assert path in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
     assert_close(orc, C, orc.gemm_f64(A, B), K, what="%s cg=%d" % (MNK, cg))
@@ -71,11 +71,11 @@ def test_gemm_unaligned_runs_generic_bit_exact(b2g, cuda, orc, MNK):
     assert np.array_equal(C.view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("cg", [1, 2])
-def test_gemm_single_element(b2g, cuda, orc, cg):
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+def test_gemm_single_element(b2g, cuda, orc, cg, tn):
     """M = N = K = 1: every mode has extent 1, so the TMA path takes it (boxes larger than
     the tensor, zero-filled loads, clipped store)."""
-    with options(b2g, cta_group=cg):
+    with options(b2g, cta_group=cg, tile_n=tn):
         A, B, C, path = _run_gemm(b2g, cuda, orc, 1, 1, 1)
     assert path in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
     assert C[0, 0] == np.float32(A[0, 0]) * np.float32(B[0, 0])

@@ -12,7 +12,7 @@ import os
 import numpy as np
 import pytest
 
-from gpu_util import assert_close, options, to_dev
+from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, to_dev
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -30,8 +30,8 @@ def _padded(torch, X, ld):
     return to_dev(torch, P)
 
 
-@pytest.mark.parametrize("cg", [1, 2])
-def test_golden_gemm_tensor_core_path(b2g, cuda, orc, cg):
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+def test_golden_gemm_tensor_core_path(b2g, cuda, orc, cg, tn):
     torch = cuda
     r8 = lambda x: (x + 7) // 8 * 8
     for A, B, C in _cases():
@@ -39,7 +39,7 @@ def test_golden_gemm_tensor_core_path(b2g, cuda, orc, cg):
         N = B.shape[1]
         lda, ldb, ldc = r8(K), r8(N), r8(N)
         dC = torch.full((M, ldc), float("nan"), dtype=torch.float32, device="cuda")
-        with options(b2g, cta_group=cg):
+        with options(b2g, cta_group=cg, tile_n=tn):
             b2g.gemm(_padded(torch, A, lda), _padded(torch, B, ldb), dC, M, N, K, lda, ldb, ldc)
         torch.cuda.synchronize()
         assert b2g.last_path() in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
@@ -77,9 +77,9 @@ def _ref_contraction(b2g, torch, force_generic):
     return z, dOut.cpu().numpy(), b2g.last_path(), nt * rt_l
 
 
-@pytest.mark.parametrize("cg", [1, 2])
-def test_golden_reference_contraction_tensor_core(b2g, cuda, orc, cg):
-    with options(b2g, cta_group=cg):
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+def test_golden_reference_contraction_tensor_core(b2g, cuda, orc, cg, tn):
+    with options(b2g, cta_group=cg, tile_n=tn):
         z, out, path, K = _ref_contraction(b2g, cuda, 0)
     assert path in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
     assert_close(orc, out, z["Out"].astype(np.float64), K, what="reference contraction")
