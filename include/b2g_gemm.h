@@ -62,6 +62,16 @@ int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t M, int64_t 
                      int64_t lda, int64_t ldb, int64_t ldc, void* stream);
 
 /*
+ * C = alpha * A.B + beta * C with the layout of b2g_gemm_f16_f32.  beta == 0 never reads C;
+ * beta == 1 adds alpha*A.B into C (TMA reduce-add in the epilogue: each element receives one
+ * addition per call, so the result is deterministic); any other beta scales C first.
+ * Extends the reference's beta = 0 semantics (mmm.cpp:1372) with the alpha/beta epilogue of
+ * its rocBLAS comparison call (rocblas_gemm_ex alpha/beta, mmm.cpp:1512-1513).
+ */
+int b2g_gemm_ex(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K,
+                int64_t lda, int64_t ldb, int64_t ldc, float alpha, float beta, void* stream);
+
+/*
  * The reference's drop-in form: contiguous row-major operands, lda = K, ldb = N, ldc = N,
  * default stream.  Same as GEMM_Naive's contract (mmm.cpp:52-62).
  */
@@ -83,6 +93,12 @@ int b2g_contract5d_f16_f32(const void* A, const int64_t a_shape[5], const int64_
                            const void* B, const int64_t b_shape[3], const int64_t b_stride[3],
                            float* C, const int64_t c_shape[4], const int64_t c_stride[4],
                            void* stream);
+
+/* The contraction with the alpha/beta epilogue of b2g_gemm_ex. */
+int b2g_contract5d_ex(const void* A, const int64_t a_shape[5], const int64_t a_stride[5],
+                      const void* B, const int64_t b_shape[3], const int64_t b_stride[3],
+                      float* C, const int64_t c_shape[4], const int64_t c_stride[4], float alpha,
+                      float beta, void* stream);
 
 /*
  * Fill n fp16 elements with the seeded uniform [-1,1] sequence: element e of the logical

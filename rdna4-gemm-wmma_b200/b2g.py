@@ -51,6 +51,12 @@ def load(path=None):
     i64p = ctypes.POINTER(ctypes.c_int64)
     L.b2g_gemm_f16_f32.restype = ctypes.c_int
     L.b2g_gemm_f16_f32.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
+    L.b2g_gemm_ex.restype = ctypes.c_int
+    L.b2g_gemm_ex.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_float,
+                              ctypes.c_float, vp]
+    L.b2g_contract5d_ex.restype = ctypes.c_int
+    L.b2g_contract5d_ex.argtypes = [vp, i64p, i64p, vp, i64p, i64p, vp, i64p, i64p,
+                                    ctypes.c_float, ctypes.c_float, vp]
     L.b2g_gemm.restype = ctypes.c_int
     L.b2g_gemm.argtypes = [vp, vp, vp, i64, i64, i64]
     L.b2g_contract5d_f16_f32.restype = ctypes.c_int
@@ -118,6 +124,14 @@ def gemm(A, B, C, M, N, K, lda=None, ldb=None, ldc=None, stream=None):
                               N if ldc is None else ldc, _stream(stream)))
 
 
+def gemm_ex(A, B, C, M, N, K, alpha=1.0, beta=0.0, lda=None, ldb=None, ldc=None, stream=None):
+    """C = alpha * A[M,K].B[K,N] + beta * C."""
+    L = load()
+    _check(L.b2g_gemm_ex(_ptr(A), _ptr(B), _ptr(C), M, N, K, K if lda is None else lda,
+                         N if ldb is None else ldb, N if ldc is None else ldc, float(alpha),
+                         float(beta), _stream(stream)))
+
+
 def GEMM(A, B, C, M, N, K):
     """The reference's drop-in form (contiguous, default stream)."""
     _check(load().b2g_gemm(_ptr(A), _ptr(B), _ptr(C), M, N, K))
@@ -135,6 +149,14 @@ def contract5d(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride,
     _check(L.b2g_contract5d_f16_f32(_ptr(A), _arr(a_shape, 5), _arr(a_stride, 5), _ptr(B),
                                     _arr(b_shape, 3), _arr(b_stride, 3), _ptr(C), _arr(c_shape, 4),
                                     _arr(c_stride, 4), _stream(stream)))
+
+
+def contract5d_ex(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, alpha=1.0,
+                  beta=0.0, stream=None):
+    L = load()
+    _check(L.b2g_contract5d_ex(_ptr(A), _arr(a_shape, 5), _arr(a_stride, 5), _ptr(B),
+                               _arr(b_shape, 3), _arr(b_stride, 3), _ptr(C), _arr(c_shape, 4),
+                               _arr(c_stride, 4), float(alpha), float(beta), _stream(stream)))
 
 
 def fill_uniform(dst, n, seed, offset=0, stream=None):

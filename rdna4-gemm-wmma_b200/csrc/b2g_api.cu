@@ -48,6 +48,7 @@ static std::atomic<int64_t> opt_timeout_ns{2000000000LL};
 static std::atomic<int64_t> opt_force_generic{0};
 static std::atomic<int64_t> opt_fault_flags{0};
 static std::atomic<int64_t> opt_tile_n{0};  // 0 = choose by shape, else 256 or 512
+static std::atomic<int64_t> opt_store_hint{0};
 
 // ------------------------------------------------------------------ driver entry point
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -100,7 +101,7 @@ struct Geo {
 };
 
 __global__ void gemm_generic_kernel(const __half* __restrict__ A, const __half* __restrict__ B,
-                                    float* __restrict__ C, const Geo g) {
+                                    float* __restrict__ C, const Geo g, float alpha, float beta) {
   const int64_t rows = g.as[0] * g.as[1] * g.as[2];
   const int64_t total = rows * g.n;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -116,7 +117,24 @@ __global__ void gemm_generic_kernel(const __half* __restrict__ A, const __half* 
       for (int64_t k = 0; k < g.as[4]; ++k)
         acc += __half2float(ar[j * g.ast[3] + k * g.ast[4]]) *
                __half2float(bc[j * g.bst[0] + k * g.bst[1]]);
-    C[ia * g.cst[0] + ib * g.cst[1] + ii * g.cst[2] + col * g.cst[3]] = acc;
+    float* c = C + ia * g.cst[0] + ib * g.cst[1] + ii * g.cst[2] + col * g.cst[3];
+    const float out = alpha == 1.0f ? acc : alpha * acc;
+    *c = beta == 0.0f ? out : out + beta * *c;  // beta == 0: C is not read
+  }
+}
+
+// C *= beta over the strided (a, b, i, n) view (the beta part of C = alpha*A.B + beta*C when
+// the tensor-core kernel then adds alpha*A.B with a TMA reduce).
+__global__ void scale_c_kernel(float* __restrict__ C, const Geo g, float beta) {
+  const int64_t total = g.as[0] * g.as[1] * g.as[2] * g.n;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = idx / g.n, col = idx - row * g.n;
+    const int64_t ii = row % g.as[2];
+    const int64_t ib = (row / g.as[2]) % g.as[1];
+    const int64_t ia = row / (g.as[2] * g.as[1]);
+    float* c = C + ia * g.cst[0] + ib * g.cst[1] + ii * g.cst[2] + col * g.cst[3];
+    *c = beta * *c;
   }
 }
 
@@ -175,7 +193,7 @@ static inline bool al16(int64_t bytes) { return (bytes & 15) == 0; }
 // ------------------------------------------------------------------ core dispatch
 static int run(const void* A, const int64_t as[5], const int64_t ast[5], const void* B,
                const int64_t bs[3], const int64_t bst[3], float* Cp, const int64_t cs[4],
-               const int64_t cst[4], cudaStream_t stream) {
+               const int64_t cst[4], float alpha, float beta, cudaStream_t stream) {
   // ---- validation
   for (int t = 0; t < 5; ++t)
     if (as[t] < 0) return fail(B2G_ERR_INVALID_ARG, "negative A extent");
@@ -201,7 +219,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   int rc = device_state(dev, &ds);
   if (rc) return rc;
 
-  auto launch_generic = [&](int path) -> int {
+  auto make_geo = [&]() {
     Geo g;
     for (int t = 0; t < 5; ++t) {
       g.as[t] = as[t];
@@ -210,19 +228,29 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     for (int t = 0; t < 3; ++t) g.bst[t] = bst[t];
     for (int t = 0; t < 4; ++t) g.cst[t] = cst[t];
     g.n = N;
-    const int64_t total = M * N;
-    const int threads = 256;
-    int64_t blocks = (total + threads - 1) / threads;
-    blocks = std::min<int64_t>(blocks, (int64_t)ds->sm_count * 32);
-    gemm_generic_kernel<<<(unsigned)blocks, threads, 0, stream>>>(
-        static_cast<const __half*>(A), static_cast<const __half*>(B), Cp, g);
+    return g;
+  };
+  const int64_t total = M * N;
+  const int eth = 256;
+  const unsigned eblocks =
+      (unsigned)std::min<int64_t>((total + eth - 1) / eth, (int64_t)ds->sm_count * 32);
+  auto launch_generic = [&](int path) -> int {
+    gemm_generic_kernel<<<eblocks, eth, 0, stream>>>(static_cast<const __half*>(A),
+                                                     static_cast<const __half*>(B), Cp,
+                                                     make_geo(), alpha, beta);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "generic kernel launch");
     t_path = path;
     return B2G_OK;
   };
 
-  if (K == 0) return launch_generic(B2G_PATH_ZERO);
+  if (K == 0 || alpha == 0.0f) {  // C = beta*C
+    if (beta == 1.0f) {
+      t_path = B2G_PATH_ZERO;
+      return B2G_OK;
+    }
+    return launch_generic(B2G_PATH_ZERO);
+  }
   if (opt_force_generic.load()) return launch_generic(B2G_PATH_GENERIC);
   if (ds->cc_major != 10) return launch_generic(B2G_PATH_GENERIC);
 
@@ -323,7 +351,13 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   int cg = (int)opt_cta_group.load();
   if (cg != 1 && cg != 2) cg = (nmt64 >= 2) ? 2 : 1;
   int bn = (int)opt_tile_n.load();
-  if (bn != 256 && bn != 512) bn = (cg == 2 && N >= 1024) ? 512 : 256;
+  if (bn != 256 && bn != 512) {
+    // 512-wide pair tiles pull a quarter fewer operand bytes from L2 per FLOP; use them when
+    // there are enough of them to fill every CTA pair at least twice.
+    const int64_t pairs = std::max(1, ds->sm_count / 2);
+    const int64_t t512 = ((nmt64 + 1) / 2) * ((N + 511) / 512);
+    bn = (cg == 2 && t512 >= 2 * pairs) ? 512 : 256;
+  }
   if (cg == 1) bn = 256;  // one CTA: 256 columns (TMEM holds two accumulators)
   const int64_t nnt64 = (N + bn - 1) / bn;
   if (nmt64 * nnt64 > INT32_MAX / 4) return launch_generic(B2G_PATH_GENERIC);
@@ -396,6 +430,14 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.num_tiles = p.num_pm_tiles * p.num_n_tiles;
   int rg = (int)opt_raster_group.load();
   p.raster_group = rg > 0 ? rg : (cg == 2 ? 8 : 16);  // measured best on 8192^3
+  p.store_hint = (int)opt_store_hint.load();
+  p.alpha = alpha;
+  p.accumulate = beta != 0.0f ? 1 : 0;
+  if (beta != 0.0f && beta != 1.0f) {  // C = beta*C first; the kernel then adds alpha*A.B
+    scale_c_kernel<<<eblocks, eth, 0, stream>>>(Cp, make_geo(), beta);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "scale kernel launch");
+  }
   p.timeout_ns = (unsigned long long)opt_timeout_ns.load();
   p.fault_flags = (int)opt_fault_flags.load();
 
@@ -471,8 +513,9 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
 // ==================================================================== C ABI
 using namespace b2g;
 
-extern "C" int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t M, int64_t N,
-                                int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+extern "C" int b2g_gemm_ex(const void* A, const void* B, float* C, int64_t M, int64_t N,
+                           int64_t K, int64_t lda, int64_t ldb, int64_t ldc, float alpha,
+                           float beta, void* stream) {
   t_err.clear();
   if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
   if (lda < std::max<int64_t>(K, 1) || ldb < std::max<int64_t>(N, 1) || ldc < std::max<int64_t>(N, 1))
@@ -480,7 +523,12 @@ extern "C" int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t 
   const int64_t as[5] = {1, 1, M, 1, K}, ast[5] = {0, 0, lda, 0, 1};
   const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
   const int64_t cs[4] = {1, 1, M, N}, cst[4] = {0, 0, ldc, 1};
-  return run(A, as, ast, B, bs, bst, C, cs, cst, static_cast<cudaStream_t>(stream));
+  return run(A, as, ast, B, bs, bst, C, cs, cst, alpha, beta, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t M, int64_t N,
+                                int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
+  return b2g_gemm_ex(A, B, C, M, N, K, lda, ldb, ldc, 1.0f, 0.0f, stream);
 }
 
 extern "C" int b2g_gemm(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K) {
@@ -488,16 +536,25 @@ extern "C" int b2g_gemm(const void* A, const void* B, float* C, int64_t M, int64
                           std::max<int64_t>(N, 1), nullptr);
 }
 
+extern "C" int b2g_contract5d_ex(const void* A, const int64_t a_shape[5],
+                                 const int64_t a_stride[5], const void* B,
+                                 const int64_t b_shape[3], const int64_t b_stride[3], float* C,
+                                 const int64_t c_shape[4], const int64_t c_stride[4], float alpha,
+                                 float beta, void* stream) {
+  t_err.clear();
+  if (!a_shape || !a_stride || !b_shape || !b_stride || !c_shape || !c_stride)
+    return fail(B2G_ERR_INVALID_ARG, "null shape/stride array");
+  return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, alpha, beta,
+             static_cast<cudaStream_t>(stream));
+}
+
 extern "C" int b2g_contract5d_f16_f32(const void* A, const int64_t a_shape[5],
                                       const int64_t a_stride[5], const void* B,
                                       const int64_t b_shape[3], const int64_t b_stride[3], float* C,
                                       const int64_t c_shape[4], const int64_t c_stride[4],
                                       void* stream) {
-  t_err.clear();
-  if (!a_shape || !a_stride || !b_shape || !b_stride || !c_shape || !c_stride)
-    return fail(B2G_ERR_INVALID_ARG, "null shape/stride array");
-  return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride,
-             static_cast<cudaStream_t>(stream));
+  return b2g_contract5d_ex(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, 1.0f,
+                           0.0f, stream);
 }
 
 extern "C" int b2g_fill_uniform_f16(void* dst, int64_t n, uint64_t seed, uint64_t offset,
@@ -563,6 +620,8 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_force_generic = value ? 1 : 0;
   } else if (!strcmp(key, "fault_flags")) {
     opt_fault_flags = value;
+  } else if (!strcmp(key, "store_hint")) {
+    opt_store_hint = value ? 1 : 0;
   } else if (!strcmp(key, "tile_n")) {
     if (value != 0 && value != 256 && value != 512) return B2G_ERR_INVALID_ARG;
     opt_tile_n = value;
@@ -580,6 +639,7 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "force_generic")) return opt_force_generic;
   if (!strcmp(key, "fault_flags")) return opt_fault_flags;
   if (!strcmp(key, "tile_n")) return opt_tile_n;
+  if (!strcmp(key, "store_hint")) return opt_store_hint;
   return -1;
 }
 

@@ -58,6 +58,9 @@ struct GemmParams {
   int k_iters;                 // j * k_blocks_per_j
   int num_tiles;               // num_pm_tiles * num_n_tiles
   int raster_group;            // strip height of the tile order, in CTA-group tiles
+  int store_hint;              // 1 = C stores carry an L2 evict-first hint
+  int accumulate;              // 1 = C += alpha*A.B (TMA reduce-add), 0 = C = alpha*A.B
+  float alpha;                 // scale of A.B
   unsigned long long timeout_ns;
   int fault_flags;             // test-only: bit 0 = producer issues no loads (forces a timeout)
 };
@@ -246,7 +249,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = make_idesc(kBM * CG, kUN, !B_KMAJOR);
       int it = 0, tc = 0;
       bool ok = true;
+      // Issue the MMAs of K block kb from stage s into N-halves [h_lo, h_hi).
+      auto issue_mma = [&](uint32_t d, int s, int kb, int h_lo, int h_hi) {
+        const uint32_t sa = base + s * C::A_BYTES;
+        const uint32_t sb = base + C::OFF_B + s * C::B_BYTES;
+#pragma unroll
+        for (int k16 = 0; k16 < kBK / 16; ++k16) {
+          const uint64_t ad = ptx::smem_desc_sw128(sa + 32u * k16, 16u, 1024u);
+#pragma unroll
+          for (int h = 0; h < C::NH; ++h) {
+            if (h < h_lo || h >= h_hi) continue;
+            const uint32_t bh = sb + (uint32_t)h * C::HALF_BYTES;
+            const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(bh + 32u * k16, 16u, 1024u)
+                                         : ptx::smem_desc_sw128(bh + 2048u * k16, 8192u, 1024u);
+            ptx::umma_f16<CG>(d + (uint32_t)h * kUN, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
+          }
+        }
+      };
       for (int t = group_id; t < p.num_tiles && ok; t += num_groups, ++tc) {
+        // BN = 256: two accumulators, tempty[acc] guards accumulator acc.
+        // BN = 512: one accumulator, tempty[h] guards its N-half h (the epilogue frees the
+        // halves one after the other).
         const int acc = (C::ACC_BUFS == 2) ? (tc & 1) : 0;
         const uint32_t aph = (uint32_t)(C::ACC_BUFS == 2 ? (tc >> 1) : tc) & 1u;
         if (!ptx::mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag, err, ERR_WAIT_TEMPTY, lim)) {
@@ -255,7 +278,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)acc * kUN;
-        for (int kb = 0; kb < p.k_iters; ++kb, ++it) {
+        int kb = 0;
+        if constexpr (C::NH == 2) {
+          // Half 0 of every K block already in shared memory first, then wait for half 1 of
+          // the accumulator (still being read by the epilogue) and complete those blocks.
+          const int pro = p.k_iters < C::STAGES ? p.k_iters : C::STAGES;
+          for (; kb < pro; ++kb) {
+            const int s = (it + kb) % C::STAGES;
+            const uint32_t ph = (uint32_t)((it + kb) / C::STAGES) & 1u;
+            if (!ptx::mbar_wait(full_bar(s), ph, abort_flag, err, ERR_WAIT_FULL, lim)) {
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
+            issue_mma(d, s, kb, 0, 1);
+          }
+          if (!ok) break;
+          if (!ptx::mbar_wait(tempty_bar(1), aph ^ 1u, abort_flag, err, ERR_WAIT_TEMPTY, lim)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          for (int k2 = 0; k2 < pro; ++k2) {
+            const int s = (it + k2) % C::STAGES;
+            issue_mma(d, s, k2, 1, 2);
+            ptx::umma_commit<CG>(empty_bar(s), (uint16_t)0x3);
+          }
+          it += pro;
+        }
+        for (; kb < p.k_iters; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
           if (!ptx::mbar_wait(full_bar(s), ph, abort_flag, err, ERR_WAIT_FULL, lim)) {
@@ -263,19 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t sa = base + s * C::A_BYTES;
-          const uint32_t sb = base + C::OFF_B + s * C::B_BYTES;
-#pragma unroll
-          for (int k16 = 0; k16 < kBK / 16; ++k16) {
-            const uint64_t ad = ptx::smem_desc_sw128(sa + 32u * k16, 16u, 1024u);
-#pragma unroll
-            for (int h = 0; h < C::NH; ++h) {
-              const uint32_t bh = sb + (uint32_t)h * C::HALF_BYTES;
-              const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(bh + 32u * k16, 16u, 1024u)
-                                           : ptx::smem_desc_sw128(bh + 2048u * k16, 8192u, 1024u);
-              ptx::umma_f16<CG>(d + (uint32_t)h * kUN, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
-            }
-          }
+          issue_mma(d, s, kb, 0, C::NH);
           ptx::umma_commit<CG>(empty_bar(s), (uint16_t)0x3);
         }
         if (!ok) break;
@@ -318,27 +357,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t buf = cbuf + (uint32_t)(nstore & 1) * kCBuf;
         if (lane == 0) ptx::bulk_wait_read<1>();
         __syncwarp();
+        uint32_t w[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          w[j] = p.alpha == 1.0f ? v[j] : __float_as_uint(__uint_as_float(v[j]) * p.alpha);
         if constexpr (!C_MCONTIG) {
           // Row `lane` as 8 16-byte chunks, 128-byte swizzle: chunk j -> j ^ (row % 8).
           const uint32_t row = buf + (uint32_t)lane * 128u;
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            ptx::st_shared_v4(row + (uint32_t)((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1],
-                              v[4 * j + 2], v[4 * j + 3]);
+            ptx::st_shared_v4(row + (uint32_t)((j ^ (lane & 7)) << 4), w[4 * j], w[4 * j + 1],
+                              w[4 * j + 2], w[4 * j + 3]);
         } else {
           // Box order (i, n, b, a): element (row, col) at ((row / si) * 32 + col) * si + row % si.
           const int blk = lane / p.si, il = lane - blk * p.si;
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            ptx::st_shared_b32(buf + 4u * (uint32_t)((blk * 32 + j) * p.si + il), v[j]);
+            ptx::st_shared_b32(buf + 4u * (uint32_t)((blk * 32 + j) * p.si + il), w[j]);
         }
         ptx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if constexpr (!C_MCONTIG)
-            ptx::tma_store_4d(&tmC, buf, gcol, ci, cb, ca);
+          const int x0 = C_MCONTIG ? ci : gcol, x1 = C_MCONTIG ? gcol : ci;
+          if (p.accumulate)
+            ptx::tma_reduce_add_4d(&tmC, buf, x0, x1, cb, ca);
+          else if (p.store_hint)
+            ptx::tma_store_4d_hint(&tmC, buf, x0, x1, cb, ca, ptx::policy_evict_first());
           else
-            ptx::tma_store_4d(&tmC, buf, ci, gcol, cb, ca);
+            ptx::tma_store_4d(&tmC, buf, x0, x1, cb, ca);
           ptx::bulk_commit();
         }
         ++nstore;
@@ -353,19 +399,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 1), v1);
         store_chunk(v0, ch);
         ptx::tmem_ld_wait();
-        if (ch + 2 < C::CHUNKS) {
-          ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 2), v0);
-        } else {
-          // Accumulator fully read: hand it back to the MMA warp.
+        if ((ch + 1) % 8 == 7) {
+          // An N-half (BN = 512) or the whole accumulator (BN = 256) has been read: hand it
+          // back to the MMA warp.
+          const int rel = C::ACC_BUFS == 2 ? acc : (ch + 1) / 8;
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) {
             if constexpr (CG == 1)
-              ptx::mbar_arrive(tempty_bar(acc));
+              ptx::mbar_arrive(tempty_bar(rel));
             else
-              ptx::mbar_arrive_cluster(tempty_bar(acc), 0);
+              ptx::mbar_arrive_cluster(tempty_bar(rel), 0);
           }
         }
+        if (ch + 2 < C::CHUNKS) ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 2), v0);
         store_chunk(v1, ch + 1);
       }
     }
