@@ -221,6 +221,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
+    ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "sharded32768"],
+                    help="gemm8192: BASELINE configs[1] per GPU (the default line); "
+                         "sharded32768: BASELINE configs[4], one 32768^3 GEMM as M-row slabs "
+                         "over the N GPUs, B broadcast in K panels inside every step")
     ap.add_argument("--kernel-only", action="store_true",
                     help="device-resident GEMM steps only (no e2e, CPU baseline or clock "
                          "sampling): the command profiled with ncu")
@@ -240,6 +244,8 @@ def main():
     if ws > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     b2g = load_b2g()
+    if args.workload == "sharded32768":
+        return run_sharded(args, torch, dist, b2g, ws, rank, local, dev)
 
     M, N, K = M_PER_GPU, N_DIM, K_DIM
     flops = 2.0 * M * N * K
@@ -357,6 +363,73 @@ def main():
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_sharded(args, torch, dist, b2g, ws, rank, local, dev):
+    """C[32768,32768] = A.B with A/C as M-row slabs over the ws ranks and
+    B broadcast from rank 0 in K panels inside every step (b2g_gemm_sharded over the
+    library's own NCCL communicator).  Strong scaling: the total work is fixed."""
+    import numpy as np
+    M = N = K = 32768
+    uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        uid.copy_(torch.from_numpy(np.frombuffer(b2g.comm_unique_id(), dtype=np.uint8).copy()))
+    if ws > 1:
+        dist.broadcast(uid, src=0)
+    comm = b2g.comm_init(ws, rank, bytes(uid.cpu().numpy().tobytes()))
+    row0, rows = b2g.slab_rows(M, ws, rank)
+    stream = torch.cuda.current_stream()
+    dA = torch.empty((rows, K), dtype=torch.float16, device=dev)
+    dB = torch.empty((K, N), dtype=torch.float16, device=dev)
+    dC = torch.empty((rows, N), dtype=torch.float32, device=dev)
+    b2g.fill_uniform(dA, rows * K, 1, row0 * K, stream)
+    if rank == 0:
+        b2g.fill_uniform(dB, K * N, 2, 0, stream)
+    panels = 8
+
+    def step():
+        b2g.gemm_sharded(dA, dB, dC, M, N, K, comm, root=0, k_panels=panels, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # spot check: first row of this rank's slab
+    from oracle import orc
+    ref = orc.gemm_f64(orc.uniform_f16((1, K), 1, row0 * K), orc.uniform_f16((K, N), 2))
+    bad = orc.check(dC[:1].cpu().numpy(), ref, K, 1.0, 1.0)[0]
+    status = b2g.device_status()
+    b2g.comm_destroy(comm)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        flops = 2.0 * M * N * K
+        print(json.dumps({
+            "metric": "sharded_gemm_tflops_32768cubed_fp16_fp32", "value": flops * args.steps / (ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 in, f32 accumulate/out",
+            "data": "synthetic: seeded U[-1,1] fp16 generated on the device",
+            "config": {"workload": "gemm 32768^3 as M-row slabs over N GPUs, B broadcast from rank 0 "
+                                   "in %d K panels every step (BASELINE configs[4])" % panels,
+                       "rows_per_rank": rows, "k_panels": panels},
+            "row0_out_of_tolerance": bad, "device_status": status,
+            "gpu_launches": args.steps * panels}), flush=True)
     return 0
 
 

@@ -108,6 +108,32 @@ int b2g_contract5d_ex(const void* A, const int64_t a_shape[5], const int64_t a_s
  */
 int b2g_fill_uniform_f16(void* dst, int64_t n, uint64_t seed, uint64_t offset, void* stream);
 
+/*
+ * Multi-GPU: one rank's part of the M-row-slab sharded GEMM C[M,N] = A[M,K].B[K,N] over NCCL
+ * (the reference is single-GPU and has no counterpart).  The rank's slab
+ * is rows [row0, row0 + rows) of b2g_slab_rows(M, world, rank); A_slab (rows x K, lda) and
+ * C_slab (rows x N, ldc) hold those rows; B is a K x N buffer (ldb) on every rank that holds
+ * B on `root`.  The call broadcasts B from root in `k_panels` row panels on an internal
+ * stream and runs the slab GEMM panel by panel as the panels arrive (panel 0 overwrites
+ * C_slab, later panels add into it), all ordered after prior work on `stream`; C is written
+ * locally with no reduction.  `comm` is an ncclComm_t (b2g_comm_init or the caller's own);
+ * every rank of the communicator must make the call with the same M, N, K, root, k_panels.
+ * NCCL is loaded at run time (libnccl.so.2) only by these entry points.
+ */
+int b2g_gemm_sharded(const void* A_slab, void* B, float* C_slab, int64_t M, int64_t N, int64_t K,
+                     int64_t lda, int64_t ldb, int64_t ldc, void* comm, int root, int k_panels,
+                     void* stream);
+
+/* Balanced contiguous row partition: rank r gets M/world rows, the first M%world ranks one more. */
+int b2g_slab_rows(int64_t M, int world, int rank, int64_t* row0, int64_t* rows);
+
+/* NCCL communicator helpers for callers without their own NCCL: a 128-byte unique id made on
+ * one rank and shared with the others out of band, then one b2g_comm_init per rank (with that
+ * rank's device current). */
+int b2g_comm_unique_id(void* id_out);
+int b2g_comm_init(void** comm, int world, int rank, const void* id);
+int b2g_comm_destroy(void* comm);
+
 /* Message for the calling thread's last failed call ("" if none). */
 const char* b2g_last_error_string(void);
 

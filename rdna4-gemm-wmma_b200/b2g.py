@@ -75,6 +75,18 @@ def load(path=None):
     L.b2g_tile_coord.restype = None
     L.b2g_tile_coord.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int)] * 2
     L.b2g_version.restype = ctypes.c_char_p
+    L.b2g_gemm_sharded.restype = ctypes.c_int
+    L.b2g_gemm_sharded.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp, ctypes.c_int,
+                                   ctypes.c_int, vp]
+    L.b2g_slab_rows.restype = ctypes.c_int
+    L.b2g_slab_rows.argtypes = [i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64),
+                                ctypes.POINTER(ctypes.c_int64)]
+    L.b2g_comm_unique_id.restype = ctypes.c_int
+    L.b2g_comm_unique_id.argtypes = [vp]
+    L.b2g_comm_init.restype = ctypes.c_int
+    L.b2g_comm_init.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int, vp]
+    L.b2g_comm_destroy.restype = ctypes.c_int
+    L.b2g_comm_destroy.argtypes = [vp]
     if path is None:
         _lib = L
     return L
@@ -185,6 +197,40 @@ def tile_coord(t, num_m, num_n, group):
     tm, tn = ctypes.c_int(), ctypes.c_int()
     load().b2g_tile_coord(t, num_m, num_n, group, ctypes.byref(tm), ctypes.byref(tn))
     return tm.value, tn.value
+
+
+def slab_rows(M, world, rank):
+    """(row0, rows) of rank's M-row slab (balanced contiguous partition)."""
+    r0, n = ctypes.c_int64(), ctypes.c_int64()
+    _check(load().b2g_slab_rows(M, world, rank, ctypes.byref(r0), ctypes.byref(n)))
+    return r0.value, n.value
+
+
+def comm_unique_id():
+    """128-byte NCCL unique id (bytes) for b2g_comm_init."""
+    buf = ctypes.create_string_buffer(128)
+    _check(load().b2g_comm_unique_id(buf))
+    return buf.raw
+
+
+def comm_init(world, rank, uid):
+    comm = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(bytes(uid), 128)
+    _check(load().b2g_comm_init(ctypes.byref(comm), world, rank, buf))
+    return comm.value
+
+
+def comm_destroy(comm):
+    _check(load().b2g_comm_destroy(comm))
+
+
+def gemm_sharded(A_slab, B, C_slab, M, N, K, comm, root=0, k_panels=4, lda=None, ldb=None,
+                 ldc=None, stream=None):
+    """This rank's part of the M-row-slab sharded GEMM; B is broadcast from root in K panels."""
+    _check(load().b2g_gemm_sharded(_ptr(A_slab), _ptr(B), _ptr(C_slab), M, N, K,
+                                   K if lda is None else lda, N if ldb is None else ldb,
+                                   N if ldc is None else ldc, comm, root, k_panels,
+                                   _stream(stream)))
 
 
 def version():

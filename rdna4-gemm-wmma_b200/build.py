@@ -15,14 +15,15 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libb2g_gemm.so")
-SOURCES = ["b2g_api.cu"]
-HEADERS = ["ptx.cuh", "gemm_sm100.cuh", "sched.h"]
+SOURCES = ["b2g_api.cu", "b2g_shard.cu"]
+HEADERS = ["ptx.cuh", "gemm_sm100.cuh", "sched.h", "errors.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC", "-shared",
     "-Xptxas", "-v",
+    "-ldl",
 ]
 
 

@@ -20,6 +20,7 @@
 #include <string>
 
 #include "../../include/b2g_gemm.h"
+#include "errors.h"
 #include "gemm_sm100.cuh"
 
 namespace b2g {
@@ -37,6 +38,8 @@ static int fail(int code, const char* fmt, ...) {
   t_err = buf;
   return code;
 }
+
+void set_error(const char* msg) { t_err = msg; }
 
 static int cuda_fail(cudaError_t e, const char* what) {
   return fail(B2G_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));

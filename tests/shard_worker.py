@@ -1,0 +1,138 @@
+"""Rank bodies for the multi-process sharding tests (imported by spawned children)."""
+import datetime
+import os
+import sys
+import traceback
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def _load_pkg(name):
+    import importlib.util
+    path = os.path.join(ROOT, "rdna4-gemm-wmma_b200", name + ".py")
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _init_gloo(rank, world, port, timeout_s):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+    return dist
+
+
+def gloo_pipeline_rank(rank, world, port, M, N, K, panels, out_q):
+    """Run shard.sharded_gemm on CPU tensors with an FP64 numpy stand-in for the per-panel GEMM
+    and report (rank, max error of the slab against the oracle)."""
+    try:
+        import torch
+        from oracle import orc
+        shard = _load_pkg("shard")
+        dist = _init_gloo(rank, world, port, 60)
+        row0, rows = shard.slab_rows(M, world, rank)
+        A = orc.uniform_f16((M, K), 1)
+        A_slab = torch.from_numpy(A[row0:row0 + rows].view(np.int16).copy()).view(torch.float16)
+        if rank == 0:
+            B = torch.from_numpy(orc.uniform_f16((K, N), 2).view(np.int16).copy()).view(torch.float16)
+        else:
+            B = torch.full((K, N), float("nan"), dtype=torch.float16)
+        C_slab = torch.full((max(rows, 1), N), float("nan"), dtype=torch.float64)
+
+        def cpu_gemm(A_view, B_view, C, r, n, k, beta, lda, ldb, ldc):
+            prod = A_view[:r, :k].double() @ B_view[:k, :n].double()
+            C[:r, :n] = prod if beta == 0.0 else C[:r, :n] + prod
+
+        got = shard.sharded_gemm(A_slab, B, C_slab, M, N, K, panels=panels, gemm=cpu_gemm)
+        assert got == (row0, rows)
+        ref = orc.gemm_f64(A, orc.uniform_f16((K, N), 2), rows=(row0, row0 + rows))
+        err = float(np.abs(C_slab[:rows].numpy() - ref).max()) if rows else 0.0
+        dist.barrier()
+        dist.destroy_process_group()
+        out_q.put((rank, rows, err, None))
+    except Exception:
+        out_q.put((rank, -1, -1.0, traceback.format_exc()))
+
+
+def gloo_dead_rank(rank, world, port, out_q):
+    """Rank 1 leaves before the first collective; rank 0's broadcast must end with an error
+    (the process-group timeout), not hang."""
+    try:
+        import torch
+        shard = _load_pkg("shard")
+        dist = _init_gloo(rank, world, port, 3)
+        if rank == 1:
+            out_q.put((rank, "left", None))
+            out_q.close()
+            out_q.join_thread()
+            os._exit(0)
+        B = torch.zeros((128, 64), dtype=torch.float16)
+        A = torch.zeros((64, 128), dtype=torch.float16)
+        C = torch.zeros((64, 64), dtype=torch.float64)
+        try:
+            shard.sharded_gemm(A, B, C, 128, 64, 128, panels=2,
+                               gemm=lambda *a: None)
+            out_q.put((rank, "no error", None))
+        except Exception as e:  # the collective reports the missing peer
+            out_q.put((rank, "error", type(e).__name__))
+        out_q.close()
+        out_q.join_thread()
+        os._exit(0)
+    except Exception:
+        out_q.put((rank, "crash", traceback.format_exc()))
+
+
+def nccl_sharded_rank(rank, world, uid_path, M, N, K, panels, out_q):
+    """b2g_gemm_sharded on `world` GPUs (one process each); rank 0 publishes the NCCL id."""
+    try:
+        import time
+        import torch
+        from oracle import orc
+        b2g = _load_pkg("b2g")
+        torch.cuda.set_device(rank)
+        if rank == 0:
+            uid = b2g.comm_unique_id()
+            with open(uid_path + ".tmp", "wb") as f:
+                f.write(uid)
+            os.replace(uid_path + ".tmp", uid_path)
+        else:
+            t0 = time.time()
+            while not os.path.exists(uid_path):
+                if time.time() - t0 > 60:
+                    raise RuntimeError("no NCCL id from rank 0")
+                time.sleep(0.05)
+            uid = open(uid_path, "rb").read()
+        comm = b2g.comm_init(world, rank, uid)
+        row0, rows = b2g.slab_rows(M, world, rank)
+        dA = torch.empty((max(rows, 1), K), dtype=torch.float16, device="cuda")
+        b2g.fill_uniform(dA, rows * K, 1, row0 * K)
+        dB = torch.full((K, N), float("nan"), dtype=torch.float16, device="cuda")
+        if rank == 0:
+            b2g.fill_uniform(dB, K * N, 2)
+        dC = torch.full((max(rows, 1), N), float("nan"), dtype=torch.float32, device="cuda")
+        b2g.gemm_sharded(dA, dB, dC, M, N, K, comm, root=0, k_panels=panels)
+        torch.cuda.synchronize()
+        status = b2g.device_status()
+        # check a sample of this rank's rows against the oracle
+        B = orc.uniform_f16((K, N), 2)
+        sample = sorted(set([0, rows - 1] + list(range(0, rows, max(1, rows // 7))))) if rows else []
+        worst = 0
+        for r in sample:
+            a = orc.uniform_f16((1, K), 1, (row0 + r) * K)
+            ref = orc.gemm_f64(a, B)
+            bad = orc.check(dC[r:r + 1].cpu().numpy(), ref, K, 1.0, 1.0)[0]
+            worst = max(worst, bad)
+        b_ok = bool(torch.equal(dB.cpu().view(torch.int16),
+                                torch.from_numpy(B.view(np.int16))))
+        b2g.comm_destroy(comm)
+        out_q.put((rank, rows, worst, status, b_ok, None))
+    except Exception:
+        out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))

@@ -95,3 +95,43 @@ def test_reference_strip_remap_is_not_a_bijection_where_ours_is(b2g):
     assert len(ref) < gx * gy
     ours = {b2g.tile_coord(t, gy, gx, 8) for t in range(gx * gy)}
     assert len(ours) == gx * gy
+
+
+def test_cpp_header_compiles_links_and_validates(b2g, tmp_path):
+    """The C++ drop-in surface (include/b2g_gemm.hpp) builds against libb2g_gemm.so; the
+    program calls only entry points that need no GPU (argument validation, partition, tile
+    order) and maps a failing status to b2g::Error."""
+    import os
+    import shutil
+    import subprocess
+    from conftest import ROOT
+    cxx = shutil.which("g++")
+    if not cxx:
+        pytest.skip("no g++")
+    src = tmp_path / "dropin.cpp"
+    src.write_text(r'''
+#include <cstdio>
+#include "b2g_gemm.hpp"
+int main() {
+  // the reference's GEMM(A, B, C, M, N, K) with a bad size: a status code, not an exit
+  int rc = b2g::GEMM(nullptr, nullptr, nullptr, -1, 8, 8);
+  if (rc != B2G_ERR_INVALID_ARG) return 1;
+  try { b2g::check(rc); return 2; } catch (const b2g::Error& e) { if (e.code() != rc) return 3; }
+  if (b2g::GEMM(nullptr, nullptr, nullptr, 0, 8, 8) != B2G_OK) return 4;   // empty problem
+  int64_t r0, n;
+  if (b2g_slab_rows(32768, 8, 3, &r0, &n) != B2G_OK || r0 != 12288 || n != 4096) return 5;
+  int tm, tn;
+  b2g_tile_coord(5, 3, 4, 2, &tm, &tn);
+  std::printf("%s %d %d\n", b2g_version(), tm, tn);
+  return 0;
+}
+''')
+    exe = tmp_path / "dropin"
+    libdir = os.path.join(ROOT, "rdna4-gemm-wmma_b200")
+    res = subprocess.run([cxx, "-std=c++17", str(src), "-I", os.path.join(ROOT, "include"),
+                          "-L", libdir, "-lb2g_gemm", "-Wl,-rpath," + libdir, "-o", str(exe)],
+                         capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, (run.returncode, run.stdout, run.stderr)
+    assert "sm_100a" in run.stdout

@@ -1,0 +1,66 @@
+"""GPU tests of b2g_gemm_sharded (M-row slabs, B broadcast from rank 0 in K panels over NCCL,
+panel GEMMs accumulating into the local C slab) against the oracle.
+
+* one rank on one GPU (a one-rank NCCL communicator): the whole pipeline -- communicator,
+  panel broadcasts on the internal stream, event ordering, panel accumulation -- runs;
+* two ranks on two GPUs (skipped with fewer): each rank's slab rows checked, and B on the
+  non-root rank (filled with NaN before the call) must equal the root's bit for bit.
+Tolerance: |C - R| <= 1e-3*sqrt(K)*max|a|*max|b| + 1e-3*|R| against the FP64 oracle.
+"""
+import multiprocessing as mp
+import os
+import sys
+import tempfile
+
+import numpy as np
+import pytest
+
+from gpu_util import assert_close
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+import shard_worker  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,N,K,panels", [(1024, 1536, 2048, 4), (640, 512, 200, 3)])
+def test_sharded_single_rank(b2g, cuda, orc, M, N, K, panels):
+    torch = cuda
+    uid = b2g.comm_unique_id()
+    comm = b2g.comm_init(1, 0, uid)
+    try:
+        dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+        dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+        b2g.fill_uniform(dA, M * K, 1)
+        b2g.fill_uniform(dB, K * N, 2)
+        dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+        b2g.gemm_sharded(dA, dB, dC, M, N, K, comm, root=0, k_panels=panels)
+        torch.cuda.synchronize()
+        assert b2g.device_status() == 0
+        A = orc.uniform_f16((M, K), 1)
+        B = orc.uniform_f16((K, N), 2)
+        assert_close(orc, dC.cpu().numpy(), orc.gemm_f64(A, B), K)
+        assert np.array_equal(dB.cpu().numpy().view(np.uint16), B.view(np.uint16))
+    finally:
+        b2g.comm_destroy(comm)
+
+
+def test_sharded_two_ranks(b2g, cuda):
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        uid_path = os.path.join(d, "nccl_id")
+        M, N, K = 4096, 2048, 4096
+        procs = [ctx.Process(target=shard_worker.nccl_sharded_rank,
+                             args=(r, 2, uid_path, M, N, K, 4, q)) for r in range(2)]
+        for p in procs:
+            p.start()
+        res = sorted(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=120)
+    for rank, rows, worst, status, b_ok, tb in res:
+        assert tb is None, tb
+        assert status == 0 and worst == 0 and b_ok, (rank, rows, worst, status, b_ok)
+    assert sum(r[1] for r in res) == M
