@@ -52,6 +52,7 @@ static std::atomic<int64_t> opt_force_generic{0};
 static std::atomic<int64_t> opt_fault_flags{0};
 static std::atomic<int64_t> opt_tile_n{0};  // 0 = choose by shape, else 256 or 512
 static std::atomic<int64_t> opt_store_hint{0};
+static std::atomic<int64_t> opt_split_k{0};  // 0 = choose by shape, else the split count
 
 // ------------------------------------------------------------------ driver entry point
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -484,11 +485,36 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
       ds->attr_set[variant][bk][cm] = true;
     }
   }
-  int groups;
-  if (cg == 1)
-    groups = std::min(ds->sm_count, p.num_tiles);
-  else
-    groups = std::min(ds->max_clusters[variant][bk][cm], p.num_tiles);
+  const int group_cap = cg == 1 ? ds->sm_count : ds->max_clusters[variant][bk][cm];
+  // ---- split-K: when the tiles cannot fill the GPU, split K so that every CTA group has a
+  // unit; each split keeps at least 8 K blocks.
+  int splits = (int)opt_split_k.load();
+  if (splits <= 0) {
+    splits = 1;
+    if (2 * p.num_tiles <= group_cap && p.k_iters >= 16)
+      splits = std::min({group_cap / std::max(1, p.num_tiles), p.k_iters / 8, 16});
+  }
+  splits = std::max(1, std::min(splits, p.k_iters));
+  p.k_per_split = (p.k_iters + splits - 1) / splits;
+  p.k_splits = (p.k_iters + p.k_per_split - 1) / p.k_per_split;  // no empty split
+  p.num_units = p.num_tiles * p.k_splits;
+  p.ws = nullptr;
+  p.counters = nullptr;
+  void* scratch = nullptr;
+  if (p.k_splits > 1) {
+    const size_t ws_bytes = (size_t)p.num_units * cg * 128 * bn * sizeof(float);
+    const size_t ctr_bytes = ((size_t)p.num_tiles * cg * sizeof(int) + 255) / 256 * 256;
+    cudaError_t e = cudaMallocAsync(&scratch, ctr_bytes + ws_bytes, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(split-K workspace)");
+    p.counters = static_cast<int*>(scratch);
+    p.ws = reinterpret_cast<float*>(static_cast<char*>(scratch) + ctr_bytes);
+    e = cudaMemsetAsync(p.counters, 0, ctr_bytes, stream);
+    if (e != cudaSuccess) {
+      cudaFreeAsync(scratch, stream);
+      return cuda_fail(e, "cudaMemsetAsync(split-K counters)");
+    }
+  }
+  int groups = std::min(group_cap, p.num_units);
   if (groups < 1) groups = 1;
 
   cudaLaunchConfig_t cfg = {};
@@ -506,6 +532,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     cfg.numAttrs = 1;
   }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
+  if (scratch) cudaFreeAsync(scratch, stream);  // stream-ordered: freed after the kernel
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 kernel launch");
   t_path = cg == 1 ? B2G_PATH_TC_1CTA : B2G_PATH_TC_2CTA;
   return B2G_OK;
@@ -623,6 +650,9 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_force_generic = value ? 1 : 0;
   } else if (!strcmp(key, "fault_flags")) {
     opt_fault_flags = value;
+  } else if (!strcmp(key, "split_k")) {
+    if (value < 0 || value > 64) return B2G_ERR_INVALID_ARG;
+    opt_split_k = value;
   } else if (!strcmp(key, "store_hint")) {
     opt_store_hint = value ? 1 : 0;
   } else if (!strcmp(key, "tile_n")) {
@@ -643,6 +673,7 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "fault_flags")) return opt_fault_flags;
   if (!strcmp(key, "tile_n")) return opt_tile_n;
   if (!strcmp(key, "store_hint")) return opt_store_hint;
+  if (!strcmp(key, "split_k")) return opt_split_k;
   return -1;
 }
 

@@ -61,6 +61,15 @@ struct GemmParams {
   int store_hint;              // 1 = C stores carry an L2 evict-first hint
   int accumulate;              // 1 = C += alpha*A.B (TMA reduce-add), 0 = C = alpha*A.B
   float alpha;                 // scale of A.B
+  // split-K: work unit u = tile * k_splits + split; split s covers K blocks
+  // [s*k_per_split, min(k_iters, (s+1)*k_per_split)).  With k_splits > 1 every unit writes its
+  // fp32 partial tile to `ws` and bumps counters[tile*CG + cta]; the unit that arrives last
+  // sums the partials in split order (deterministic) and stores C, then resets the counter.
+  int k_splits;
+  int k_per_split;
+  int num_units;               // num_tiles * k_splits
+  float* ws;                   // num_units * CG * 128 * BN floats (k_splits > 1)
+  int* counters;               // num_tiles * CG ints, zero between calls
   unsigned long long timeout_ns;
   int fault_flags;             // test-only: bit 0 = producer issues no loads (forces a timeout)
 };
@@ -206,14 +215,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int t = group_id; t < p.num_tiles && ok; t += num_groups) {
+      for (int u = group_id; u < p.num_units && ok; u += num_groups) {
+        const int t = u / p.k_splits;
+        const int kb_lo = (u - t * p.k_splits) * p.k_per_split;
+        const int kb_hi = min(p.k_iters, kb_lo + p.k_per_split);
         int pm, tn;
         b2g_sched_tile(t, p.num_pm_tiles, p.num_n_tiles, p.raster_group, &pm, &tn);
         const int mt = pm * CG + (int)cta_rank;
         int i0, b0, a0;
         m_tile_origin(p, mt, i0, b0, a0);
         const int n0 = tn * BN;
-        for (int kb = 0; kb < p.k_iters; ++kb, ++it) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
           if (!ptx::mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, err, ERR_WAIT_EMPTY, lim)) {
@@ -266,7 +278,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       };
-      for (int t = group_id; t < p.num_tiles && ok; t += num_groups, ++tc) {
+      for (int u = group_id; u < p.num_units && ok; u += num_groups, ++tc) {
+        const int t = u / p.k_splits;
+        const int kb_lo = (u - t * p.k_splits) * p.k_per_split;
+        const int nkb = min(p.k_iters, kb_lo + p.k_per_split) - kb_lo;
         // BN = 256: two accumulators, tempty[acc] guards accumulator acc.
         // BN = 512: one accumulator, tempty[h] guards its N-half h (the epilogue frees the
         // halves one after the other).
@@ -278,11 +293,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)acc * kUN;
-        int kb = 0;
+        int kb = 0;  // K block of this unit, relative to kb_lo
         if constexpr (C::NH == 2) {
           // Half 0 of every K block already in shared memory first, then wait for half 1 of
           // the accumulator (still being read by the epilogue) and complete those blocks.
-          const int pro = p.k_iters < C::STAGES ? p.k_iters : C::STAGES;
+          const int pro = nkb < C::STAGES ? nkb : C::STAGES;
           for (; kb < pro; ++kb) {
             const int s = (it + kb) % C::STAGES;
             const uint32_t ph = (uint32_t)((it + kb) / C::STAGES) & 1u;
@@ -306,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           it += pro;
         }
-        for (; kb < p.k_iters; ++kb, ++it) {
+        for (; kb < nkb; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
           if (!ptx::mbar_wait(full_bar(s), ph, abort_flag, err, ERR_WAIT_FULL, lim)) {
@@ -334,7 +349,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int b_l = (r0 / p.bi) % p.bb;
     const int i_l = r0 % p.bi;
     int tc = 0, nstore = 0;
-    for (int t = group_id; t < p.num_tiles; t += num_groups, ++tc) {
+    for (int u = group_id; u < p.num_units; u += num_groups, ++tc) {
+      const int t = u / p.k_splits;
       int pm, tn;
       b2g_sched_tile(t, p.num_pm_tiles, p.num_n_tiles, p.raster_group, &pm, &tn);
       const int mt = pm * CG + (int)cta_rank;
@@ -390,6 +406,84 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++nstore;
       };
 
+      // Hand accumulator (or N-half) `rel` back to the MMA warp.
+      auto release = [&](int rel) {
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 1)
+            ptx::mbar_arrive(tempty_bar(rel));
+          else
+            ptx::mbar_arrive_cluster(tempty_bar(rel), 0);
+        }
+      };
+
+      if (p.k_splits > 1) {
+        // ---- split-K unit: partial tile -> workspace; the last unit of the tile reduces.
+        // Workspace block of (unit, CTA): 128 x BN floats laid out [chunk][row][32] so each
+        // warp writes and reads 4 KiB contiguous per chunk.
+        const size_t blk = (size_t)128 * BN;
+        float* mine = p.ws + ((size_t)u * CG + cta_rank) * blk + (size_t)(32 * q + lane) * 32;
+#pragma unroll 1
+        for (int ch = 0; ch < C::CHUNKS; ++ch) {
+          uint32_t v[32];
+          ptx::tmem_ld_32x32b_x32(tbase + 32u * ch, v);
+          ptx::tmem_ld_wait();
+          float4* dst = reinterpret_cast<float4*>(mine + (size_t)ch * 128 * 32);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                 __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+        }
+        if constexpr (C::ACC_BUFS == 2) {
+          release(acc);
+        } else {
+          release(0);
+          release(1);
+        }
+        __threadfence();
+        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
+        if (threadIdx.x == 64) {
+          int* ctr = p.counters + (size_t)t * CG + cta_rank;
+          const int old = atomicAdd(ctr, 1);
+          const int last = old == p.k_splits - 1;
+          if (last) *ctr = 0;  // every split has arrived: ready for the next call
+          *last_flag = last;
+        }
+        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        if (*last_flag) {
+          __threadfence();
+          const float* base_t = p.ws + ((size_t)t * p.k_splits * CG + cta_rank) * blk +
+                                (size_t)(32 * q + lane) * 32;
+#pragma unroll 1
+          for (int ch = 0; ch < C::CHUNKS; ++ch) {
+            float a[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] = 0.0f;
+            for (int sp = 0; sp < p.k_splits; ++sp) {  // fixed order: deterministic sums
+              const float4* src = reinterpret_cast<const float4*>(
+                  base_t + (size_t)sp * CG * blk + (size_t)ch * 128 * 32);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 x = __ldcg(src + j);
+                a[4 * j] += x.x;
+                a[4 * j + 1] += x.y;
+                a[4 * j + 2] += x.z;
+                a[4 * j + 3] += x.w;
+              }
+            }
+            uint32_t v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(a[j]);
+            store_chunk(v, ch);
+          }
+        }
+        // the next unit's partial writes reuse no buffer of this one; nothing more to order
+        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        continue;
+      }
+
       // TMEM loads are software-pipelined: chunk ch+1 is in flight while chunk ch is stored.
       uint32_t v0[32], v1[32];
       ptx::tmem_ld_32x32b_x32(tbase, v0);
@@ -402,15 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((ch + 1) % 8 == 7) {
           // An N-half (BN = 512) or the whole accumulator (BN = 256) has been read: hand it
           // back to the MMA warp.
-          const int rel = C::ACC_BUFS == 2 ? acc : (ch + 1) / 8;
-          ptx::tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if constexpr (CG == 1)
-              ptx::mbar_arrive(tempty_bar(rel));
-            else
-              ptx::mbar_arrive_cluster(tempty_bar(rel), 0);
-          }
+          release(C::ACC_BUFS == 2 ? acc : (ch + 1) / 8);
         }
         if (ch + 2 < C::CHUNKS) ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 2), v0);
         store_chunk(v1, ch + 1);

@@ -119,6 +119,11 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
   }
 }
 
+// Named barrier `id` over `count` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // ---------------------------------------------------------------- cluster barrier
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::

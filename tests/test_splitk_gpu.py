@@ -1,0 +1,94 @@
+"""GPU tests of split-K (K split over several work units whose fp32 partial tiles are summed
+in split order by the last unit of each tile) against the oracle.
+
+Tolerance: |C - R| <= 1e-3*sqrt(K)*max|a|*max|b|*|alpha| + 1e-3*|R| against FP64.  Split-K is
+deterministic: the partials of a tile are always summed in split order, so repeated calls give
+identical bits (this also shows the per-tile counters are reset for the next call).
+"""
+import numpy as np
+import pytest
+
+from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, to_dev
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("splits", [2, 3, 5])
+def test_split_k_forced(b2g, cuda, orc, cg, tn, splits):
+    torch = cuda
+    M, N, K = 384, 1024, 2048 + 192  # K blocks not divisible by the split count
+    A = orc.uniform_f16((M, K), 61)
+    B = orc.uniform_f16((K, N), 62)
+    dA, dB = to_dev(torch, A), to_dev(torch, B)
+    dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    with options(b2g, cta_group=cg, tile_n=tn, split_k=splits):
+        b2g.gemm(dA, dB, dC, M, N, K)
+        torch.cuda.synchronize()
+        assert b2g.device_status() == 0
+        first = dC.clone()
+        b2g.gemm(dA, dB, dC, M, N, K)
+        torch.cuda.synchronize()
+    assert torch.equal(first, dC)
+    assert_close(orc, dC.cpu().numpy(), orc.gemm_f64(A, B), K, what="split %d" % splits)
+
+
+def test_split_k_alpha_beta_and_ragged(b2g, cuda, orc):
+    torch = cuda
+    M, N, K = 200, 300, 1000
+    r8 = lambda x: (x + 7) // 8 * 8
+    A = orc.uniform_f16((M, K), 63)
+    B = orc.uniform_f16((K, N), 64)
+    C0 = orc.uniform_f16((M, N), 65).astype(np.float32)
+    Ap = np.zeros((M, r8(K)), np.float16)
+    Ap[:, :K] = A
+    Bp = np.zeros((K, r8(N)), np.float16)
+    Bp[:, :N] = B
+    Cp = np.zeros((M, r8(N)), np.float32)
+    Cp[:, :N] = C0
+    dC = to_dev(torch, Cp)
+    with options(b2g, split_k=4):
+        b2g.gemm_ex(to_dev(torch, Ap), to_dev(torch, Bp), dC, M, N, K, 2.0, 1.0, lda=r8(K),
+                    ldb=r8(N), ldc=r8(N))
+    torch.cuda.synchronize()
+    assert b2g.last_path() in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
+    ref = 2.0 * orc.gemm_f64(A, B) + C0.astype(np.float64)
+    assert_close(orc, dC.cpu().numpy()[:, :N], ref, K, 2.0, 1.0)
+
+
+def test_split_k_reference_contraction(b2g, cuda, orc):
+    """Split-K through the M-contiguous store of the reference's contraction layout."""
+    torch = cuda
+    mt, rt, nt, rt_l, bt = 4, 32, 16, 128, 256
+    G = orc.uniform_f16((rt * nt * mt * rt_l,), 66)
+    In = orc.uniform_f16((bt * nt * rt_l,), 67)
+    a_shape, a_st = (mt, 1, rt, nt, rt_l), (rt_l, 0, nt * mt * rt_l, mt * rt_l, 1)
+    b_shape, b_st = (nt, rt_l, bt), (rt_l, 1, nt * rt_l)
+    c_shape, c_st = (mt, 1, rt, bt), (bt * rt, 0, 1, rt)
+    dOut = torch.full((mt * bt * rt,), float("nan"), dtype=torch.float32, device="cuda")
+    with options(b2g, split_k=3):
+        b2g.contract5d(to_dev(torch, G), a_shape, a_st, to_dev(torch, In), b_shape, b_st, dOut,
+                       c_shape, c_st)
+    torch.cuda.synchronize()
+    ref = orc.contract5d_f64(G, a_shape, a_st, In, b_shape, b_st, c_shape, c_st,
+                             c_size=mt * bt * rt)
+    assert_close(orc, dOut.cpu().numpy(), ref, nt * rt_l)
+
+
+def test_split_k_auto_skinny(b2g, cuda, orc):
+    """BASELINE configs[3]'s HBM-bound shape 128 x 8192 x 8192 takes split-K by default;
+    checked on a sample of rows."""
+    torch = cuda
+    M, N, K = 128, 8192, 8192
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+    dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+    dC = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    b2g.fill_uniform(dA, M * K, 1)
+    b2g.fill_uniform(dB, K * N, 2)
+    b2g.gemm(dA, dB, dC, M, N, K)
+    torch.cuda.synchronize()
+    assert b2g.device_status() == 0
+    B = orc.uniform_f16((K, N), 2)
+    for r in (0, 1, 63, 64, 127):
+        a = orc.uniform_f16((1, K), 1, r * K)
+        assert_close(orc, dC[r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, what="row %d" % r)
