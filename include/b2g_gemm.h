@@ -72,6 +72,24 @@ int b2g_gemm_ex(const void* A, const void* B, float* C, int64_t M, int64_t N, in
                 int64_t lda, int64_t ldb, int64_t ldc, float alpha, float beta, void* stream);
 
 /*
+ * b2g_gemm_f16_f32 for callers that can't call cudaMalloc: this entry point allocates
+ * nothing.  (No counterpart in the reference, which allocates everything up front in main.)
+ * Some callers can't allocate device memory per call -- a host runtime that has handed all
+ * device memory to its own pool allocator, or a serving loop that must not allocate on every
+ * call.  When the problem has too few output tiles to fill the GPU the library splits K and
+ * needs a workspace for the partial tiles; here it comes from a 32 MiB array compiled into
+ * the library (every GPU that loads the library holds it until the process exits), not from
+ * cudaMallocAsync.  A request whose split-K workspace would exceed 32 MiB returns
+ * B2G_ERR_INVALID_ARG with a message saying so.  The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress) for that device; make that first call before
+ * any stream capture.  All calls share the one array, and it keeps the last call's contents
+ * (each call clears the split counters it relies on): calls that overlap on the GPU -- on
+ * different streams, or from different host threads -- race on it and must be serialized.
+ */
+int b2g_gemm_f16_f32_noalloc(const void* A, const void* B, float* C, int64_t M, int64_t N,
+                             int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+
+/*
  * The reference's drop-in form: contiguous row-major operands, lda = K, ldb = N, ldc = N,
  * default stream.  Same as GEMM_Naive's contract (mmm.cpp:52-62).
  */

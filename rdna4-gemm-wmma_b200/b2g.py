@@ -59,6 +59,8 @@ def load(path=None):
                                     ctypes.c_float, ctypes.c_float, vp]
     L.b2g_gemm.restype = ctypes.c_int
     L.b2g_gemm.argtypes = [vp, vp, vp, i64, i64, i64]
+    L.b2g_gemm_f16_f32_noalloc.restype = ctypes.c_int
+    L.b2g_gemm_f16_f32_noalloc.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
     L.b2g_contract5d_f16_f32.restype = ctypes.c_int
     L.b2g_contract5d_f16_f32.argtypes = [vp, i64p, i64p, vp, i64p, i64p, vp, i64p, i64p, vp]
     L.b2g_fill_uniform_f16.restype = ctypes.c_int

@@ -161,6 +161,39 @@ __global__ void fill_uniform_kernel(__half* __restrict__ dst, int64_t n, uint64_
   }
 }
 
+// ------------------------------------------------------------------ fixed scratch
+// Split-K scratch for b2g_gemm_f16_f32_noalloc: a file-scope device array, so that entry point
+// never allocates.  Each device that loads the library holds it until the process exits.
+// Host code must not use `g_noalloc_scratch` as an address (on the host it is only a stand-in
+// symbol); its device address comes from cudaGetSymbolAddress, once per device.
+constexpr size_t kNoAllocScratchBytes = (size_t)32 << 20;  // 32 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct FixedScratch {
+  void* ptr;
+  size_t bytes;
+};
+
+// Device address of g_noalloc_scratch on the current device (set-up on the first call).
+static int noalloc_scratch(FixedScratch* out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(B2G_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    addr[dev] = p;
+  }
+  out->ptr = addr[dev];
+  out->bytes = kNoAllocScratchBytes;
+  return B2G_OK;
+}
+
 // ------------------------------------------------------------------ planning
 struct Mode {
   int64_t size, sa, sc;  // extent, stride in the first operand, stride in the second
@@ -197,7 +230,8 @@ static inline bool al16(int64_t bytes) { return (bytes & 15) == 0; }
 // ------------------------------------------------------------------ core dispatch
 static int run(const void* A, const int64_t as[5], const int64_t ast[5], const void* B,
                const int64_t bs[3], const int64_t bst[3], float* Cp, const int64_t cs[4],
-               const int64_t cst[4], float alpha, float beta, cudaStream_t stream) {
+               const int64_t cst[4], float alpha, float beta, cudaStream_t stream,
+               const FixedScratch* fixed = nullptr) {
   // ---- validation
   for (int t = 0; t < 5; ++t)
     if (as[t] < 0) return fail(B2G_ERR_INVALID_ARG, "negative A extent");
@@ -501,7 +535,20 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.ws = nullptr;
   p.counters = nullptr;
   void* scratch = nullptr;
-  if (p.k_splits > 1) {
+  if (p.k_splits > 1 && fixed) {
+    // caller-supplied scratch (b2g_gemm_f16_f32_noalloc): no allocation
+    const size_t ws_bytes = (size_t)p.num_units * cg * 128 * bn * sizeof(float);
+    const size_t ctr_bytes = ((size_t)p.num_tiles * cg * sizeof(int) + 255) / 256 * 256;
+    if (ctr_bytes + ws_bytes > fixed->bytes)
+      return fail(B2G_ERR_INVALID_ARG,
+                  "split-K scratch of %zu bytes exceeds the %zu-byte static scratch of "
+                  "b2g_gemm_f16_f32_noalloc",
+                  ctr_bytes + ws_bytes, fixed->bytes);
+    p.counters = static_cast<int*>(fixed->ptr);
+    p.ws = reinterpret_cast<float*>(static_cast<char*>(fixed->ptr) + ctr_bytes);
+    cudaError_t e = cudaMemsetAsync(p.counters, 0, ctr_bytes, stream);  // counters start at 0
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split-K counters)");
+  } else if (p.k_splits > 1) {
     const size_t ws_bytes = (size_t)p.num_units * cg * 128 * bn * sizeof(float);
     const size_t ctr_bytes = ((size_t)p.num_tiles * cg * sizeof(int) + 255) / 256 * 256;
     cudaError_t e = cudaMallocAsync(&scratch, ctr_bytes + ws_bytes, stream);
@@ -559,6 +606,23 @@ extern "C" int b2g_gemm_ex(const void* A, const void* B, float* C, int64_t M, in
 extern "C" int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t M, int64_t N,
                                 int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
   return b2g_gemm_ex(A, B, C, M, N, K, lda, ldb, ldc, 1.0f, 0.0f, stream);
+}
+
+extern "C" int b2g_gemm_f16_f32_noalloc(const void* A, const void* B, float* C, int64_t M,
+                                        int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                                        int64_t ldc, void* stream) {
+  t_err.clear();
+  if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
+  if (lda < std::max<int64_t>(K, 1) || ldb < std::max<int64_t>(N, 1) || ldc < std::max<int64_t>(N, 1))
+    return fail(B2G_ERR_INVALID_ARG, "leading dimension smaller than the row length");
+  FixedScratch fs;
+  int rc = noalloc_scratch(&fs);
+  if (rc != B2G_OK) return rc;
+  const int64_t as[5] = {1, 1, M, 1, K}, ast[5] = {0, 0, lda, 0, 1};
+  const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
+  const int64_t cs[4] = {1, 1, M, N}, cst[4] = {0, 0, ldc, 1};
+  return run(A, as, ast, B, bs, bst, C, cs, cst, 1.0f, 0.0f, static_cast<cudaStream_t>(stream),
+             &fs);
 }
 
 extern "C" int b2g_gemm(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K) {
