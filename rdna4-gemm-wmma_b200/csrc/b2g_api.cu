@@ -18,6 +18,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 
 #include "../../include/b2g_gemm.h"
 #include "errors.h"
@@ -53,6 +54,8 @@ static std::atomic<int64_t> opt_fault_flags{0};
 static std::atomic<int64_t> opt_tile_n{0};  // 0 = choose by shape, else 256 or 512
 static std::atomic<int64_t> opt_store_hint{0};
 static std::atomic<int64_t> opt_split_k{0};  // 0 = choose by shape, else the split count
+static std::atomic<int64_t> opt_tail_split{1};  // split the tail wave's tiles (auto mode)
+static std::atomic<int64_t> opt_serial_fixup{0};  // 1 = always the last-arriver fix-up
 
 // ------------------------------------------------------------------ driver entry point
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -67,6 +70,58 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
       fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   });
   return fn;
+}
+
+// ------------------------------------------------------------------ tensor-map cache
+// A tensor map is a pure function of (base address, type, dims, strides, box, swizzle, L2
+// promotion), so repeated calls on the same buffers reuse the encoded map instead of calling
+// the driver again.  Small and bounded: cleared when full.
+struct MapKey {
+  uint64_t w[24];
+  bool operator==(const MapKey& o) const { return std::memcmp(w, o.w, sizeof(w)) == 0; }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = 1469598103934665603ull;
+    for (uint64_t x : k.w) h = (h ^ x) * 1099511628211ull;
+    return (size_t)h;
+  }
+};
+static std::mutex g_map_mu;
+static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_map_cache;
+
+static CUresult encode_cached(CUtensorMap* out, CUtensorMapDataType dt, cuuint32_t rank, void* addr,
+                              const cuuint64_t* dims, const cuuint64_t* strides,
+                              const cuuint32_t* box, CUtensorMapSwizzle swz,
+                              CUtensorMapL2promotion l2) {
+  MapKey key;
+  std::memset(key.w, 0, sizeof(key.w));
+  key.w[0] = (uint64_t)(uintptr_t)addr;
+  key.w[1] = ((uint64_t)dt << 32) | ((uint64_t)rank << 24) | ((uint64_t)swz << 8) | (uint64_t)l2;
+  for (cuuint32_t i = 0; i < rank; ++i) {
+    key.w[2 + i] = dims[i];
+    key.w[7 + i] = box[i];
+    if (i + 1 < rank) key.w[12 + i] = strides[i];
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_map_cache.find(key);
+    if (it != g_map_cache.end()) {
+      *out = it->second;
+      return CUDA_SUCCESS;
+    }
+  }
+  auto encode = get_encode();
+  if (!encode) return CUDA_ERROR_NOT_SUPPORTED;
+  const cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = encode(out, dt, rank, addr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      swz, l2, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS) {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    if (g_map_cache.size() >= 1024) g_map_cache.clear();
+    g_map_cache.emplace(key, *out);
+  }
+  return r;
 }
 
 // ------------------------------------------------------------------ per-device state
@@ -159,6 +214,35 @@ __global__ void fill_uniform_kernel(__half* __restrict__ dst, int64_t n, uint64_
     const int32_t r = (int32_t)(h >> 40) - 8388608;
     dst[e] = __float2half_rn((float)r * (1.0f / 8388608.0f));
   }
+}
+
+// ------------------------------------------------------------------ split-K workspace pool
+// Stream-ordered pool of the split-K workspaces, one per device, that keeps freed memory for
+// reuse (release threshold: unlimited) instead of returning it to the driver at every
+// synchronisation as the default pool does.
+static int split_pool(cudaMemPool_t* out) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(B2G_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (!pools[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    e = cudaMemPoolCreate(&pool, &props);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemPoolCreate(split-K)");
+    uint64_t keep = ~0ull;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    pools[dev] = pool;
+  }
+  *out = pools[dev];
+  return B2G_OK;
 }
 
 // ------------------------------------------------------------------ fixed scratch
@@ -355,8 +439,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   if (c_m) tma_ok = tma_ok && (N == 1 || al16(c_sn * 4));
   if (!tma_ok) return launch_generic(B2G_PATH_GENERIC);
 
-  auto encode = get_encode();
-  if (!encode) return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (!get_encode()) return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
 
   // filler stride for size-1 modes: anything 16-byte aligned works (coordinate is always 0)
   auto fill = [](int64_t s, int64_t size, int64_t prev_extent_bytes) -> cuuint64_t {
@@ -375,10 +458,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     st[2] = fill(M3[1].sa * 2, bsz, (int64_t)st[1] * isz);
     st[3] = fill(M3[0].sa * 2, asz, (int64_t)st[2] * bsz);
     cuuint32_t box[5] = {64, 1, (cuuint32_t)bi, (cuuint32_t)bb, (cuuint32_t)ba};
-    cuuint32_t es[5] = {1, 1, 1, 1, 1};
-    CUresult r = encode(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(A), dims, st, box,
-                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode_cached(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(A), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map A not encodable
   }
   // choose CTA grouping
@@ -407,10 +487,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     st[0] = fill(K2[1].sc * 2, ksz, N * 2);
     st[1] = fill(K2[0].sc * 2, jsz, (int64_t)st[0] * ksz);
     cuuint32_t box[3] = {64, 64, 1};
-    cuuint32_t es[3] = {1, 1, 1};
-    CUresult r = encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B), dims, st, box,
-                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode_cached(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map B (N-major) not encodable
   } else {  // dims (k, j, n)
     cuuint64_t dims[3] = {(cuuint64_t)ksz, (cuuint64_t)jsz, (cuuint64_t)N};
@@ -418,10 +495,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     st[0] = fill(K2[0].sc * 2, jsz, ksz * 2);
     st[1] = fill(b_sn * 2, N, (int64_t)st[0] * jsz);
     cuuint32_t box[3] = {64, 1, (cuuint32_t)bph};
-    cuuint32_t es[3] = {1, 1, 1};
-    CUresult r = encode(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B), dims, st, box,
-                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode_cached(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map B (K-major) not encodable
   }
   // C
@@ -432,10 +506,8 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     st[1] = fill(M3[1].sc * 4, bsz, (int64_t)st[0] * isz);
     st[2] = fill(M3[0].sc * 4, asz, (int64_t)st[1] * bsz);
     cuuint32_t box[4] = {32, (cuuint32_t)si, (cuuint32_t)sb, (cuuint32_t)sa};
-    cuuint32_t es[4] = {1, 1, 1, 1};
-    CUresult r = encode(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, dims, st, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode_cached(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_NONE);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map C (N-major) not encodable
   } else {  // dims (i, n, b, a), unswizzled si x 32 boxes
     cuuint64_t dims[4] = {(cuuint64_t)isz, (cuuint64_t)N, (cuuint64_t)bsz, (cuuint64_t)asz};
@@ -444,10 +516,8 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     st[1] = fill(M3[1].sc * 4, bsz, (int64_t)st[0] * N);
     st[2] = fill(M3[0].sc * 4, asz, (int64_t)st[1] * bsz);
     cuuint32_t box[4] = {(cuuint32_t)si, 32, (cuuint32_t)sb, (cuuint32_t)sa};
-    cuuint32_t es[4] = {1, 1, 1, 1};
-    CUresult r = encode(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, dims, st, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode_cached(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, dims, st, box, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_NONE);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map C (M-major) not encodable
   }
 
@@ -522,23 +592,51 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   const int group_cap = cg == 1 ? ds->sm_count : ds->max_clusters[variant][bk][cm];
   // ---- split-K: when the tiles cannot fill the GPU, split K so that every CTA group has a
   // unit; each split keeps at least 8 K blocks.
+  // Tail split: when the tiles fill whole waves plus a partial one, split only the tiles of
+  // the partial wave so that its units fill the CTA groups.
   int splits = (int)opt_split_k.load();
+  int full = 0;
   if (splits <= 0) {
     splits = 1;
-    if (2 * p.num_tiles <= group_cap && p.k_iters >= 16)
-      splits = std::min({group_cap / std::max(1, p.num_tiles), p.k_iters / 8, 16});
+    full = p.num_tiles;
+    const int waves = p.num_tiles / std::max(1, group_cap);
+    const int rem = p.num_tiles - waves * group_cap;
+    // every split keeps >= 16 K blocks: below that the fixed cost of a unit (pipeline fill,
+    // partial write and fence, fix-up) outweighs the shorter main loop (1024^3 runs 15.6 us
+    // unsplit, 27.8 us split two ways)
+    if (2 * p.num_tiles <= group_cap && p.k_iters >= 32) {
+      splits = std::min({group_cap / std::max(1, p.num_tiles), p.k_iters / 16, 16});
+      full = 0;
+    } else if (opt_tail_split.load() && waves >= 1 && rem > 0 && group_cap / rem >= 2 &&
+               p.k_iters >= 32) {
+      splits = std::min({group_cap / rem, 4, p.k_iters / 16});
+      full = waves * group_cap;
+    }
   }
   splits = std::max(1, std::min(splits, p.k_iters));
   p.k_per_split = (p.k_iters + splits - 1) / splits;
   p.k_splits = (p.k_iters + p.k_per_split - 1) / p.k_per_split;  // no empty split
-  p.num_units = p.num_tiles * p.k_splits;
+  if (p.k_splits == 1) full = p.num_tiles;
+  if (fixed && full > 0 && full < p.num_tiles) {
+    // the tail split is an optimisation: under a fixed scratch it is dropped if it does not fit
+    const size_t need = (size_t)(p.num_tiles - full) * p.k_splits * cg * 128 * bn * sizeof(float) +
+                        ((size_t)(p.num_tiles - full) * cg * sizeof(int) + 255) / 256 * 256;
+    if (need > fixed->bytes) {
+      full = p.num_tiles;
+      p.k_splits = 1;
+      p.k_per_split = p.k_iters;
+    }
+  }
+  p.num_full = full;
+  p.num_units = full + (p.num_tiles - full) * p.k_splits;
   p.ws = nullptr;
   p.counters = nullptr;
   void* scratch = nullptr;
+  const size_t split_tiles = (size_t)(p.num_tiles - p.num_full);
   if (p.k_splits > 1 && fixed) {
     // caller-supplied scratch (b2g_gemm_f16_f32_noalloc): no allocation
-    const size_t ws_bytes = (size_t)p.num_units * cg * 128 * bn * sizeof(float);
-    const size_t ctr_bytes = ((size_t)p.num_tiles * cg * sizeof(int) + 255) / 256 * 256;
+    const size_t ws_bytes = split_tiles * p.k_splits * cg * 128 * bn * sizeof(float);
+    const size_t ctr_bytes = (split_tiles * cg * sizeof(int) + 255) / 256 * 256;
     if (ctr_bytes + ws_bytes > fixed->bytes)
       return fail(B2G_ERR_INVALID_ARG,
                   "split-K scratch of %zu bytes exceeds the %zu-byte static scratch of "
@@ -549,10 +647,13 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     cudaError_t e = cudaMemsetAsync(p.counters, 0, ctr_bytes, stream);  // counters start at 0
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split-K counters)");
   } else if (p.k_splits > 1) {
-    const size_t ws_bytes = (size_t)p.num_units * cg * 128 * bn * sizeof(float);
-    const size_t ctr_bytes = ((size_t)p.num_tiles * cg * sizeof(int) + 255) / 256 * 256;
-    cudaError_t e = cudaMallocAsync(&scratch, ctr_bytes + ws_bytes, stream);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocAsync(split-K workspace)");
+    const size_t ws_bytes = split_tiles * p.k_splits * cg * 128 * bn * sizeof(float);
+    const size_t ctr_bytes = (split_tiles * cg * sizeof(int) + 255) / 256 * 256;
+    cudaMemPool_t pool = nullptr;
+    int prc = split_pool(&pool);
+    if (prc != B2G_OK) return prc;
+    cudaError_t e = cudaMallocFromPoolAsync(&scratch, ctr_bytes + ws_bytes, pool, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMallocFromPoolAsync(split-K workspace)");
     p.counters = static_cast<int*>(scratch);
     p.ws = reinterpret_cast<float*>(static_cast<char*>(scratch) + ctr_bytes);
     e = cudaMemsetAsync(p.counters, 0, ctr_bytes, stream);
@@ -563,6 +664,12 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   }
   int groups = std::min(group_cap, p.num_units);
   if (groups < 1) groups = 1;
+  // parallel fix-up only when each CTA group holds at most one split unit (all split units of
+  // the launch then run at the same time, so their mutual waits always end)
+  p.fixup_parallel = (p.k_splits > 1 && p.num_full % groups == 0 &&
+                      p.num_units - p.num_full <= groups && !opt_serial_fixup.load())
+                         ? 1
+                         : 0;
 
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -714,6 +821,10 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_force_generic = value ? 1 : 0;
   } else if (!strcmp(key, "fault_flags")) {
     opt_fault_flags = value;
+  } else if (!strcmp(key, "serial_fixup")) {
+    opt_serial_fixup = value ? 1 : 0;
+  } else if (!strcmp(key, "tail_split")) {
+    opt_tail_split = value ? 1 : 0;
   } else if (!strcmp(key, "split_k")) {
     if (value < 0 || value > 64) return B2G_ERR_INVALID_ARG;
     opt_split_k = value;
@@ -738,6 +849,8 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "tile_n")) return opt_tile_n;
   if (!strcmp(key, "store_hint")) return opt_store_hint;
   if (!strcmp(key, "split_k")) return opt_split_k;
+  if (!strcmp(key, "tail_split")) return opt_tail_split;
+  if (!strcmp(key, "serial_fixup")) return opt_serial_fixup;
   return -1;
 }
 

@@ -38,6 +38,7 @@ enum : int {
   ERR_WAIT_TEMPTY = 3,  // MMA waiting for the epilogue to release an accumulator
   ERR_WAIT_TFULL = 4,   // epilogue waiting for an accumulator
   ERR_WAIT_DRAIN = 5,   // teardown waiting for copies / MMAs in flight
+  ERR_WAIT_FIXUP = 6,   // split-K unit waiting for the partial tiles of its siblings
 };
 
 // Problem description computed on the host (b2g_api.cu) and passed by value.
@@ -61,15 +62,23 @@ struct GemmParams {
   int store_hint;              // 1 = C stores carry an L2 evict-first hint
   int accumulate;              // 1 = C += alpha*A.B (TMA reduce-add), 0 = C = alpha*A.B
   float alpha;                 // scale of A.B
-  // split-K: work unit u = tile * k_splits + split; split s covers K blocks
-  // [s*k_per_split, min(k_iters, (s+1)*k_per_split)).  With k_splits > 1 every unit writes its
-  // fp32 partial tile to `ws` and bumps counters[tile*CG + cta]; the unit that arrives last
-  // sums the partials in split order (deterministic) and stores C, then resets the counter.
+  // Work units: the first num_full tiles (in tile order) are one unit each over all of K; each
+  // remaining tile is split into k_splits units, split s covering the K blocks
+  // [s*k_per_split, min(k_iters, (s+1)*k_per_split)).  num_full = 0 is plain split-K (too few
+  // tiles to fill the GPU); num_full = (waves)*(CTA groups) splits only the tail wave.  A split
+  // unit writes its fp32 partial tile to `ws` and bumps counters[split tile*CG + cta]; the unit
+  // that arrives last sums the partials in split order (deterministic), stores C and resets
+  // the counter.
+  int num_full;
   int k_splits;
   int k_per_split;
-  int num_units;               // num_tiles * k_splits
-  float* ws;                   // num_units * CG * 128 * BN floats (k_splits > 1)
-  int* counters;               // num_tiles * CG ints, zero between calls
+  int num_units;               // num_full + (num_tiles - num_full) * k_splits
+  float* ws;                   // (num_tiles - num_full) * k_splits * CG * 128 * BN floats
+  int* counters;               // (num_tiles - num_full) * CG ints, zero between calls
+  // 1 = parallel fix-up: every CTA group holds at most one split unit, so all splits of a tile
+  // run at the same time; each waits (bounded) for the tile's partials and reduces 1/k_splits
+  // of it.  0 = the unit that arrives last reduces the whole tile (no waiting).
+  int fixup_parallel;
   unsigned long long timeout_ns;
   int fault_flags;             // test-only: bit 0 = producer issues no loads (forces a timeout)
 };
@@ -123,6 +132,26 @@ static_assert(Cfg<2, 512>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512>::STAGES >= 4,
 __host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool b_mn_major) {
   return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
+}
+
+// Unit u -> (tile, split index, number of splits of that tile, K-block range).
+__device__ __forceinline__ void unit_info(const GemmParams& p, int u, int& t, int& sp, int& ns,
+                                          int& kb_lo, int& kb_hi) {
+  if (u < p.num_full) {
+    t = u;
+    sp = 0;
+    ns = 1;
+    kb_lo = 0;
+    kb_hi = p.k_iters;
+  } else {
+    const int v = u - p.num_full;
+    const int st = v / p.k_splits;
+    t = p.num_full + st;
+    sp = v - st * p.k_splits;
+    ns = p.k_splits;
+    kb_lo = sp * p.k_per_split;
+    kb_hi = min(p.k_iters, kb_lo + p.k_per_split);
+  }
 }
 
 __device__ __forceinline__ void m_tile_origin(const GemmParams& p, int mt, int& i0, int& b0,
@@ -216,9 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it = 0;
       bool ok = true;
       for (int u = group_id; u < p.num_units && ok; u += num_groups) {
-        const int t = u / p.k_splits;
-        const int kb_lo = (u - t * p.k_splits) * p.k_per_split;
-        const int kb_hi = min(p.k_iters, kb_lo + p.k_per_split);
+        int t, sp, ns, kb_lo, kb_hi;
+        unit_info(p, u, t, sp, ns, kb_lo, kb_hi);
         int pm, tn;
         b2g_sched_tile(t, p.num_pm_tiles, p.num_n_tiles, p.raster_group, &pm, &tn);
         const int mt = pm * CG + (int)cta_rank;
@@ -279,9 +307,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       for (int u = group_id; u < p.num_units && ok; u += num_groups, ++tc) {
-        const int t = u / p.k_splits;
-        const int kb_lo = (u - t * p.k_splits) * p.k_per_split;
-        const int nkb = min(p.k_iters, kb_lo + p.k_per_split) - kb_lo;
+        int t, sp, ns, kb_lo, kb_hi;
+        unit_info(p, u, t, sp, ns, kb_lo, kb_hi);
+        const int nkb = kb_hi - kb_lo;
         // BN = 256: two accumulators, tempty[acc] guards accumulator acc.
         // BN = 512: one accumulator, tempty[h] guards its N-half h (the epilogue frees the
         // halves one after the other).
@@ -350,7 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int i_l = r0 % p.bi;
     int tc = 0, nstore = 0;
     for (int u = group_id; u < p.num_units; u += num_groups, ++tc) {
-      const int t = u / p.k_splits;
+      int t, sp, ns, kb_lo, kb_hi;
+      unit_info(p, u, t, sp, ns, kb_lo, kb_hi);
       int pm, tn;
       b2g_sched_tile(t, p.num_pm_tiles, p.num_n_tiles, p.raster_group, &pm, &tn);
       const int mt = pm * CG + (int)cta_rank;
@@ -418,12 +447,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
 
-      if (p.k_splits > 1) {
+      if (ns > 1) {
         // ---- split-K unit: partial tile -> workspace; the last unit of the tile reduces.
-        // Workspace block of (unit, CTA): 128 x BN floats laid out [chunk][row][32] so each
+        // Workspace block of (split unit, CTA): 128 x BN floats laid out [chunk][row][32] so each
         // warp writes and reads 4 KiB contiguous per chunk.
         const size_t blk = (size_t)128 * BN;
-        float* mine = p.ws + ((size_t)u * CG + cta_rank) * blk + (size_t)(32 * q + lane) * 32;
+        const int v = u - p.num_full;   // split unit index
+        const int st = t - p.num_full;  // split tile index
+        float* mine = p.ws + ((size_t)v * CG + cta_rank) * blk + (size_t)(32 * q + lane) * 32;
 #pragma unroll 1
         for (int ch = 0; ch < C::CHUNKS; ++ch) {
           uint32_t v[32];
@@ -444,8 +475,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         __threadfence();
         ptx::named_barrier_sync(1, kEpiWarps * 32);
         volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
-        if (threadIdx.x == 64) {
-          int* ctr = p.counters + (size_t)t * CG + cta_rank;
+        int* ctr = p.counters + (size_t)st * CG + cta_rank;
+        int ch_first = 0, ch_step = 1;
+        if (p.fixup_parallel) {
+          // publish this partial, then wait until every split of the tile has published
+          if (threadIdx.x == 64) {
+            atomicAdd(ctr, 1);
+            *last_flag = ptx::wait_counter_ge(ctr, ns, abort_flag, err, ERR_WAIT_FIXUP, lim) ? 1 : 0;
+          }
+          ch_first = sp;  // this unit reduces chunks sp, sp + ns, ...
+          ch_step = ns;
+        } else if (threadIdx.x == 64) {
           const int old = atomicAdd(ctr, 1);
           const int last = old == p.k_splits - 1;
           if (last) *ctr = 0;  // every split has arrived: ready for the next call
@@ -454,10 +494,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::named_barrier_sync(1, kEpiWarps * 32);
         if (*last_flag) {
           __threadfence();
-          const float* base_t = p.ws + ((size_t)t * p.k_splits * CG + cta_rank) * blk +
+          const float* base_t = p.ws + ((size_t)st * p.k_splits * CG + cta_rank) * blk +
                                 (size_t)(32 * q + lane) * 32;
 #pragma unroll 1
-          for (int ch = 0; ch < C::CHUNKS; ++ch) {
+          for (int ch = ch_first; ch < C::CHUNKS; ch += ch_step) {
             float a[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) a[j] = 0.0f;
@@ -479,8 +519,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_chunk(v, ch);
           }
         }
-        // the next unit's partial writes reuse no buffer of this one; nothing more to order
         ptx::named_barrier_sync(1, kEpiWarps * 32);
+        if (p.fixup_parallel && threadIdx.x == 64) {
+          // done reading the partials; the last split to get here resets the counter
+          if (atomicAdd(ctr, 1) == 2 * ns - 1) *ctr = 0;
+        }
         continue;
       }
 

@@ -113,6 +113,25 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, i
   }
 }
 
+// Bounded wait until the global counter *ctr reaches `target` (acquire loads, with a short
+// sleep between polls).  Used only when every CTA that adds to the counter is resident.
+__device__ __forceinline__ bool wait_counter_ge(const int* ctr, int target, volatile int* abort_flag,
+                                                int* err, int code, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer();
+  for (uint32_t n = 0;; ++n) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if (*abort_flag) return false;
+    if ((n & 15u) == 15u && globaltimer() - t0 > limit_ns) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, code);
+      return false;
+    }
+    __nanosleep(64);
+  }
+}
+
 __device__ __forceinline__ void spin_ns(uint64_t ns) {
   const uint64_t t0 = globaltimer();
   while (globaltimer() - t0 < ns) {

@@ -92,3 +92,52 @@ def test_split_k_auto_skinny(b2g, cuda, orc):
     for r in (0, 1, 63, 64, 127):
         a = orc.uniform_f16((1, K), 1, r * K)
         assert_close(orc, dC[r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, what="row %d" % r)
+
+
+@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+def test_split_k_parallel_and_serial_fixup_agree(b2g, cuda, orc, cg, tn):
+    """Both fix-up schedules sum the same partials in split order: identical bits."""
+    torch = cuda
+    M, N, K = 256, 1024, 4096
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+    dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+    b2g.fill_uniform(dA, M * K, 81)
+    b2g.fill_uniform(dB, K * N, 82)
+    outs = []
+    for serial in (0, 1):
+        dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+        with options(b2g, cta_group=cg, tile_n=tn, split_k=4, serial_fixup=serial):
+            b2g.gemm(dA, dB, dC, M, N, K)
+        torch.cuda.synchronize()
+        assert b2g.device_status() == 0
+        outs.append(dC)
+    assert torch.equal(outs[0], outs[1])
+    A = orc.uniform_f16((M, K), 81)
+    B = orc.uniform_f16((K, N), 82)
+    assert_close(orc, outs[0].cpu().numpy(), orc.gemm_f64(A, B), K)
+
+
+def test_tail_split_contraction_shape(b2g, cuda, orc):
+    """8192 x 4096 x 8192 (BASELINE configs[2] as a GEMM view): 3.5 waves of 256x512 tiles,
+    so only the tail wave's tiles are split in K.  Same result as without the tail split
+    within tolerance, and correct against the oracle on sampled rows."""
+    torch = cuda
+    M, N, K = 8192, 4096, 8192
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+    dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+    b2g.fill_uniform(dA, M * K, 1)
+    b2g.fill_uniform(dB, K * N, 2)
+    res = {}
+    for tail in (1, 0):
+        dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+        with options(b2g, tail_split=tail):
+            b2g.gemm(dA, dB, dC, M, N, K)
+        torch.cuda.synchronize()
+        assert b2g.device_status() == 0
+        res[tail] = dC
+    diff = (res[1] - res[0]).abs().max().item()
+    assert diff <= orc.tolerance(K, 1.0, 1.0), diff
+    B = orc.uniform_f16((K, N), 2)
+    for r in (0, 4095, 6000, 7935, 8191):
+        a = orc.uniform_f16((1, K), 1, r * K)
+        assert_close(orc, res[1][r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, what="row %d" % r)
