@@ -225,6 +225,11 @@ def main():
                     help="gemm8192: BASELINE configs[1] per GPU (the default line); "
                          "sharded32768: BASELINE configs[4], one 32768^3 GEMM as M-row slabs "
                          "over the N GPUs, B broadcast in K panels inside every step")
+    ap.add_argument("--shape", default=None,
+                    help="M,N,K: time this row-major GEMM instead of 8192^3 (device-resident "
+                         "kernel loop only; used for the other BASELINE shapes and for profiling)")
+    ap.add_argument("--dtype", default="f16", choices=["f16", "bf16", "e4m3", "e5m2"],
+                    help="operand type (f16 = BASELINE's; the others are secondary lines)")
     ap.add_argument("--kernel-only", action="store_true",
                     help="device-resident GEMM steps only (no e2e, CPU baseline or clock "
                          "sampling): the command profiled with ncu")
@@ -248,21 +253,32 @@ def main():
         return run_sharded(args, torch, dist, b2g, ws, rank, local, dev)
 
     M, N, K = M_PER_GPU, N_DIM, K_DIM
+    if args.shape:
+        # another BASELINE shape (configs[0], [2] as its GEMM view, [3]); kernel loop only
+        M, N, K = (int(x) for x in args.shape.split(","))
+        args.kernel_only = True
     flops = 2.0 * M * N * K
     stream = torch.cuda.current_stream()
-    dA = torch.empty((M, K), dtype=torch.float16, device=dev)
-    dB = torch.empty((K, N), dtype=torch.float16, device=dev)
+    dt = {"f16": 0, "bf16": 1, "e4m3": 2, "e5m2": 3}[args.dtype]
+    tdt = {0: torch.float16, 1: torch.bfloat16, 2: torch.uint8, 3: torch.uint8}[dt]
+    if dt:
+        args.kernel_only = True  # secondary operand types: device-resident kernel loop only
+    dA = torch.empty((M, K), dtype=tdt, device=dev)
+    dB = torch.empty((K, N), dtype=tdt, device=dev)
     dC = torch.empty((M, N), dtype=torch.float32, device=dev)
     # rank r's slab of the (M*ws) x K matrix A; B generated on rank 0 and broadcast once
-    b2g.fill_uniform(dA, M * K, 1, rank * M * K, stream)
+    b2g.fill_uniform(dA, M * K, 1, rank * M * K, stream, dtype=dt)
     if rank == 0:
-        b2g.fill_uniform(dB, K * N, 2, 0, stream)
+        b2g.fill_uniform(dB, K * N, 2, 0, stream, dtype=dt)
     if ws > 1:
         dist.broadcast(dB, src=0)
     torch.cuda.synchronize()
 
     def step():
-        b2g.gemm(dA, dB, dC, M, N, K, K, N, N, stream)
+        if dt:
+            b2g.gemm_typed(dA, dB, dC, M, N, K, dt, stream=stream)
+        else:
+            b2g.gemm(dA, dB, dC, M, N, K, K, N, N, stream)
 
     for _ in range(args.warmup):
         step()
@@ -318,6 +334,10 @@ def main():
     # the sustained (power-capped) library figure, otherwise with the burst one
     sustained = elapsed_ms > 250.0
     peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    peak_note = ""
+    if dt >= 2:  # fp8 tensor rate is twice fp16/bf16 (nominal 4.5 vs 2.25 PFLOP/s dense)
+        peak *= 2.0
+        peak_note = " x2 (fp8 = 2x the measured 16-bit rate)"
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and not args.kernel_only:
         v, rows, secs, thr = cpu_baseline(args.cpu_seconds)
@@ -330,8 +350,13 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    metric = "gemm_tflops_8192cubed_fp16_fp32"
+    if args.shape:
+        metric = "gemm_tflops_%dx%dx%d_fp16_fp32" % (M, N, K)
+    if dt:
+        metric = metric.replace("fp16", args.dtype)
     line = {
-        "metric": "gemm_tflops_8192cubed_fp16_fp32",
+        "metric": metric,
         "value": value,
         "unit": "TFLOP/s",
         "n_gpus": ws,
@@ -341,19 +366,23 @@ def main():
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "f16 in, f32 accumulate/out",
-        "data": "synthetic: seeded U[-1,1] fp16 generated on the device (b2g_fill_uniform_f16)",
+        "dtype": "%s in, f32 accumulate/out" % args.dtype,
+        "data": "synthetic: seeded U[-1,1] %s generated on the device (b2g_fill_uniform)" % args.dtype,
         "config": {
-            "workload": "gemm 8192x8192x8192 row-major fp16->fp32 per GPU (BASELINE configs[1]);"
-                        " N>1: M-row slabs of a (8192N)x8192x8192 GEMM, B broadcast once",
+            "workload": ("gemm %dx%dx%d row-major fp16->fp32 (kernel loop)" % (M, N, K)) if args.shape
+                        else "gemm 8192x8192x8192 row-major fp16->fp32 per GPU (BASELINE configs[1]);"
+                             " N>1: M-row slabs of a (8192N)x8192x8192 GEMM, B broadcast once",
             "M": M, "N": N, "K": K, "world_size": ws, "path": path,
-            "l2": "inputs+output 512 MiB per GPU > 126 MB L2 (no flush needed)",
+            "l2": "inputs+output %.0f MiB per GPU (%s 126 MB L2)" % (
+                (2 * M * K + 2 * K * N + 4 * M * N) / 2**20,
+                "> : no flush needed" if 2 * M * K + 2 * K * N + 4 * M * N > 126e6 else
+                "< : steps may hit L2"),
             "frac_of_spec_2250": value / ws / SPEC_TFLOPS,
         },
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": profiled_traffic(),
-                     "peak_source": "%s %s" % (peaks_src, "bf16_tflops_sustained" if sustained
-                                               else "bf16_tflops"),
+                     "peak_source": "%s %s%s" % (peaks_src, "bf16_tflops_sustained" if sustained
+                                                 else "bf16_tflops", peak_note),
                      "kernel": "gemm_tc_kernel", "flops_per_launch": flops,
                      "avg_launch_ms": avg_launch_ms},
         "cpu_baseline": cpu,

@@ -41,6 +41,14 @@ enum {
   B2G_ERR_NCCL = 5,        /* collective failure in the sharded path */
 };
 
+/* Operand element types of the typed entry points (C is always fp32). */
+enum {
+  B2G_DTYPE_F16 = 0,  /* IEEE binary16 (the reference's _Float16) */
+  B2G_DTYPE_BF16 = 1, /* bfloat16 */
+  B2G_DTYPE_E4M3 = 2, /* fp8 e4m3 (OCP / NVIDIA __nv_fp8_e4m3) */
+  B2G_DTYPE_E5M2 = 3, /* fp8 e5m2 */
+};
+
 /* Which kernel the calling thread's last successful compute call ran. */
 enum {
   B2G_PATH_NONE = 0,
@@ -70,6 +78,16 @@ int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t M, int64_t 
  */
 int b2g_gemm_ex(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K,
                 int64_t lda, int64_t ldb, int64_t ldc, float alpha, float beta, void* stream);
+
+/*
+ * b2g_gemm_ex with the operand type as an argument: A and B are both `dtype`
+ * (B2G_DTYPE_*), products are exact in fp32 and accumulated in fp32 (tcgen05 kind::f16 for
+ * fp16/bf16, kind::f8f6f4 for the fp8 types).  fp16 is the reference's type (mmm.cpp:27);
+ * bf16 and fp8 have no counterpart in the reference.
+ */
+int b2g_gemm_typed(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K,
+                   int64_t lda, int64_t ldb, int64_t ldc, int dtype, float alpha, float beta,
+                   void* stream);
 
 /*
  * b2g_gemm_f16_f32 for callers that can't call cudaMalloc: this entry point allocates
@@ -117,6 +135,16 @@ int b2g_contract5d_ex(const void* A, const int64_t a_shape[5], const int64_t a_s
                       const void* B, const int64_t b_shape[3], const int64_t b_stride[3],
                       float* C, const int64_t c_shape[4], const int64_t c_stride[4], float alpha,
                       float beta, void* stream);
+
+/* The contraction with an operand type argument (see b2g_gemm_typed). */
+int b2g_contract5d_typed(const void* A, const int64_t a_shape[5], const int64_t a_stride[5],
+                         const void* B, const int64_t b_shape[3], const int64_t b_stride[3],
+                         float* C, const int64_t c_shape[4], const int64_t c_stride[4], int dtype,
+                         float alpha, float beta, void* stream);
+
+/* b2g_fill_uniform_f16 for any operand type: the same exact fp32 values, rounded to nearest
+ * even into `dtype` (saturating to the largest finite value for the fp8 types). */
+int b2g_fill_uniform(void* dst, int64_t n, int dtype, uint64_t seed, uint64_t offset, void* stream);
 
 /*
  * Fill n fp16 elements with the seeded uniform [-1,1] sequence: element e of the logical

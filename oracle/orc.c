@@ -464,3 +464,133 @@ int64_t orc_check_tolerance(const float* got, int64_t ldg, const double* ref, in
   *max_rel = mr;
   return bad;
 }
+
+/* ------------------------------------------------------------------ */
+/* bf16 and fp8 (e4m3, e5m2) operands: exact decode and round-to-      */
+/* nearest-even encode from the format definitions:                    */
+/*   bf16: the top 16 bits of an IEEE binary32.                        */
+/*   e4m3: 1 sign, 4 exponent (bias 7), 3 mantissa; no infinities,     */
+/*         S.1111.111 is NaN; largest finite 448.                      */
+/*   e5m2: 1 sign, 5 exponent (bias 15), 2 mantissa; IEEE-style        */
+/*         infinities and NaNs; largest finite 57344.                  */
+/* Encoding saturates to the largest finite value (the convention of   */
+/* the CUDA library's fill kernel).  Type codes match b2g_gemm.h:      */
+/* 0 f16, 1 bf16, 2 e4m3, 3 e5m2.                                      */
+/* ------------------------------------------------------------------ */
+float orc_bf16_to_f32(uint16_t b) {
+  uint32_t x = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &x, 4);
+  return f;
+}
+
+uint16_t orc_f32_to_bf16(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  if ((x & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((x >> 16) | 0x40); /* quiet NaN */
+  x += 0x7fffu + ((x >> 16) & 1u);
+  return (uint16_t)(x >> 16);
+}
+
+float orc_fp8_to_f32(uint8_t c, int e4m3) {
+  const int mb = e4m3 ? 3 : 2, eb = e4m3 ? 4 : 5, bias = e4m3 ? 7 : 15;
+  const int s = c >> 7, e = (c >> mb) & ((1 << eb) - 1), m = c & ((1 << mb) - 1);
+  float v;
+  if (e4m3 && e == 15 && m == 7)
+    v = NAN;
+  else if (!e4m3 && e == 31)
+    v = m ? NAN : INFINITY;
+  else if (e == 0)
+    v = ldexpf((float)m, 1 - bias - mb);
+  else
+    v = ldexpf((float)((1 << mb) | m), e - bias - mb);
+  return s ? -v : v;
+}
+
+uint8_t orc_f32_to_fp8(float f, int e4m3) {
+  const int maxcode = e4m3 ? 0x7e : 0x7b; /* largest finite positive code */
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  const uint8_t sign = (uint8_t)((x >> 24) & 0x80);
+  if (f != f) return (uint8_t)(sign | 0x7f);
+  const double a = fabs((double)f);
+  if (a >= (double)orc_fp8_to_f32((uint8_t)maxcode, e4m3)) return (uint8_t)(sign | maxcode);
+  /* positive finite codes are increasing in value: find the last code <= a */
+  int lo = 0, hi = maxcode;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) / 2;
+    if ((double)orc_fp8_to_f32((uint8_t)mid, e4m3) <= a)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  const double v0 = orc_fp8_to_f32((uint8_t)lo, e4m3);
+  if (v0 == a) return (uint8_t)(sign | lo);
+  const double v1 = orc_fp8_to_f32((uint8_t)(lo + 1), e4m3);
+  const double mid = 0.5 * (v0 + v1);
+  int c = a < mid ? lo : a > mid ? lo + 1 : ((lo & 1) ? lo + 1 : lo);
+  return (uint8_t)(sign | c);
+}
+
+/* dst (fp32) <- n elements of type `dt` */
+void orc_typed_to_f32(const void* src, int dt, float* dst, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    if (dt == 0) dst[i] = orc_h2f(((const uint16_t*)src)[i]);
+    else if (dt == 1) dst[i] = orc_bf16_to_f32(((const uint16_t*)src)[i]);
+    else dst[i] = orc_fp8_to_f32(((const uint8_t*)src)[i], dt == 2);
+  }
+}
+
+/* dst (type `dt`) <- n fp32 values, round to nearest even */
+void orc_f32_to_typed(const float* src, int dt, void* dst, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) {
+    if (dt == 0) ((uint16_t*)dst)[i] = orc_f2h(src[i]);
+    else if (dt == 1) ((uint16_t*)dst)[i] = orc_f32_to_bf16(src[i]);
+    else ((uint8_t*)dst)[i] = orc_f32_to_fp8(src[i], dt == 2);
+  }
+}
+
+/* The seeded U[-1,1] sequence (orc_uniform_f16_at's fp32 value) in type `dt`. */
+void orc_fill_uniform(void* dst, int64_t n, int dt, uint64_t seed, uint64_t offset) {
+  const uint64_t key = mix64(seed);
+  for (int64_t i = 0; i < n; ++i) {
+    uint64_t h = mix64(key + offset + (uint64_t)i);
+    int32_t r = (int32_t)(h >> 40) - 8388608;
+    float v = (float)r * (1.0f / 8388608.0f);
+    orc_f32_to_typed(&v, dt, (char*)dst + i * (dt >= 2 ? 1 : 2), 1);
+  }
+}
+
+/* FP64-accumulated GEMM on fp32 operands (exact widenings of any operand type), rows [r0, r1);
+ * C row 0 holds output row r0. */
+typedef struct {
+  const float *A, *B;
+  double* C;
+  int64_t N, K, lda, ldb, ldc, r0;
+} f64f_ctx;
+
+static void f64f_rows(void* p, int64_t lo, int64_t hi) {
+  f64f_ctx* c = (f64f_ctx*)p;
+  double* acc = (double*)malloc(sizeof(double) * (size_t)(c->N > 0 ? c->N : 1));
+  for (int64_t rr = lo; rr < hi; ++rr) {
+    int64_t r = c->r0 + rr;
+    for (int64_t n = 0; n < c->N; ++n) acc[n] = 0.0;
+    for (int64_t k = 0; k < c->K; ++k) {
+      double a = (double)c->A[r * c->lda + k];
+      if (a == 0.0) continue;
+      const float* brow = c->B + k * c->ldb;
+      for (int64_t n = 0; n < c->N; ++n) acc[n] += a * (double)brow[n];
+    }
+    for (int64_t n = 0; n < c->N; ++n) c->C[rr * c->ldc + n] = acc[n];
+  }
+  free(acc);
+}
+
+int orc_gemm_f64_f32in(const float* A, const float* B, double* C, int64_t M, int64_t N, int64_t K,
+                       int64_t lda, int64_t ldb, int64_t ldc, int64_t r0, int64_t r1,
+                       int nthreads) {
+  (void)M;
+  f64f_ctx ctx = {A, B, C, N, K, lda, ldb, ldc, r0};
+  parallel_for(r1 - r0, nthreads, f64f_rows, &ctx);
+  return 0;
+}

@@ -43,6 +43,11 @@ def lib():
         L.orc_gemm_f32_blocked.restype = ctypes.c_int
         L.orc_gemm_f32_blocked.argtypes = [_p, _p, _p, _p] + [_i64] * 8 + [ctypes.c_int]
         L.orc_simd_level.restype = ctypes.c_int
+        L.orc_typed_to_f32.argtypes = [_p, ctypes.c_int, _p, _i64]
+        L.orc_f32_to_typed.argtypes = [_p, ctypes.c_int, _p, _i64]
+        L.orc_fill_uniform.argtypes = [_p, _i64, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64]
+        L.orc_gemm_f64_f32in.restype = ctypes.c_int
+        L.orc_gemm_f64_f32in.argtypes = [_p, _p, _p] + [_i64] * 8 + [ctypes.c_int]
         L.orc_check_tolerance.restype = _i64
         L.orc_check_tolerance.argtypes = [_p, _i64, _p, _i64, _i64, _i64, _i64, ctypes.c_double,
                                           ctypes.c_double, _p, _p, _p]
@@ -178,3 +183,46 @@ def check(got, ref, K, max_a, max_b):
                                     g2.shape[1], K, float(max_a), float(max_b), ctypes.byref(ma),
                                     ctypes.byref(mr), ctypes.byref(fb))
     return int(bad), ma.value, mr.value, int(fb.value)
+
+
+# ---- operand types other than fp16 (codes of b2g_gemm.h): raw bits as uint16 / uint8 arrays
+F16, BF16, E4M3, E5M2 = 0, 1, 2, 3
+_BITS = {F16: np.uint16, BF16: np.uint16, E4M3: np.uint8, E5M2: np.uint8}
+
+
+def uniform(shape, seed, dtype, offset=0):
+    """The seeded U[-1,1] sequence rounded (nearest even) into `dtype`; raw bits."""
+    n = int(np.prod(shape)) if len(shape) else 1
+    out = np.empty(n, dtype=_BITS[dtype])
+    lib().orc_fill_uniform(_ptr(out), n, dtype, seed, offset)
+    return out.reshape(shape)
+
+
+def to_f32(bits, dtype):
+    """Exact fp32 values of `dtype` bits."""
+    bits = np.ascontiguousarray(bits, dtype=_BITS[dtype])
+    out = np.empty(bits.shape, dtype=np.float32)
+    lib().orc_typed_to_f32(_ptr(bits), dtype, _ptr(out), bits.size)
+    return out
+
+
+def from_f32(x, dtype):
+    """fp32 -> `dtype` bits, round to nearest even (fp8: saturating)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=_BITS[dtype])
+    lib().orc_f32_to_typed(_ptr(x), dtype, _ptr(out), x.size)
+    return out
+
+
+def gemm_f64_typed(A_bits, B_bits, dtype, rows=None, threads=None):
+    """FP64-accumulated GEMM of two `dtype` matrices given as raw bits, rows [r0, r1)."""
+    A = to_f32(A_bits, dtype)
+    B = to_f32(B_bits, dtype)
+    M, K = A.shape
+    K2, N = B.shape
+    assert K == K2
+    r0, r1 = rows if rows is not None else (0, M)
+    C = np.empty((r1 - r0, N), dtype=np.float64)
+    lib().orc_gemm_f64_f32in(_ptr(A), _ptr(B), _ptr(C), M, N, K, K, N, N, r0, r1,
+                             threads or nthreads())
+    return C

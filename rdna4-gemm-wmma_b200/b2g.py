@@ -24,6 +24,8 @@ ERR_CUDA = 3
 ERR_TIMEOUT = 4
 ERR_NCCL = 5
 
+DTYPE_F16, DTYPE_BF16, DTYPE_E4M3, DTYPE_E5M2 = 0, 1, 2, 3
+
 PATH_NONE, PATH_TC_1CTA, PATH_TC_2CTA, PATH_GENERIC, PATH_ZERO, PATH_EMPTY = range(6)
 PATH_NAMES = {0: "none", 1: "tc_1cta", 2: "tc_2cta", 3: "generic", 4: "zero", 5: "empty"}
 
@@ -59,6 +61,14 @@ def load(path=None):
                                     ctypes.c_float, ctypes.c_float, vp]
     L.b2g_gemm.restype = ctypes.c_int
     L.b2g_gemm.argtypes = [vp, vp, vp, i64, i64, i64]
+    L.b2g_gemm_typed.restype = ctypes.c_int
+    L.b2g_gemm_typed.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int,
+                                 ctypes.c_float, ctypes.c_float, vp]
+    L.b2g_contract5d_typed.restype = ctypes.c_int
+    L.b2g_contract5d_typed.argtypes = [vp, i64p, i64p, vp, i64p, i64p, vp, i64p, i64p,
+                                       ctypes.c_int, ctypes.c_float, ctypes.c_float, vp]
+    L.b2g_fill_uniform.restype = ctypes.c_int
+    L.b2g_fill_uniform.argtypes = [vp, i64, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64, vp]
     L.b2g_gemm_f16_f32_noalloc.restype = ctypes.c_int
     L.b2g_gemm_f16_f32_noalloc.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
     L.b2g_contract5d_f16_f32.restype = ctypes.c_int
@@ -173,8 +183,17 @@ def contract5d_ex(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stri
                                _arr(c_stride, 4), float(alpha), float(beta), _stream(stream)))
 
 
-def fill_uniform(dst, n, seed, offset=0, stream=None):
-    _check(load().b2g_fill_uniform_f16(_ptr(dst), n, seed, offset, _stream(stream)))
+def fill_uniform(dst, n, seed, offset=0, stream=None, dtype=DTYPE_F16):
+    """n elements of the seeded U[-1,1] sequence (element offset `offset`) in `dtype`."""
+    _check(load().b2g_fill_uniform(_ptr(dst), n, dtype, seed, offset, _stream(stream)))
+
+
+def gemm_typed(A, B, C, M, N, K, dtype, alpha=1.0, beta=0.0, lda=None, ldb=None, ldc=None,
+               stream=None):
+    """C = alpha * A.B + beta * C with A, B of operand type `dtype` (DTYPE_*)."""
+    _check(load().b2g_gemm_typed(_ptr(A), _ptr(B), _ptr(C), M, N, K, K if lda is None else lda,
+                                 N if ldb is None else ldb, N if ldc is None else ldc, dtype,
+                                 float(alpha), float(beta), _stream(stream)))
 
 
 def last_path():

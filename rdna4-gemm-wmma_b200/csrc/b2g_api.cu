@@ -7,7 +7,9 @@
 // Layouts outside TMA's addressing rules run on gemm_generic_kernel below, which computes
 // exactly GEMM_Naive's arithmetic (mmm.cpp:52-62).  There is no host/CPU compute path.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -128,8 +130,8 @@ static CUresult encode_cached(CUtensorMap* out, CUtensorMapDataType dt, cuuint32
 struct DevState {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
-  bool attr_set[3][2][2] = {};  // [variant][b_kmajor][c_mcontig]
-  int max_clusters[3][2][2] = {};
+  bool attr_set[2][3][2][2] = {};  // [fp8][variant][b_kmajor][c_mcontig]
+  int max_clusters[2][3][2][2] = {};
 };
 static std::mutex g_dev_mu;
 static DevState g_dev[64];
@@ -159,7 +161,21 @@ struct Geo {
   int64_t cst[4];         // a,b,i,n strides
 };
 
-__global__ void gemm_generic_kernel(const __half* __restrict__ A, const __half* __restrict__ B,
+// Operand element -> float (exact for every supported type).
+template <int DT>
+__device__ __forceinline__ float elem_f32(const void* base, int64_t i) {
+  if constexpr (DT == B2G_DTYPE_F16)
+    return __half2float(static_cast<const __half*>(base)[i]);
+  else if constexpr (DT == B2G_DTYPE_BF16)
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
+  else if constexpr (DT == B2G_DTYPE_E4M3)
+    return float(static_cast<const __nv_fp8_e4m3*>(base)[i]);
+  else
+    return float(static_cast<const __nv_fp8_e5m2*>(base)[i]);
+}
+
+template <int DT>
+__global__ void gemm_generic_kernel(const void* __restrict__ A, const void* __restrict__ B,
                                     float* __restrict__ C, const Geo g, float alpha, float beta) {
   const int64_t rows = g.as[0] * g.as[1] * g.as[2];
   const int64_t total = rows * g.n;
@@ -169,13 +185,13 @@ __global__ void gemm_generic_kernel(const __half* __restrict__ A, const __half* 
     const int64_t ii = row % g.as[2];
     const int64_t ib = (row / g.as[2]) % g.as[1];
     const int64_t ia = row / (g.as[2] * g.as[1]);
-    const __half* ar = A + ia * g.ast[0] + ib * g.ast[1] + ii * g.ast[2];
-    const __half* bc = B + col * g.bst[2];
+    const int64_t ar = ia * g.ast[0] + ib * g.ast[1] + ii * g.ast[2];
+    const int64_t bc = col * g.bst[2];
     float acc = 0.0f;
     for (int64_t j = 0; j < g.as[3]; ++j)
       for (int64_t k = 0; k < g.as[4]; ++k)
-        acc += __half2float(ar[j * g.ast[3] + k * g.ast[4]]) *
-               __half2float(bc[j * g.bst[0] + k * g.bst[1]]);
+        acc += elem_f32<DT>(A, ar + j * g.ast[3] + k * g.ast[4]) *
+               elem_f32<DT>(B, bc + j * g.bst[0] + k * g.bst[1]);
     float* c = C + ia * g.cst[0] + ib * g.cst[1] + ii * g.cst[2] + col * g.cst[3];
     const float out = alpha == 1.0f ? acc : alpha * acc;
     *c = beta == 0.0f ? out : out + beta * *c;  // beta == 0: C is not read
@@ -205,14 +221,23 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 
-__global__ void fill_uniform_kernel(__half* __restrict__ dst, int64_t n, uint64_t seed,
+template <int DT>
+__global__ void fill_uniform_kernel(void* __restrict__ dst, int64_t n, uint64_t seed,
                                     uint64_t offset) {
   const uint64_t key = mix64(seed);
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
        e += (int64_t)gridDim.x * blockDim.x) {
     const uint64_t h = mix64(key + offset + (uint64_t)e);
     const int32_t r = (int32_t)(h >> 40) - 8388608;
-    dst[e] = __float2half_rn((float)r * (1.0f / 8388608.0f));
+    const float v = (float)r * (1.0f / 8388608.0f);  // exact; rounded to nearest even below
+    if constexpr (DT == B2G_DTYPE_F16)
+      static_cast<__half*>(dst)[e] = __float2half_rn(v);
+    else if constexpr (DT == B2G_DTYPE_BF16)
+      static_cast<__nv_bfloat16*>(dst)[e] = __float2bfloat16_rn(v);
+    else if constexpr (DT == B2G_DTYPE_E4M3)
+      static_cast<__nv_fp8_e4m3*>(dst)[e] = __nv_fp8_e4m3(v);
+    else
+      static_cast<__nv_fp8_e5m2*>(dst)[e] = __nv_fp8_e5m2(v);
   }
 }
 
@@ -311,11 +336,26 @@ static int coalesce(Mode* m, int n) {
 
 static inline bool al16(int64_t bytes) { return (bytes & 15) == 0; }
 
+// ------------------------------------------------------------------ operand types
+static inline int dt_size(int dt) { return dt >= B2G_DTYPE_E4M3 ? 1 : 2; }
+// UMMA operand format code: kind::f16 0 = F16, 1 = BF16; kind::f8f6f4 0 = E4M3, 1 = E5M2
+static inline int dt_fmt(int dt) { return (dt == B2G_DTYPE_BF16 || dt == B2G_DTYPE_E5M2) ? 1 : 0; }
+static inline CUtensorMapDataType dt_map(int dt) {
+  return dt == B2G_DTYPE_F16    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+         : dt == B2G_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                : CU_TENSOR_MAP_DATA_TYPE_UINT8;  // fp8: bytes
+}
+
 // ------------------------------------------------------------------ core dispatch
 static int run(const void* A, const int64_t as[5], const int64_t ast[5], const void* B,
                const int64_t bs[3], const int64_t bst[3], float* Cp, const int64_t cs[4],
-               const int64_t cst[4], float alpha, float beta, cudaStream_t stream,
+               const int64_t cst[4], int dtype, float alpha, float beta, cudaStream_t stream,
                const FixedScratch* fixed = nullptr) {
+  if (dtype < B2G_DTYPE_F16 || dtype > B2G_DTYPE_E5M2)
+    return fail(B2G_ERR_INVALID_ARG, "unknown operand type code %d", dtype);
+  const int esz = dt_size(dtype);
+  const int kb_elems = kRowBytes / esz;  // K elements per 128-byte stage row
+  const CUtensorMapDataType map_type = dt_map(dtype);
   // ---- validation
   for (int t = 0; t < 5; ++t)
     if (as[t] < 0) return fail(B2G_ERR_INVALID_ARG, "negative A extent");
@@ -357,9 +397,21 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   const unsigned eblocks =
       (unsigned)std::min<int64_t>((total + eth - 1) / eth, (int64_t)ds->sm_count * 32);
   auto launch_generic = [&](int path) -> int {
-    gemm_generic_kernel<<<eblocks, eth, 0, stream>>>(static_cast<const __half*>(A),
-                                                     static_cast<const __half*>(B), Cp,
-                                                     make_geo(), alpha, beta);
+    const Geo g = make_geo();
+    switch (dtype) {
+      case B2G_DTYPE_F16:
+        gemm_generic_kernel<B2G_DTYPE_F16><<<eblocks, eth, 0, stream>>>(A, B, Cp, g, alpha, beta);
+        break;
+      case B2G_DTYPE_BF16:
+        gemm_generic_kernel<B2G_DTYPE_BF16><<<eblocks, eth, 0, stream>>>(A, B, Cp, g, alpha, beta);
+        break;
+      case B2G_DTYPE_E4M3:
+        gemm_generic_kernel<B2G_DTYPE_E4M3><<<eblocks, eth, 0, stream>>>(A, B, Cp, g, alpha, beta);
+        break;
+      default:
+        gemm_generic_kernel<B2G_DTYPE_E5M2><<<eblocks, eth, 0, stream>>>(A, B, Cp, g, alpha, beta);
+        break;
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "generic kernel launch");
     t_path = path;
@@ -432,10 +484,10 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   // every M mode is an outer dimension of A; of C too, except the innermost one when C is
   // M-contiguous (it is then the map's unit-stride dimension 0)
   for (int t = 0; t < 3; ++t)
-    tma_ok = tma_ok && stride_ok(M3[t], true, 2) && ((c_m && t == 2) || stride_ok(M3[t], false, 4));
-  tma_ok = tma_ok && stride_ok(K2[0], true, 2) && stride_ok(K2[0], false, 2);
-  if (b_mn) tma_ok = tma_ok && stride_ok(K2[1], false, 2);
-  if (b_k) tma_ok = tma_ok && (N == 1 || al16(b_sn * 2));
+    tma_ok = tma_ok && stride_ok(M3[t], true, esz) && ((c_m && t == 2) || stride_ok(M3[t], false, 4));
+  tma_ok = tma_ok && stride_ok(K2[0], true, esz) && stride_ok(K2[0], false, esz);
+  if (b_mn) tma_ok = tma_ok && stride_ok(K2[1], false, esz);
+  if (b_k) tma_ok = tma_ok && (N == 1 || al16(b_sn * esz));
   if (c_m) tma_ok = tma_ok && (N == 1 || al16(c_sn * 4));
   if (!tma_ok) return launch_generic(B2G_PATH_GENERIC);
 
@@ -453,12 +505,12 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     cuuint64_t dims[5] = {(cuuint64_t)ksz, (cuuint64_t)jsz, (cuuint64_t)isz, (cuuint64_t)bsz,
                           (cuuint64_t)asz};
     cuuint64_t st[4];
-    st[0] = fill(K2[0].sa * 2, jsz, ksz * 2);
-    st[1] = fill(M3[2].sa * 2, isz, (int64_t)st[0] * jsz);
-    st[2] = fill(M3[1].sa * 2, bsz, (int64_t)st[1] * isz);
-    st[3] = fill(M3[0].sa * 2, asz, (int64_t)st[2] * bsz);
-    cuuint32_t box[5] = {64, 1, (cuuint32_t)bi, (cuuint32_t)bb, (cuuint32_t)ba};
-    CUresult r = encode_cached(&tmA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(A), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    st[0] = fill(K2[0].sa * esz, jsz, ksz * esz);
+    st[1] = fill(M3[2].sa * esz, isz, (int64_t)st[0] * jsz);
+    st[2] = fill(M3[1].sa * esz, bsz, (int64_t)st[1] * isz);
+    st[3] = fill(M3[0].sa * esz, asz, (int64_t)st[2] * bsz);
+    cuuint32_t box[5] = {(cuuint32_t)kb_elems, 1, (cuuint32_t)bi, (cuuint32_t)bb, (cuuint32_t)ba};
+    CUresult r = encode_cached(&tmA, map_type, 5, const_cast<void*>(A), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map A not encodable
   }
   // choose CTA grouping
@@ -484,18 +536,18 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   if (b_mn) {  // dims (n, k, j)
     cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)ksz, (cuuint64_t)jsz};
     cuuint64_t st[2];
-    st[0] = fill(K2[1].sc * 2, ksz, N * 2);
-    st[1] = fill(K2[0].sc * 2, jsz, (int64_t)st[0] * ksz);
-    cuuint32_t box[3] = {64, 64, 1};
-    CUresult r = encode_cached(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    st[0] = fill(K2[1].sc * esz, ksz, N * esz);
+    st[1] = fill(K2[0].sc * esz, jsz, (int64_t)st[0] * ksz);
+    cuuint32_t box[3] = {(cuuint32_t)kb_elems, (cuuint32_t)kb_elems, 1};  // one MN-major atom
+    CUresult r = encode_cached(&tmB, map_type, 3, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map B (N-major) not encodable
   } else {  // dims (k, j, n)
     cuuint64_t dims[3] = {(cuuint64_t)ksz, (cuuint64_t)jsz, (cuuint64_t)N};
     cuuint64_t st[2];
-    st[0] = fill(K2[0].sc * 2, jsz, ksz * 2);
-    st[1] = fill(b_sn * 2, N, (int64_t)st[0] * jsz);
-    cuuint32_t box[3] = {64, 1, (cuuint32_t)bph};
-    CUresult r = encode_cached(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    st[0] = fill(K2[0].sc * esz, jsz, ksz * esz);
+    st[1] = fill(b_sn * esz, N, (int64_t)st[0] * jsz);
+    cuuint32_t box[3] = {(cuuint32_t)kb_elems, 1, (cuuint32_t)bph};
+    CUresult r = encode_cached(&tmB, map_type, 3, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map B (K-major) not encodable
   }
   // C
@@ -533,7 +585,8 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.num_pm_tiles = (int)((nmt64 + cg - 1) / cg);
   p.n_size = (int)N;
   p.num_n_tiles = (int)nnt64;
-  p.k_blocks_per_j = (int)((ksz + kBK - 1) / kBK);
+  p.k_blocks_per_j = (int)((ksz + kb_elems - 1) / kb_elems);
+  p.ab_format = dt_fmt(dtype);
   p.k_iters = (int)(jsz * p.k_blocks_per_j);
   p.num_tiles = p.num_pm_tiles * p.num_n_tiles;
   int rg = (int)opt_raster_group.load();
@@ -553,20 +606,27 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
   const int bk = b_k ? 1 : 0, cm = c_m ? 1 : 0;
   const int variant = cg == 1 ? 0 : (bn == 256 ? 1 : 2);
-  static const KernFn table[3][2][2] = {
-      {{gemm_tc_kernel<1, 256, false, false>, gemm_tc_kernel<1, 256, false, true>},
-       {gemm_tc_kernel<1, 256, true, false>, gemm_tc_kernel<1, 256, true, true>}},
-      {{gemm_tc_kernel<2, 256, false, false>, gemm_tc_kernel<2, 256, false, true>},
-       {gemm_tc_kernel<2, 256, true, false>, gemm_tc_kernel<2, 256, true, true>}},
-      {{gemm_tc_kernel<2, 512, false, false>, gemm_tc_kernel<2, 512, false, true>},
-       {gemm_tc_kernel<2, 512, true, false>, gemm_tc_kernel<2, 512, true, true>}}};
+  static const KernFn table[2][3][2][2] = {
+      {{{gemm_tc_kernel<1, 256, false, false, 2>, gemm_tc_kernel<1, 256, false, true, 2>},
+        {gemm_tc_kernel<1, 256, true, false, 2>, gemm_tc_kernel<1, 256, true, true, 2>}},
+       {{gemm_tc_kernel<2, 256, false, false, 2>, gemm_tc_kernel<2, 256, false, true, 2>},
+        {gemm_tc_kernel<2, 256, true, false, 2>, gemm_tc_kernel<2, 256, true, true, 2>}},
+       {{gemm_tc_kernel<2, 512, false, false, 2>, gemm_tc_kernel<2, 512, false, true, 2>},
+        {gemm_tc_kernel<2, 512, true, false, 2>, gemm_tc_kernel<2, 512, true, true, 2>}}},
+      {{{gemm_tc_kernel<1, 256, false, false, 1>, gemm_tc_kernel<1, 256, false, true, 1>},
+        {gemm_tc_kernel<1, 256, true, false, 1>, gemm_tc_kernel<1, 256, true, true, 1>}},
+       {{gemm_tc_kernel<2, 256, false, false, 1>, gemm_tc_kernel<2, 256, false, true, 1>},
+        {gemm_tc_kernel<2, 256, true, false, 1>, gemm_tc_kernel<2, 256, true, true, 1>}},
+       {{gemm_tc_kernel<2, 512, false, false, 1>, gemm_tc_kernel<2, 512, false, true, 1>},
+        {gemm_tc_kernel<2, 512, true, false, 1>, gemm_tc_kernel<2, 512, true, true, 1>}}}};
   static const uint32_t smem_of[3] = {Cfg<1, 256>::SMEM_BYTES, Cfg<2, 256>::SMEM_BYTES,
                                       Cfg<2, 512>::SMEM_BYTES};
-  KernFn kern = table[variant][bk][cm];
+  const int e8 = esz == 1 ? 1 : 0;
+  KernFn kern = table[e8][variant][bk][cm];
   const uint32_t smem = smem_of[variant];
   {
     std::lock_guard<std::mutex> lk(g_dev_mu);
-    if (!ds->attr_set[variant][bk][cm]) {
+    if (!ds->attr_set[e8][variant][bk][cm]) {
       cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(smem)");
       if (cg == 2) {
@@ -584,12 +644,12 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
         int nclu = 0;
         e = cudaOccupancyMaxActiveClusters(&nclu, (void*)kern, &qc);
         if (e != cudaSuccess || nclu <= 0) nclu = ds->sm_count / 2;
-        ds->max_clusters[variant][bk][cm] = nclu;
+        ds->max_clusters[e8][variant][bk][cm] = nclu;
       }
-      ds->attr_set[variant][bk][cm] = true;
+      ds->attr_set[e8][variant][bk][cm] = true;
     }
   }
-  const int group_cap = cg == 1 ? ds->sm_count : ds->max_clusters[variant][bk][cm];
+  const int group_cap = cg == 1 ? ds->sm_count : ds->max_clusters[e8][variant][bk][cm];
   // ---- split-K: when the tiles cannot fill the GPU, split K so that every CTA group has a
   // unit; each split keeps at least 8 K blocks.
   // Tail split: when the tiles fill whole waves plus a partial one, split only the tiles of
@@ -707,7 +767,8 @@ extern "C" int b2g_gemm_ex(const void* A, const void* B, float* C, int64_t M, in
   const int64_t as[5] = {1, 1, M, 1, K}, ast[5] = {0, 0, lda, 0, 1};
   const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
   const int64_t cs[4] = {1, 1, M, N}, cst[4] = {0, 0, ldc, 1};
-  return run(A, as, ast, B, bs, bst, C, cs, cst, alpha, beta, static_cast<cudaStream_t>(stream));
+  return run(A, as, ast, B, bs, bst, C, cs, cst, B2G_DTYPE_F16, alpha, beta,
+             static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t M, int64_t N,
@@ -728,7 +789,8 @@ extern "C" int b2g_gemm_f16_f32_noalloc(const void* A, const void* B, float* C, 
   const int64_t as[5] = {1, 1, M, 1, K}, ast[5] = {0, 0, lda, 0, 1};
   const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
   const int64_t cs[4] = {1, 1, M, N}, cst[4] = {0, 0, ldc, 1};
-  return run(A, as, ast, B, bs, bst, C, cs, cst, 1.0f, 0.0f, static_cast<cudaStream_t>(stream),
+  return run(A, as, ast, B, bs, bst, C, cs, cst, B2G_DTYPE_F16, 1.0f, 0.0f,
+             static_cast<cudaStream_t>(stream),
              &fs);
 }
 
@@ -745,7 +807,8 @@ extern "C" int b2g_contract5d_ex(const void* A, const int64_t a_shape[5],
   t_err.clear();
   if (!a_shape || !a_stride || !b_shape || !b_stride || !c_shape || !c_stride)
     return fail(B2G_ERR_INVALID_ARG, "null shape/stride array");
-  return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, alpha, beta,
+  return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, B2G_DTYPE_F16,
+             alpha, beta,
              static_cast<cudaStream_t>(stream));
 }
 
@@ -758,10 +821,12 @@ extern "C" int b2g_contract5d_f16_f32(const void* A, const int64_t a_shape[5],
                            0.0f, stream);
 }
 
-extern "C" int b2g_fill_uniform_f16(void* dst, int64_t n, uint64_t seed, uint64_t offset,
-                                    void* stream) {
+extern "C" int b2g_fill_uniform(void* dst, int64_t n, int dtype, uint64_t seed, uint64_t offset,
+                                void* stream) {
   t_err.clear();
   if (n < 0) return fail(B2G_ERR_INVALID_ARG, "negative length");
+  if (dtype < B2G_DTYPE_F16 || dtype > B2G_DTYPE_E5M2)
+    return fail(B2G_ERR_INVALID_ARG, "unknown operand type code %d", dtype);
   if (n == 0) return B2G_OK;
   if (!dst) return fail(B2G_ERR_INVALID_ARG, "dst is null");
   int dev = 0;
@@ -771,12 +836,57 @@ extern "C" int b2g_fill_uniform_f16(void* dst, int64_t n, uint64_t seed, uint64_
   int rc = device_state(dev, &ds);
   if (rc) return rc;
   const int threads = 256;
-  int64_t blocks = std::min<int64_t>((n + threads - 1) / threads, (int64_t)ds->sm_count * 16);
-  fill_uniform_kernel<<<(unsigned)blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<__half*>(dst), n, seed, offset);
+  const unsigned blocks =
+      (unsigned)std::min<int64_t>((n + threads - 1) / threads, (int64_t)ds->sm_count * 16);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case B2G_DTYPE_F16:
+      fill_uniform_kernel<B2G_DTYPE_F16><<<blocks, threads, 0, s>>>(dst, n, seed, offset);
+      break;
+    case B2G_DTYPE_BF16:
+      fill_uniform_kernel<B2G_DTYPE_BF16><<<blocks, threads, 0, s>>>(dst, n, seed, offset);
+      break;
+    case B2G_DTYPE_E4M3:
+      fill_uniform_kernel<B2G_DTYPE_E4M3><<<blocks, threads, 0, s>>>(dst, n, seed, offset);
+      break;
+    default:
+      fill_uniform_kernel<B2G_DTYPE_E5M2><<<blocks, threads, 0, s>>>(dst, n, seed, offset);
+      break;
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fill kernel launch");
   return B2G_OK;
+}
+
+extern "C" int b2g_fill_uniform_f16(void* dst, int64_t n, uint64_t seed, uint64_t offset,
+                                    void* stream) {
+  return b2g_fill_uniform(dst, n, B2G_DTYPE_F16, seed, offset, stream);
+}
+
+extern "C" int b2g_gemm_typed(const void* A, const void* B, float* C, int64_t M, int64_t N,
+                              int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int dtype,
+                              float alpha, float beta, void* stream) {
+  t_err.clear();
+  if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
+  if (lda < std::max<int64_t>(K, 1) || ldb < std::max<int64_t>(N, 1) || ldc < std::max<int64_t>(N, 1))
+    return fail(B2G_ERR_INVALID_ARG, "leading dimension smaller than the row length");
+  const int64_t as[5] = {1, 1, M, 1, K}, ast[5] = {0, 0, lda, 0, 1};
+  const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
+  const int64_t cs[4] = {1, 1, M, N}, cst[4] = {0, 0, ldc, 1};
+  return run(A, as, ast, B, bs, bst, C, cs, cst, dtype, alpha, beta,
+             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2g_contract5d_typed(const void* A, const int64_t a_shape[5],
+                                    const int64_t a_stride[5], const void* B,
+                                    const int64_t b_shape[3], const int64_t b_stride[3], float* C,
+                                    const int64_t c_shape[4], const int64_t c_stride[4], int dtype,
+                                    float alpha, float beta, void* stream) {
+  t_err.clear();
+  if (!a_shape || !a_stride || !b_shape || !b_stride || !c_shape || !c_stride)
+    return fail(B2G_ERR_INVALID_ARG, "null shape/stride array");
+  return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, dtype, alpha, beta,
+             static_cast<cudaStream_t>(stream));
 }
 
 extern "C" const char* b2g_last_error_string(void) { return t_err.c_str(); }

@@ -79,12 +79,13 @@ struct GemmParams {
   // run at the same time; each waits (bounded) for the tile's partials and reduces 1/k_splits
   // of it.  0 = the unit that arrives last reduces the whole tile (no waiting).
   int fixup_parallel;
+  int ab_format;               // UMMA operand format code (see make_idesc)
   unsigned long long timeout_ns;
   int fault_flags;             // test-only: bit 0 = producer issues no loads (forces a timeout)
 };
 
 constexpr int kBM = 128;  // rows per CTA (UMMA M per CTA)
-constexpr int kBK = 64;   // K per stage: one 128-byte swizzle row of fp16
+constexpr int kRowBytes = 128;  // bytes of K per stage and operand row: one 128-byte swizzle row
 constexpr int kUN = 256;  // N of one UMMA instruction
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = 192;
@@ -104,9 +105,9 @@ struct Cfg {
   static constexpr int ACC_BUFS = BN == 256 ? 2 : 1;  // accumulators held in TMEM
   static constexpr int BPH = kUN / CG;                // B columns per N-half held by one CTA
   static constexpr int BN_CTA = BN / CG;              // B columns loaded per CTA
-  static constexpr uint32_t A_BYTES = kBM * kBK * 2;  // 16 KiB
-  static constexpr uint32_t B_BYTES = BN_CTA * kBK * 2;
-  static constexpr uint32_t HALF_BYTES = BPH * kBK * 2;  // one N-half of B in shared memory
+  static constexpr uint32_t A_BYTES = kBM * kRowBytes;  // 16 KiB
+  static constexpr uint32_t B_BYTES = BN_CTA * kRowBytes;
+  static constexpr uint32_t HALF_BYTES = BPH * kRowBytes;  // one N-half of B in shared memory
   static constexpr uint32_t EPI_BYTES = kEpiWarps * 2 * kCBuf;
   static constexpr int NUM_BARS_FIXED = 2 + 2 + 1;
   static constexpr int STAGES =
@@ -127,11 +128,12 @@ static_assert(Cfg<1, 256>::SMEM_BYTES <= kSmemLimit && Cfg<1, 256>::STAGES >= 4,
 static_assert(Cfg<2, 256>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256>::STAGES >= 6, "CG=2 budget");
 static_assert(Cfg<2, 512>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512>::STAGES >= 4, "BN=512 budget");
 
-// Instruction descriptor, kind::f16: D fp32 (bit 4), A/B fp16 (format 0), A K-major,
-// B major per template, N>>3 at bit 17, M>>4 at bit 24.
-__host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool b_mn_major) {
-  return (1u << 4) | ((b_mn_major ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
-         ((uint32_t)(M >> 4) << 24);
+// Instruction descriptor (kind::f16 and kind::f8f6f4 share the layout): D fp32 (bit 4), A and
+// B format at bits 7 and 10 (kind::f16: 0 = F16, 1 = BF16; kind::f8f6f4: 0 = E4M3,
+// 1 = E5M2), A K-major, B major per template (bit 16), N>>3 at bit 17, M>>4 at bit 24.
+__host__ __device__ constexpr uint32_t make_idesc(int M, int N, bool b_mn_major, uint32_t fmt) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 // Unit u -> (tile, split index, number of splits of that tile, K-block range).
@@ -165,11 +167,17 @@ __device__ __forceinline__ void m_tile_origin(const GemmParams& p, int mt, int& 
   a0 = ia * p.ba;
 }
 
-template <int CG, int BN, bool B_KMAJOR, bool C_MCONTIG>
+// ESZ: operand element size in bytes (2 = fp16/bf16 via kind::f16, 1 = fp8 via kind::f8f6f4).
+// A K block is 128 bytes of K (64 or 128 elements), consumed by 4 UMMAs of 32 bytes of K each.
+template <int CG, int BN, bool B_KMAJOR, bool C_MCONTIG, int ESZ>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using C = Cfg<CG, BN>;
+  constexpr int KB = kRowBytes / ESZ;                 // K elements per stage
+  constexpr int ATOM = kRowBytes / ESZ;               // MN-major swizzle atom width (elements)
+  constexpr uint32_t ATOM_BYTES = (uint32_t)kRowBytes * KB;  // one atom: ATOM x KB elements
+  constexpr uint32_t MN_STEP = 32u / ESZ * kRowBytes;  // MN-major descriptor advance per UMMA
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint32_t base = ptx::smem_u32(smem_raw);
   const uint32_t pad = (1024u - (base & 1023u)) & 1023u;
@@ -233,8 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tma_load_3d<CG>(dst, &tmB, fb, kc, jj, nh);
       } else {
 #pragma unroll
-        for (int c = 0; c < C::BPH / 64; ++c)
-          ptx::tma_load_3d<CG>(dst + (uint32_t)c * 8192u, &tmB, fb, nh + 64 * c, kc, jj);
+        for (int c = 0; c < C::BPH / ATOM; ++c)
+          ptx::tma_load_3d<CG>(dst + (uint32_t)c * ATOM_BYTES, &tmB, fb, nh + ATOM * c, kc, jj);
       }
     }
   };
@@ -264,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) ptx::mbar_arrive_expect_tx(full_bar(s), C::TX_BYTES);
           if (p.fault_flags & 1) continue;
           const int jj = kb / p.k_blocks_per_j;
-          const int kc = (kb - jj * p.k_blocks_per_j) * kBK;
+          const int kc = (kb - jj * p.k_blocks_per_j) * KB;
           ptx::tma_load_5d<CG>(base + s * C::A_BYTES, &tmA, fb, kc, jj, i0, b0, a0);
           issue_b(base + C::OFF_B + s * C::B_BYTES, fb, n0, kc, jj);
         }
@@ -286,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = make_idesc(kBM * CG, kUN, !B_KMAJOR);
+      const uint32_t idesc = make_idesc(kBM * CG, kUN, !B_KMAJOR, (uint32_t)p.ab_format);
       int it = 0, tc = 0;
       bool ok = true;
       // Issue the MMAs of K block kb from stage s into N-halves [h_lo, h_hi).
@@ -294,15 +302,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sa = base + s * C::A_BYTES;
         const uint32_t sb = base + C::OFF_B + s * C::B_BYTES;
 #pragma unroll
-        for (int k16 = 0; k16 < kBK / 16; ++k16) {
+        for (int k16 = 0; k16 < 4; ++k16) {  // 4 UMMAs of 32 bytes of K
           const uint64_t ad = ptx::smem_desc_sw128(sa + 32u * k16, 16u, 1024u);
 #pragma unroll
           for (int h = 0; h < C::NH; ++h) {
             if (h < h_lo || h >= h_hi) continue;
             const uint32_t bh = sb + (uint32_t)h * C::HALF_BYTES;
             const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(bh + 32u * k16, 16u, 1024u)
-                                         : ptx::smem_desc_sw128(bh + 2048u * k16, 8192u, 1024u);
-            ptx::umma_f16<CG>(d + (uint32_t)h * kUN, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
+                                         : ptx::smem_desc_sw128(bh + MN_STEP * k16, ATOM_BYTES, 1024u);
+            ptx::umma<CG, ESZ>(d + (uint32_t)h * kUN, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
           }
         }
       };

@@ -150,3 +150,41 @@ def test_contraction_oracle_matches_numpy_einsum(orc, shape):
                              st((a, b, i, n)))
     want = np.einsum("abijk,jkn->abin", A.astype(np.float64), B.astype(np.float64))
     assert np.allclose(ref.reshape(a, b, i, n), want, rtol=1e-13, atol=1e-13)
+
+
+@pytest.mark.parametrize("dt,tname", [(2, "float8_e4m3fn"), (3, "float8_e5m2")])
+def test_fp8_conversions_match_torch(orc, dt, tname):
+    """Decode of all 256 codes and round-to-nearest-even encode of random and tie values agree
+    with torch's independent float8 implementation (in range; both saturate differently out of
+    range, where torch gives NaN)."""
+    torch = pytest.importorskip("torch")
+    tdt = getattr(torch, tname)
+    codes = np.arange(256, dtype=np.uint8)
+    mine = orc.to_f32(codes, dt)
+    ref = torch.from_numpy(codes).view(tdt).float().numpy()
+    assert ((mine == ref) | (np.isnan(mine) & np.isnan(ref))).all()
+    lim = 440.0 if dt == 2 else 57000.0
+    x = np.clip(np.random.default_rng(dt).standard_normal(100000) * 4, -lim, lim).astype(np.float32)
+    finite = ref[np.isfinite(ref)]
+    ties = ((np.sort(finite)[1:] + np.sort(finite)[:-1]) / 2).astype(np.float32)
+    x = np.concatenate([x, ties[np.abs(ties) < lim]])
+    assert np.array_equal(orc.from_f32(x, dt), torch.from_numpy(x).to(tdt).view(torch.uint8).numpy())
+
+
+def test_bf16_conversions_match_torch(orc):
+    torch = pytest.importorskip("torch")
+    allb = np.arange(65536, dtype=np.uint16)
+    m = orc.to_f32(allb, orc.BF16)
+    r = torch.from_numpy(allb.view(np.int16)).view(torch.bfloat16).float().numpy()
+    assert ((m == r) | (np.isnan(m) & np.isnan(r))).all()
+    x = (np.random.default_rng(5).standard_normal(100000) * 100).astype(np.float32)
+    assert np.array_equal(orc.from_f32(x, orc.BF16),
+                          torch.from_numpy(x).to(torch.bfloat16).view(torch.uint16).numpy())
+
+
+def test_typed_uniform_is_the_fp16_sequence_rounded(orc):
+    """Every operand type draws the same fp32 values; fp16 matches uniform_f16 bit for bit."""
+    assert np.array_equal(orc.uniform((4096,), 9, orc.F16), orc.uniform_f16((4096,), 9).view(np.uint16))
+    for dt in (orc.BF16, orc.E4M3, orc.E5M2):
+        v = orc.to_f32(orc.uniform((4096,), 9, dt), dt)
+        assert np.abs(v).max() <= 1.0 and np.abs(v - orc.uniform_f16((4096,), 9).astype(np.float32)).max() < 0.07
