@@ -53,7 +53,7 @@ enum {
 enum {
   B2G_PATH_NONE = 0,
   B2G_PATH_TC_1CTA = 1,   /* tcgen05 kernel, one CTA per 128x256 tile */
-  B2G_PATH_TC_2CTA = 2,   /* tcgen05 kernel, CTA pair per 256x256 tile (cta_group::2) */
+  B2G_PATH_TC_2CTA = 2,   /* tcgen05 kernel, CTA pair per 256x256 or 256x512 tile (cta_group::2) */
   B2G_PATH_GENERIC = 3,   /* generic CUDA kernel (layouts outside TMA's rules) */
   B2G_PATH_ZERO = 4,      /* K == 0: C filled with zeros */
   B2G_PATH_EMPTY = 5,     /* M == 0 or N == 0: nothing to do */
@@ -170,6 +170,30 @@ int b2g_gemm_sharded(const void* A_slab, void* B, float* C_slab, int64_t M, int6
                      int64_t lda, int64_t ldb, int64_t ldc, void* comm, int root, int k_panels,
                      void* stream);
 
+/*
+ * Tensor-parallel variants for shapes whose B is too large to replicate (no reference
+ * counterpart).
+ *
+ * K-split with reduce-scatter: rank r holds the K slab b2g_slab_rows(K, world, r) of A
+ * (M x k_r, lda) and of B (k_r x N, ldb); its C_slab (M/world x N, ldc) receives rows
+ * [r*M/world, (r+1)*M/world) of C = sum over ranks of A_r.B_r (fp32 partials in a
+ * stream-ordered scratch buffer, ncclReduceScatter).  M must be a multiple of the rank count.
+ */
+int b2g_gemm_sharded_k(const void* A_kslab, const void* B_kslab, float* C_slab, int64_t M,
+                       int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* comm,
+                       void* stream);
+
+/*
+ * N-slabs with all-gather: rank r holds the column slab b2g_slab_rows(N, world, r) of B
+ * (K x n_r, ldb) and of C (M x n_r, ldc); A (M x K, lda, every rank) is broadcast from `root`
+ * in `m_panels` row panels, each followed by the GEMM of its rows.  With C_full != NULL
+ * (N a multiple of the rank count) every rank also receives the whole row-major C (M x N)
+ * there (ncclAllGather).
+ */
+int b2g_gemm_sharded_n(void* A, const void* B_nslab, float* C_nslab, int64_t M, int64_t N,
+                       int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* comm, int root,
+                       int m_panels, float* C_full, void* stream);
+
 /* Balanced contiguous row partition: rank r gets M/world rows, the first M%world ranks one more. */
 int b2g_slab_rows(int64_t M, int world, int rank, int64_t* row0, int64_t* rows);
 
@@ -201,9 +225,15 @@ int b2g_device_status(int clear);
  *   "raster_group" strip height of the persistent tile order (0 = default)
  *   "timeout_ns"   limit of every bounded device-side wait (default 2e9)
  *   "force_generic" 1 = run the generic kernel for every call (testing)
+ *   "tile_n"       0 = choose by shape (default), 256 or 512 columns per CTA-pair tile
+ *   "split_k"      0 = choose by shape (default), else split every tile's K this many ways
+ *   "tail_split"   1 (default) = split only the tiles of a partial last wave; 0 = never
+ *   "serial_fixup" 1 = split-K partials are always summed by the last unit to arrive
+ *   "store_hint"   1 = C stores carry an L2 evict-first hint
  *   "fault_flags"  test-only fault injection: bit 0 = the TMA producer issues no loads,
  *                  so the MMA wait runs out and the call reports B2G_ERR_TIMEOUT
- * Returns B2G_OK or B2G_ERR_INVALID_ARG for an unknown key.  Options are process-wide.
+ * Returns B2G_OK or B2G_ERR_INVALID_ARG for an unknown key or value.  Options are
+ * process-wide.
  */
 int b2g_set_option(const char* key, int64_t value);
 int64_t b2g_get_option(const char* key);

@@ -90,6 +90,11 @@ def load(path=None):
     L.b2g_gemm_sharded.restype = ctypes.c_int
     L.b2g_gemm_sharded.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp, ctypes.c_int,
                                    ctypes.c_int, vp]
+    L.b2g_gemm_sharded_k.restype = ctypes.c_int
+    L.b2g_gemm_sharded_k.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp, vp]
+    L.b2g_gemm_sharded_n.restype = ctypes.c_int
+    L.b2g_gemm_sharded_n.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp, ctypes.c_int,
+                                     ctypes.c_int, vp, vp]
     L.b2g_slab_rows.restype = ctypes.c_int
     L.b2g_slab_rows.argtypes = [i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64),
                                 ctypes.POINTER(ctypes.c_int64)]
@@ -252,6 +257,34 @@ def gemm_sharded(A_slab, B, C_slab, M, N, K, comm, root=0, k_panels=4, lda=None,
                                    K if lda is None else lda, N if ldb is None else ldb,
                                    N if ldc is None else ldc, comm, root, k_panels,
                                    _stream(stream)))
+
+
+def _ld(x, given, what):
+    if given is not None:
+        return given
+    if hasattr(x, "stride"):
+        return max(1, x.stride(0))
+    raise ValueError(what + " is required for a raw pointer")
+
+
+def gemm_sharded_k(A_kslab, B_kslab, C_slab, M, N, K, comm, lda=None, ldb=None, ldc=None,
+                   stream=None):
+    """K-split GEMM + reduce-scatter: this rank holds K slab slab_rows(K, world, rank) of A and
+    B and receives rows [rank*M/world, (rank+1)*M/world) of C.  Leading dimensions default to
+    the tensors' row strides."""
+    _check(load().b2g_gemm_sharded_k(_ptr(A_kslab), _ptr(B_kslab), _ptr(C_slab), M, N, K,
+                                     _ld(A_kslab, lda, "lda"), _ld(B_kslab, ldb, "ldb"),
+                                     _ld(C_slab, ldc, "ldc"), comm, _stream(stream)))
+
+
+def gemm_sharded_n(A, B_nslab, C_nslab, M, N, K, comm, root=0, m_panels=4, C_full=None,
+                   lda=None, ldb=None, ldc=None, stream=None):
+    """N-slab GEMM: A broadcast from root in row panels, this rank's column slab of C
+    computed locally; with C_full, every rank also receives the whole C (all-gather)."""
+    _check(load().b2g_gemm_sharded_n(_ptr(A), _ptr(B_nslab), _ptr(C_nslab), M, N, K,
+                                     _ld(A, lda, "lda"), _ld(B_nslab, ldb, "ldb"),
+                                     _ld(C_nslab, ldc, "ldc"), comm, root, m_panels,
+                                     _ptr(C_full), _stream(stream)))
 
 
 def version():

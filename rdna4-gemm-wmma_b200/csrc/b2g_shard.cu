@@ -27,6 +27,10 @@ namespace {
 
 struct NcclApi {
   decltype(&ncclBroadcast) bcast = nullptr;
+  decltype(&ncclReduceScatter) reduce_scatter = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclGroupStart) group_start = nullptr;
+  decltype(&ncclGroupEnd) group_end = nullptr;
   decltype(&ncclGetErrorString) errstr = nullptr;
   decltype(&ncclGetUniqueId) unique_id = nullptr;
   decltype(&ncclCommInitRank) init_rank = nullptr;
@@ -52,6 +56,10 @@ NcclApi* nccl() {
       return;
     }
     api.bcast = reinterpret_cast<decltype(api.bcast)>(dlsym(h, "ncclBroadcast"));
+    api.reduce_scatter = reinterpret_cast<decltype(api.reduce_scatter)>(dlsym(h, "ncclReduceScatter"));
+    api.all_gather = reinterpret_cast<decltype(api.all_gather)>(dlsym(h, "ncclAllGather"));
+    api.group_start = reinterpret_cast<decltype(api.group_start)>(dlsym(h, "ncclGroupStart"));
+    api.group_end = reinterpret_cast<decltype(api.group_end)>(dlsym(h, "ncclGroupEnd"));
     api.errstr = reinterpret_cast<decltype(api.errstr)>(dlsym(h, "ncclGetErrorString"));
     api.unique_id = reinterpret_cast<decltype(api.unique_id)>(dlsym(h, "ncclGetUniqueId"));
     api.init_rank = reinterpret_cast<decltype(api.init_rank)>(dlsym(h, "ncclCommInitRank"));
@@ -59,7 +67,8 @@ NcclApi* nccl() {
     api.count = reinterpret_cast<decltype(api.count)>(dlsym(h, "ncclCommCount"));
     api.user_rank = reinterpret_cast<decltype(api.user_rank)>(dlsym(h, "ncclCommUserRank"));
     if (!api.bcast || !api.errstr || !api.unique_id || !api.init_rank || !api.destroy ||
-        !api.count || !api.user_rank)
+        !api.count || !api.user_rank || !api.reduce_scatter || !api.all_gather ||
+        !api.group_start || !api.group_end)
       api.error = "libnccl.so.2 lacks an expected symbol";
   });
   return api.error.empty() ? &api : nullptr;
@@ -187,5 +196,165 @@ extern "C" int b2g_gemm_sharded(const void* A_slab, void* B, float* C_slab, int6
   }
   cudaEventDestroy(start);
   for (int p = 0; p < P; ++p) cudaEventDestroy(done[p]);
+  return rc;
+}
+
+// ------------------------------------------------------------------ tensor-parallel variants
+namespace {
+
+// Stream-ordered scratch for the partial / gathered fp32 matrices of the sharded variants.
+cudaMemPool_t shard_pool(int dev) {
+  static std::mutex mu;
+  static cudaMemPool_t pools[64] = {};
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!pools[dev]) {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    if (cudaMemPoolCreate(&pools[dev], &props) != cudaSuccess) return nullptr;
+    uint64_t keep = ~0ull;
+    cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+  return pools[dev];
+}
+
+int comm_info(void* comm, int* world, int* rank) {
+  NcclApi* n = nccl();
+  if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
+  ncclResult_t r = n->count(static_cast<ncclComm_t>(comm), world);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclCommCount");
+  r = n->user_rank(static_cast<ncclComm_t>(comm), rank);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclCommUserRank");
+  return B2G_OK;
+}
+
+}  // namespace
+
+extern "C" int b2g_gemm_sharded_k(const void* A_kslab, const void* B_kslab, float* C_slab,
+                                  int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                                  int64_t ldc, void* comm, void* stream) {
+  b2g::set_error("");
+  if (M < 0 || N < 0 || K < 0 || !comm) return sfail(B2G_ERR_INVALID_ARG, "bad sharded arguments");
+  int world = 0, rank = 0;
+  int rc = comm_info(comm, &world, &rank);
+  if (rc) return rc;
+  if (M % world != 0) return sfail(B2G_ERR_INVALID_ARG, "M must be a multiple of the rank count");
+  if (ldc < std::max<int64_t>(N, 1)) return sfail(B2G_ERR_INVALID_ARG, "ldc < N");
+  NcclApi* n = nccl();
+  int64_t k0 = 0, kr = 0;
+  b2g_slab_rows(K, world, rank, &k0, &kr);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaMemPool_t pool = shard_pool(dev);
+  if (!pool) return sfail(B2G_ERR_CUDA, "no scratch pool");
+  const int64_t rows = M / world;
+  const bool direct = (ldc == N);  // the reduce-scatter can land in C_slab itself
+  const size_t pbytes = (size_t)M * N * sizeof(float);
+  const size_t tbytes = direct ? 0 : (size_t)rows * N * sizeof(float);
+  void* scratch = nullptr;
+  cudaError_t e = cudaMallocFromPoolAsync(&scratch, pbytes + tbytes + 256, pool, s);
+  if (e != cudaSuccess) return sfail(B2G_ERR_CUDA, cudaGetErrorString(e));
+  float* P = static_cast<float*>(scratch);
+  float* recv = direct ? C_slab : reinterpret_cast<float*>(static_cast<char*>(scratch) + pbytes);
+  // this rank's partial product over its K slab (kr == 0: zeros)
+  rc = b2g_gemm_ex(A_kslab, B_kslab, P, M, N, kr, kr > 0 ? lda : 1, ldb, N, 1.0f, 0.0f, s);
+  if (rc == B2G_OK) {
+    ncclResult_t r = n->reduce_scatter(P, recv, (size_t)rows * N, ncclFloat32, ncclSum,
+                                       static_cast<ncclComm_t>(comm), s);
+    if (r != ncclSuccess) rc = nccl_fail(r, "ncclReduceScatter");
+  }
+  if (rc == B2G_OK && !direct && rows > 0) {
+    e = cudaMemcpy2DAsync(C_slab, ldc * sizeof(float), recv, N * sizeof(float), N * sizeof(float),
+                          rows, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) rc = sfail(B2G_ERR_CUDA, cudaGetErrorString(e));
+  }
+  cudaFreeAsync(scratch, s);
+  return rc;
+}
+
+extern "C" int b2g_gemm_sharded_n(void* A, const void* B_nslab, float* C_nslab, int64_t M,
+                                  int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                                  void* comm, int root, int m_panels, float* C_full,
+                                  void* stream) {
+  b2g::set_error("");
+  if (M < 0 || N < 0 || K < 0 || !comm) return sfail(B2G_ERR_INVALID_ARG, "bad sharded arguments");
+  int world = 0, rank = 0;
+  int rc = comm_info(comm, &world, &rank);
+  if (rc) return rc;
+  if (root < 0 || root >= world) return sfail(B2G_ERR_INVALID_ARG, "root out of range");
+  if (lda < std::max<int64_t>(K, 1)) return sfail(B2G_ERR_INVALID_ARG, "lda < K");
+  if (C_full && N % world != 0)
+    return sfail(B2G_ERR_INVALID_ARG, "the gathered C needs N to be a multiple of the rank count");
+  NcclApi* n = nccl();
+  int64_t n0 = 0, nr = 0;
+  b2g_slab_rows(N, world, rank, &n0, &nr);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaStream_t cs = comm_stream(dev);
+  if (!cs) return sfail(B2G_ERR_CUDA, "no communication stream");
+  // A is broadcast in row panels (contiguous); the slab GEMM of a panel writes its own rows
+  // of C, so panel p's GEMM overlaps panel p+1's transfer and nothing accumulates.
+  const int P = std::max(1, std::min<int>(m_panels, 64));
+  const int64_t mp = M > 0 ? (M + P - 1) / P : 0;
+  cudaEvent_t start, done[64];
+  cudaEventCreateWithFlags(&start, cudaEventDisableTiming);
+  for (int p = 0; p < P; ++p) cudaEventCreateWithFlags(&done[p], cudaEventDisableTiming);
+  cudaEventRecord(start, s);
+  cudaStreamWaitEvent(cs, start, 0);
+  for (int p = 0; p < P && rc == B2G_OK; ++p) {
+    const int64_t m0 = (int64_t)p * mp, m1 = std::min<int64_t>(M, m0 + mp);
+    if (m1 > m0) {
+      char* ap = static_cast<char*>(A) + m0 * lda * 2;
+      ncclResult_t r = n->bcast(ap, ap, (size_t)((m1 - m0) * lda * 2), ncclUint8, root,
+                                static_cast<ncclComm_t>(comm), cs);
+      if (r != ncclSuccess) {
+        rc = nccl_fail(r, "ncclBroadcast");
+        break;
+      }
+    }
+    cudaEventRecord(done[p], cs);
+    cudaStreamWaitEvent(s, done[p], 0);
+    if (m1 > m0 && nr > 0)
+      rc = b2g_gemm_ex(static_cast<const char*>(A) + m0 * lda * 2, B_nslab, C_nslab + m0 * ldc,
+                       m1 - m0, nr, K, lda, ldb, ldc, 1.0f, 0.0f, s);
+  }
+  cudaEventDestroy(start);
+  for (int p = 0; p < P; ++p) cudaEventDestroy(done[p]);
+  if (rc != B2G_OK || !C_full) return rc;
+  // all-gather the column slabs: [rank][M][N/world] in a scratch buffer, then into the
+  // row-major full C (one strided copy per rank)
+  const int64_t nw = N / world;
+  cudaMemPool_t pool = shard_pool(dev);
+  if (!pool) return sfail(B2G_ERR_CUDA, "no scratch pool");
+  const size_t gbytes = (size_t)world * M * nw * sizeof(float);
+  const size_t sbytes = (ldc == nw) ? 0 : (size_t)M * nw * sizeof(float);
+  void* scratch = nullptr;
+  cudaError_t e = cudaMallocFromPoolAsync(&scratch, gbytes + sbytes + 256, pool, s);
+  if (e != cudaSuccess) return sfail(B2G_ERR_CUDA, cudaGetErrorString(e));
+  float* G = static_cast<float*>(scratch);
+  const float* send = C_nslab;
+  if (sbytes) {  // pack the slab contiguously first
+    float* packed = reinterpret_cast<float*>(static_cast<char*>(scratch) + gbytes);
+    e = cudaMemcpy2DAsync(packed, nw * sizeof(float), C_nslab, ldc * sizeof(float),
+                          nw * sizeof(float), M, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) rc = sfail(B2G_ERR_CUDA, cudaGetErrorString(e));
+    send = packed;
+  }
+  if (rc == B2G_OK) {
+    ncclResult_t r = n->all_gather(send, G, (size_t)M * nw, ncclFloat32,
+                                   static_cast<ncclComm_t>(comm), s);
+    if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather");
+  }
+  for (int q = 0; q < world && rc == B2G_OK; ++q) {
+    e = cudaMemcpy2DAsync(C_full + q * nw, N * sizeof(float), G + (size_t)q * M * nw,
+                          nw * sizeof(float), nw * sizeof(float), M, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) rc = sfail(B2G_ERR_CUDA, cudaGetErrorString(e));
+  }
+  cudaFreeAsync(scratch, s);
   return rc;
 }

@@ -1,10 +1,14 @@
-"""M-row-slab sharding of C = A.B across ranks of a torch.distributed process group.
+"""Sharding of C = A.B across ranks of a torch.distributed process group: the pipelines of the
+C entry points in csrc/b2g_shard.cu, driven through torch.distributed for callers that already
+run one process per GPU under torchrun.
 
-The same pipeline as the C entry point b2g_gemm_sharded (csrc/b2g_shard.cu), driven through
-torch.distributed for callers that already run one process per GPU under torchrun: B is
-broadcast from `root` in K-row panels and each rank multiplies its own row slab of A by each
-panel as it arrives (panel 0 overwrites the C slab, later panels add into it).  C stays
-local: no reduction, no gather.
+* sharded_gemm (b2g_gemm_sharded), M-row slabs: B is broadcast from `root` in K-row panels
+  and each rank multiplies its own row slab of A by each panel as it arrives (panel 0
+  overwrites the C slab, later panels add into it).  C stays local: no reduction, no gather.
+* sharded_gemm_k (b2g_gemm_sharded_k), K slabs: each rank multiplies its K slab of A and B
+  into an fp32 partial of the whole C; a reduce-scatter leaves each rank M/world summed rows.
+* sharded_gemm_n (b2g_gemm_sharded_n), N slabs: A is broadcast from `root` in row panels,
+  each rank computes its column slab of C; an optional all-gather assembles the whole C.
 
 `gemm(A_view, B_view, C, rows, N, k, beta)` is the per-panel compute.  It defaults to the CUDA
 library (b2g_gemm_ex); host-side tests pass a CPU stand-in to check the partition and the
@@ -61,3 +65,56 @@ def sharded_gemm(A_slab, B, C_slab, M, N, K, group=None, root=0, panels=4, gemm=
             gemm(A_slab[:, k0:], B[k0:], C_slab, rows, N, k1 - k0, 0.0 if p == 0 else 1.0,
                  A_slab.stride(0), B.stride(0), C_slab.stride(0))
     return row0, rows
+
+
+def sharded_gemm_k(A_kslab, B_kslab, C_slab, M, N, K, group=None, gemm=None):
+    """K-split + reduce-scatter.  A_kslab: M x k_r, B_kslab: k_r x N with (k0, k_r) =
+    slab_rows(K, world, rank); C_slab: M/world x N receives rows [rank*M/world, ...) of C.
+    The partial is fp32 (as in the C library) unless C_slab has another type."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if M % world:
+        raise ValueError("M must be a multiple of the rank count")
+    k0, kr = slab_rows(K, world, rank)
+    rows = M // world
+    gemm = gemm or _b2g_gemm
+    P = torch.empty((M, N), dtype=C_slab.dtype, device=C_slab.device)
+    gemm(A_kslab, B_kslab, P, M, N, kr, 0.0, A_kslab.stride(0) if kr else 1, B_kslab.stride(0),
+         N)
+    out = C_slab if C_slab.is_contiguous() else torch.empty((rows, N), dtype=C_slab.dtype,
+                                                             device=C_slab.device)
+    dist.reduce_scatter_tensor(out, P, group=group)
+    if out is not C_slab:
+        C_slab.copy_(out)
+    return rank * rows, rows
+
+
+def sharded_gemm_n(A, B_nslab, C_nslab, M, N, K, group=None, root=0, panels=4, C_full=None,
+                   gemm=None):
+    """N slabs: A (M x K on every rank, filled from `root`) arrives in row panels (multiples of
+    64 rows but the last), each followed by the GEMM of its rows against this rank's column
+    slab B_nslab (K x n_r, (n0, n_r) = slab_rows(N, world, rank)) into C_nslab (M x n_r).
+    With C_full (M x N, N a multiple of world) every rank also receives the whole C."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n0, nr = slab_rows(N, world, rank)
+    gemm = gemm or _b2g_gemm
+    src = dist.get_global_rank(group, root) if group else root
+    for m0, m1 in k_panels(M, panels):
+        if m1 > m0:
+            dist.broadcast(A[m0:m1], src=src, group=group)
+            if nr > 0:
+                gemm(A[m0:], B_nslab, C_nslab[m0:], m1 - m0, nr, K, 0.0, A.stride(0),
+                     B_nslab.stride(0), C_nslab.stride(0))
+    if C_full is not None:
+        if N % world:
+            raise ValueError("the gathered C needs N to be a multiple of the rank count")
+        nw = N // world
+        G = torch.empty((world * M, nw), dtype=C_nslab.dtype, device=C_nslab.device)
+        dist.all_gather_into_tensor(G, C_nslab[:M, :nw].contiguous(), group=group)
+        C_full.copy_(G.view(world, M, nw).permute(1, 0, 2).reshape(M, N))
+    return n0, nr

@@ -136,3 +136,119 @@ def nccl_sharded_rank(rank, world, uid_path, M, N, K, panels, out_q):
         out_q.put((rank, rows, worst, status, b_ok, None))
     except Exception:
         out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))
+
+
+def _f16(x):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(x).view(np.int16).copy()).view(torch.float16)
+
+
+def _cpu_gemm(A_view, B_view, C, r, n, k, beta, lda, ldb, ldc):
+    """FP64 stand-in for the per-call GEMM of shard.py on CPU tensors."""
+    prod = A_view[:r, :k].double() @ B_view[:k, :n].double()
+    C[:r, :n] = prod if beta == 0.0 else C[:r, :n] + prod
+
+
+def gloo_tp_rank(mode, rank, world, port, M, N, K, panels, out_q):
+    """shard.sharded_gemm_k ("k") or shard.sharded_gemm_n ("n") on CPU tensors with the FP64
+    stand-in; reports (rank, max error against the FP64 oracle of the rows/columns this rank
+    owns, max error of the gathered C or 0)."""
+    try:
+        import torch
+        from oracle import orc
+        shard = _load_pkg("shard")
+        dist = _init_gloo(rank, world, port, 60)
+        A = orc.uniform_f16((M, K), 1)
+        B = orc.uniform_f16((K, N), 2)
+        ref = orc.gemm_f64(A, B)
+        gerr = 0.0
+        if mode == "k":
+            k0, kr = shard.slab_rows(K, world, rank)
+            C_slab = torch.full((M // world, N), float("nan"), dtype=torch.float64)
+            row0, rows = shard.sharded_gemm_k(_f16(A[:, k0:k0 + kr]), _f16(B[k0:k0 + kr]), C_slab,
+                                              M, N, K, gemm=_cpu_gemm)
+            err = float(np.abs(C_slab.numpy() - ref[row0:row0 + rows]).max()) if rows else 0.0
+        else:
+            n0, nr = shard.slab_rows(N, world, rank)
+            A_t = _f16(A) if rank == 0 else torch.full((M, K), float("nan"), dtype=torch.float16)
+            C_n = torch.full((M, max(nr, 1)), float("nan"), dtype=torch.float64)
+            C_full = torch.full((M, N), float("nan"), dtype=torch.float64) if N % world == 0 else None
+            got = shard.sharded_gemm_n(A_t, _f16(B[:, n0:n0 + nr]), C_n, M, N, K, panels=panels,
+                                       C_full=C_full, gemm=_cpu_gemm)
+            assert got == (n0, nr)
+            err = float(np.abs(C_n[:, :nr].numpy() - ref[:, n0:n0 + nr]).max()) if nr else 0.0
+            if C_full is not None:
+                gerr = float(np.abs(C_full.numpy() - ref).max())
+            assert np.array_equal(A_t.view(torch.int16).numpy(), A.view(np.int16))
+        dist.barrier()
+        dist.destroy_process_group()
+        out_q.put((rank, err, gerr, None))
+    except Exception:
+        out_q.put((rank, -1.0, -1.0, traceback.format_exc()))
+
+
+def _nccl_comm(b2g, rank, world, uid_path):
+    import time
+    if rank == 0:
+        uid = b2g.comm_unique_id()
+        with open(uid_path + ".tmp", "wb") as f:
+            f.write(uid)
+        os.replace(uid_path + ".tmp", uid_path)
+    else:
+        t0 = time.time()
+        while not os.path.exists(uid_path):
+            if time.time() - t0 > 60:
+                raise RuntimeError("no NCCL id from rank 0")
+            time.sleep(0.05)
+        uid = open(uid_path, "rb").read()
+    return b2g.comm_init(world, rank, uid)
+
+
+def nccl_tp_rank(mode, rank, world, uid_path, M, N, K, panels, out_q):
+    """b2g_gemm_sharded_k ("k") or b2g_gemm_sharded_n ("n") on `world` GPUs; reports
+    (rank, failing elements of this rank's part on sampled rows, failing elements of the
+    gathered C on sampled rows, device status, A-broadcast bit-exact)."""
+    try:
+        import torch
+        from oracle import orc
+        b2g = _load_pkg("b2g")
+        torch.cuda.set_device(rank)
+        comm = _nccl_comm(b2g, rank, world, uid_path)
+        dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+        dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+        b2g.fill_uniform(dA, M * K, 1)
+        b2g.fill_uniform(dB, K * N, 2)
+        B = orc.uniform_f16((K, N), 2)
+        bad = gbad = 0
+        a_ok = True
+        if mode == "k":
+            k0, kr = b2g.slab_rows(K, world, rank)
+            rows = M // world
+            dC = torch.full((rows, N), float("nan"), dtype=torch.float32, device="cuda")
+            b2g.gemm_sharded_k(dA[:, k0:k0 + kr].contiguous(), dB[k0:k0 + kr].contiguous(), dC,
+                               M, N, K, comm)
+            torch.cuda.synchronize()
+            for r in sorted(set([0, rows - 1, rows // 2, rows // 3])):
+                a = orc.uniform_f16((1, K), 1, (rank * rows + r) * K)
+                bad += orc.check(dC[r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, 1.0, 1.0)[0]
+        else:
+            n0, nr = b2g.slab_rows(N, world, rank)
+            if rank != 0:
+                dA.fill_(float("nan"))
+            dBn = dB[:, n0:n0 + nr].contiguous()
+            dCn = torch.full((M, nr), float("nan"), dtype=torch.float32, device="cuda")
+            dCf = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+            b2g.gemm_sharded_n(dA, dBn, dCn, M, N, K, comm, root=0, m_panels=panels, C_full=dCf)
+            torch.cuda.synchronize()
+            for r in sorted(set([0, M - 1, M // 2, M // 3, M // 7])):
+                a = orc.uniform_f16((1, K), 1, r * K)
+                ref = orc.gemm_f64(a, B)
+                bad += orc.check(dCn[r:r + 1].cpu().numpy(), ref[:, n0:n0 + nr], K, 1.0, 1.0)[0]
+                gbad += orc.check(dCf[r:r + 1].cpu().numpy(), ref, K, 1.0, 1.0)[0]
+            a_ok = bool(torch.equal(dA.cpu().view(torch.int16),
+                                    torch.from_numpy(orc.uniform_f16((M, K), 1).view(np.int16))))
+        status = b2g.device_status()
+        b2g.comm_destroy(comm)
+        out_q.put((rank, bad, gbad, status, a_ok, None))
+    except Exception:
+        out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))

@@ -164,3 +164,24 @@ def test_gemm_timeout_reports_error(b2g, cuda, orc):
     # the device still works
     A, B, C, path = _run_gemm(b2g, cuda, orc, 256, 256, 256)
     assert_close(orc, C, orc.gemm_f64(A, B), 256)
+
+
+def test_gemm_c_larger_than_4gib(b2g, cuda, orc):
+    """32768 x 32768 x 1024: C is 4 GiB (64-bit offsets everywhere); rows near the end checked."""
+    torch = cuda
+    M = N = 32768
+    K = 1024
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+    dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+    dC = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    b2g.fill_uniform(dA, M * K, 1)
+    b2g.fill_uniform(dB, K * N, 2)
+    b2g.gemm(dA, dB, dC, M, N, K)
+    torch.cuda.synchronize()
+    assert b2g.device_status() == 0
+    B = orc.uniform_f16((K, N), 2)
+    for r in (0, 16383, 32767):
+        a = orc.uniform_f16((1, K), 1, r * K)
+        assert_close(orc, dC[r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, what="row %d" % r)
+    del dC
+    torch.cuda.empty_cache()

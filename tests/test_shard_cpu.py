@@ -2,7 +2,8 @@
 and of shard.py agree and tile the rows exactly; the K-panel schedule; the broadcast/panel
 pipeline on world_size-2 gloo ranks with an FP64 CPU stand-in for the per-panel GEMM; and a
 rank that leaves before the collective makes the other rank's broadcast fail instead of
-hanging."""
+hanging.  The K-split (reduce-scatter) and N-slab (A broadcast, all-gather) schedules run the
+same way on gloo ranks."""
 import multiprocessing as mp
 import os
 import random
@@ -91,3 +92,30 @@ def test_gloo_dead_rank_surfaces_error():
             p.kill()
     assert res[1][0] == "left"
     assert res[0][0] == "error", res[0]
+
+
+def _run_tp(mode, world, M, N, K, panels):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=shard_worker.gloo_tp_rank,
+                         args=(mode, r, world, port, M, N, K, panels, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for rank, err, gerr, tb in res:
+        assert tb is None, tb
+        assert 0 <= err < 1e-9 and 0 <= gerr < 1e-9, (rank, err, gerr)
+
+
+@pytest.mark.parametrize("world,M,N,K", [(2, 96, 40, 192), (2, 8, 24, 1), (3, 30, 17, 100)])
+def test_gloo_k_split_reduce_scatter(world, M, N, K):
+    _run_tp("k", world, M, N, K, 1)
+
+
+@pytest.mark.parametrize("world,M,N,K,panels", [(2, 200, 48, 64, 3), (2, 7, 5, 33, 2),
+                                                (3, 130, 30, 20, 4)])
+def test_gloo_n_slabs_all_gather(world, M, N, K, panels):
+    _run_tp("n", world, M, N, K, panels)

@@ -5,6 +5,9 @@ panel GEMMs accumulating into the local C slab) against the oracle.
   panel broadcasts on the internal stream, event ordering, panel accumulation -- runs;
 * two ranks on two GPUs (skipped with fewer): each rank's slab rows checked, and B on the
   non-root rank (filled with NaN before the call) must equal the root's bit for bit.
+The tensor-parallel variants b2g_gemm_sharded_k (K slabs, fp32 partials reduce-scattered into
+M/world-row slabs) and b2g_gemm_sharded_n (N slabs, A broadcast in row panels, optional
+all-gather of C) run the same way: one rank in-process, two ranks as spawned processes.
 Tolerance: |C - R| <= 1e-3*sqrt(K)*max|a|*max|b| + 1e-3*|R| against the FP64 oracle.
 """
 import multiprocessing as mp
@@ -64,3 +67,59 @@ def test_sharded_two_ranks(b2g, cuda):
         assert tb is None, tb
         assert status == 0 and worst == 0 and b_ok, (rank, rows, worst, status, b_ok)
     assert sum(r[1] for r in res) == M
+
+
+class _ListQueue(list):
+    put = list.append
+
+
+@pytest.mark.parametrize("mode", ["k", "n"])
+def test_tp_single_rank(b2g, cuda, mode):
+    with tempfile.TemporaryDirectory() as d:
+        q = _ListQueue()
+        shard_worker.nccl_tp_rank(mode, 0, 1, os.path.join(d, "id"), 512, 768, 1024, 3, q)
+    rank, bad, gbad, status, a_ok, tb = q[0]
+    assert tb is None, tb
+    assert bad == 0 and gbad == 0 and status == 0 and a_ok
+
+
+def test_tp_k_split_padded_c(b2g, cuda, orc):
+    """K-split with ldc > N (the reduce-scatter lands in scratch, then a strided copy)."""
+    torch = cuda
+    M, N, K, ldc = 256, 200, 300, 264
+    uid = b2g.comm_unique_id()
+    comm = b2g.comm_init(1, 0, uid)
+    try:
+        A = orc.uniform_f16((M, K), 5)
+        B = orc.uniform_f16((K, N), 6)
+        dA = torch.from_numpy(A.view(np.int16)).view(torch.float16).cuda()
+        dB = torch.from_numpy(B.view(np.int16)).view(torch.float16).cuda()
+        dC = torch.full((M, ldc), float("nan"), dtype=torch.float32, device="cuda")
+        b2g.gemm_sharded_k(dA, dB, dC, M, N, K, comm, lda=K, ldb=N, ldc=ldc)
+        torch.cuda.synchronize()
+        assert b2g.device_status() == 0
+        out = dC.cpu().numpy()
+        assert_close(orc, out[:, :N], orc.gemm_f64(A, B), K)
+        assert np.isnan(out[:, N:]).all()  # padding untouched
+    finally:
+        b2g.comm_destroy(comm)
+
+
+@pytest.mark.parametrize("mode", ["k", "n"])
+def test_tp_two_ranks(b2g, cuda, mode):
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=shard_worker.nccl_tp_rank,
+                             args=(mode, r, 2, os.path.join(d, "id"), 2048, 1536, 4096, 4, q))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        res = sorted(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=120)
+    for rank, bad, gbad, status, a_ok, tb in res:
+        assert tb is None, tb
+        assert bad == 0 and gbad == 0 and status == 0 and a_ok, (rank, bad, gbad, status, a_ok)
