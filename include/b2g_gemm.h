@@ -52,7 +52,7 @@ enum {
 /* Which kernel the calling thread's last successful compute call ran. */
 enum {
   B2G_PATH_NONE = 0,
-  B2G_PATH_TC_1CTA = 1,   /* tcgen05 kernel, one CTA per 128x256 tile */
+  B2G_PATH_TC_1CTA = 1,   /* tcgen05 kernel, one CTA per 128x256 or 128x128 tile */
   B2G_PATH_TC_2CTA = 2,   /* tcgen05 kernel, CTA pair per 256x256 or 256x512 tile (cta_group::2) */
   B2G_PATH_GENERIC = 3,   /* generic CUDA kernel (layouts outside TMA's rules) */
   B2G_PATH_ZERO = 4,      /* K == 0: C filled with zeros */
@@ -225,7 +225,8 @@ int b2g_device_status(int clear);
  *   "raster_group" strip height of the persistent tile order (0 = default)
  *   "timeout_ns"   limit of every bounded device-side wait (default 2e9)
  *   "force_generic" 1 = run the generic kernel for every call (testing)
- *   "tile_n"       0 = choose by shape (default), 256 or 512 columns per CTA-pair tile
+ *   "tile_n"       0 = choose by shape (default); 128 (one CTA, 128x128 tiles), 256 or 512
+ *                  columns per tile (512 needs CTA pairs)
  *   "split_k"      0 = choose by shape (default), else split every tile's K this many ways
  *   "tail_split"   1 (default) = split only the tiles of a partial last wave; 0 = never
  *   "serial_fixup" 1 = split-K partials are always summed by the last unit to arrive

@@ -130,8 +130,8 @@ static CUresult encode_cached(CUtensorMap* out, CUtensorMapDataType dt, cuuint32
 struct DevState {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
-  bool attr_set[2][3][2][2] = {};  // [fp8][variant][b_kmajor][c_mcontig]
-  int max_clusters[2][3][2][2] = {};
+  bool attr_set[2][4][2][2] = {};  // [fp8][variant][b_kmajor][c_mcontig]
+  int max_clusters[2][4][2][2] = {};
 };
 static std::mutex g_dev_mu;
 static DevState g_dev[64];
@@ -301,6 +301,60 @@ static int noalloc_scratch(FixedScratch* out) {
   out->ptr = addr[dev];
   out->bytes = kNoAllocScratchBytes;
   return B2G_OK;
+}
+
+// ------------------------------------------------------------------ split-K counters
+// Arrival counters of split tiles come from a per-device ring in a file-scope device array
+// (zero at module load).  Every kernel returns the counters it used to zero (the last unit of
+// each split tile resets its counter), so a call needs no memset: it takes the next range of
+// the ring.  A kernel that gave up on a bounded wait may leave counters non-zero; clearing the
+// device error (b2g_device_status(1)) marks the ring for one full reset before its next use.
+// Calls captured into a CUDA graph do not use the ring (a graph replays fixed addresses long
+// after the ring has moved on); they zero their counters with a memset node instead.
+constexpr size_t kCounterSlots = (size_t)1 << 20;  // 4 MiB of ints per device
+static __device__ int g_split_counters[kCounterSlots];
+
+struct CounterRing {
+  int* base = nullptr;
+  size_t next = 0;
+  bool dirty = false;
+};
+static std::mutex g_ring_mu;
+static CounterRing g_ring[64];
+
+// `n` zeroed counters on the current device, or nullptr when `n` is too large for the ring.
+static int ring_counters(size_t n, cudaStream_t stream, int** out) {
+  *out = nullptr;
+  if (n == 0 || n > kCounterSlots / 8) return B2G_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(B2G_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_ring_mu);
+  CounterRing& r = g_ring[dev];
+  if (!r.base) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_split_counters);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(split-K counters)");
+    r.base = static_cast<int*>(p);
+  }
+  if (r.dirty) {
+    e = cudaMemsetAsync(r.base, 0, kCounterSlots * sizeof(int), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split-K counter ring)");
+    r.dirty = false;
+  }
+  const size_t m = (n + 63) / 64 * 64;  // 256-byte granules
+  if (r.next + m > kCounterSlots) r.next = 0;
+  *out = r.base + r.next;
+  r.next += m;
+  return B2G_OK;
+}
+
+static void ring_mark_dirty() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return;
+  std::lock_guard<std::mutex> lk(g_ring_mu);
+  g_ring[dev].dirty = true;
 }
 
 // ------------------------------------------------------------------ planning
@@ -519,19 +573,30 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   const int num_m_tiles_a = (int)((asz + ba - 1) / ba);
   const int64_t nmt64 = (int64_t)num_m_tiles_i * num_m_tiles_b * num_m_tiles_a;
   int cg = (int)opt_cta_group.load();
-  if (cg != 1 && cg != 2) cg = (nmt64 >= 2) ? 2 : 1;
   int bn = (int)opt_tile_n.load();
-  if (bn != 256 && bn != 512) {
+  if (bn == 128) cg = 1;  // the 128-column tile exists for one CTA only
+  if (cg != 1 && cg != 2) {
+    // Small problems (fewer 128x256 tiles than SMs) take 128x128 tiles: four times as many
+    // tiles as the pair tile, so more SMs share the work.
+    if (bn == 0 && nmt64 * ((N + 255) / 256) < ds->sm_count) {
+      cg = 1;
+      bn = 128;
+    } else {
+      cg = (nmt64 >= 2) ? 2 : 1;
+    }
+  }
+  if (bn != 128 && bn != 256 && bn != 512) {
     // 512-wide pair tiles pull a quarter fewer operand bytes from L2 per FLOP; use them when
     // there are enough of them to fill every CTA pair at least twice.
     const int64_t pairs = std::max(1, ds->sm_count / 2);
     const int64_t t512 = ((nmt64 + 1) / 2) * ((N + 511) / 512);
     bn = (cg == 2 && t512 >= 2 * pairs) ? 512 : 256;
   }
-  if (cg == 1) bn = 256;  // one CTA: 256 columns (TMEM holds two accumulators)
+  if (cg == 1 && bn == 512) bn = 256;  // one CTA: at most 256 columns (two accumulators)
+  if (cg == 2 && bn == 128) bn = 256;
   const int64_t nnt64 = (N + bn - 1) / bn;
   if (nmt64 * nnt64 > INT32_MAX / 4) return launch_generic(B2G_PATH_GENERIC);
-  const int bph = 256 / cg;  // B columns of one N-half held by one CTA
+  const int bph = std::min(bn, 256) / cg;  // B columns of one N-half held by one CTA
   // B
   if (b_mn) {  // dims (n, k, j)
     cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)ksz, (cuuint64_t)jsz};
@@ -605,22 +670,26 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   // ---- launch
   using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
   const int bk = b_k ? 1 : 0, cm = c_m ? 1 : 0;
-  const int variant = cg == 1 ? 0 : (bn == 256 ? 1 : 2);
-  static const KernFn table[2][3][2][2] = {
+  const int variant = cg == 1 ? (bn == 128 ? 3 : 0) : (bn == 256 ? 1 : 2);
+  static const KernFn table[2][4][2][2] = {
       {{{gemm_tc_kernel<1, 256, false, false, 2>, gemm_tc_kernel<1, 256, false, true, 2>},
         {gemm_tc_kernel<1, 256, true, false, 2>, gemm_tc_kernel<1, 256, true, true, 2>}},
        {{gemm_tc_kernel<2, 256, false, false, 2>, gemm_tc_kernel<2, 256, false, true, 2>},
         {gemm_tc_kernel<2, 256, true, false, 2>, gemm_tc_kernel<2, 256, true, true, 2>}},
        {{gemm_tc_kernel<2, 512, false, false, 2>, gemm_tc_kernel<2, 512, false, true, 2>},
-        {gemm_tc_kernel<2, 512, true, false, 2>, gemm_tc_kernel<2, 512, true, true, 2>}}},
+        {gemm_tc_kernel<2, 512, true, false, 2>, gemm_tc_kernel<2, 512, true, true, 2>}},
+       {{gemm_tc_kernel<1, 128, false, false, 2>, gemm_tc_kernel<1, 128, false, true, 2>},
+        {gemm_tc_kernel<1, 128, true, false, 2>, gemm_tc_kernel<1, 128, true, true, 2>}}},
       {{{gemm_tc_kernel<1, 256, false, false, 1>, gemm_tc_kernel<1, 256, false, true, 1>},
         {gemm_tc_kernel<1, 256, true, false, 1>, gemm_tc_kernel<1, 256, true, true, 1>}},
        {{gemm_tc_kernel<2, 256, false, false, 1>, gemm_tc_kernel<2, 256, false, true, 1>},
         {gemm_tc_kernel<2, 256, true, false, 1>, gemm_tc_kernel<2, 256, true, true, 1>}},
        {{gemm_tc_kernel<2, 512, false, false, 1>, gemm_tc_kernel<2, 512, false, true, 1>},
-        {gemm_tc_kernel<2, 512, true, false, 1>, gemm_tc_kernel<2, 512, true, true, 1>}}}};
-  static const uint32_t smem_of[3] = {Cfg<1, 256>::SMEM_BYTES, Cfg<2, 256>::SMEM_BYTES,
-                                      Cfg<2, 512>::SMEM_BYTES};
+        {gemm_tc_kernel<2, 512, true, false, 1>, gemm_tc_kernel<2, 512, true, true, 1>}},
+       {{gemm_tc_kernel<1, 128, false, false, 1>, gemm_tc_kernel<1, 128, false, true, 1>},
+        {gemm_tc_kernel<1, 128, true, false, 1>, gemm_tc_kernel<1, 128, true, true, 1>}}}};
+  static const uint32_t smem_of[4] = {Cfg<1, 256>::SMEM_BYTES, Cfg<2, 256>::SMEM_BYTES,
+                                      Cfg<2, 512>::SMEM_BYTES, Cfg<1, 128>::SMEM_BYTES};
   const int e8 = esz == 1 ? 1 : 0;
   KernFn kern = table[e8][variant][bk][cm];
   const uint32_t smem = smem_of[variant];
@@ -693,33 +762,51 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.counters = nullptr;
   void* scratch = nullptr;
   const size_t split_tiles = (size_t)(p.num_tiles - p.num_full);
+  int* ring = nullptr;  // counters from the ring: no memset
+  if (p.k_splits > 1) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+    if (cap == cudaStreamCaptureStatusNone) {
+      int rrc = ring_counters(split_tiles * cg, stream, &ring);
+      if (rrc != B2G_OK) return rrc;
+    }
+  }
   if (p.k_splits > 1 && fixed) {
     // caller-supplied scratch (b2g_gemm_f16_f32_noalloc): no allocation
     const size_t ws_bytes = split_tiles * p.k_splits * cg * 128 * bn * sizeof(float);
-    const size_t ctr_bytes = (split_tiles * cg * sizeof(int) + 255) / 256 * 256;
+    const size_t ctr_bytes = ring ? 0 : (split_tiles * cg * sizeof(int) + 255) / 256 * 256;
     if (ctr_bytes + ws_bytes > fixed->bytes)
       return fail(B2G_ERR_INVALID_ARG,
                   "split-K scratch of %zu bytes exceeds the %zu-byte static scratch of "
                   "b2g_gemm_f16_f32_noalloc",
                   ctr_bytes + ws_bytes, fixed->bytes);
-    p.counters = static_cast<int*>(fixed->ptr);
     p.ws = reinterpret_cast<float*>(static_cast<char*>(fixed->ptr) + ctr_bytes);
-    cudaError_t e = cudaMemsetAsync(p.counters, 0, ctr_bytes, stream);  // counters start at 0
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split-K counters)");
+    if (ring) {
+      p.counters = ring;
+    } else {
+      p.counters = static_cast<int*>(fixed->ptr);
+      cudaError_t e = cudaMemsetAsync(p.counters, 0, ctr_bytes, stream);  // counters start at 0
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split-K counters)");
+    }
   } else if (p.k_splits > 1) {
     const size_t ws_bytes = split_tiles * p.k_splits * cg * 128 * bn * sizeof(float);
-    const size_t ctr_bytes = (split_tiles * cg * sizeof(int) + 255) / 256 * 256;
+    const size_t ctr_bytes = ring ? 0 : (split_tiles * cg * sizeof(int) + 255) / 256 * 256;
     cudaMemPool_t pool = nullptr;
     int prc = split_pool(&pool);
     if (prc != B2G_OK) return prc;
     cudaError_t e = cudaMallocFromPoolAsync(&scratch, ctr_bytes + ws_bytes, pool, stream);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMallocFromPoolAsync(split-K workspace)");
-    p.counters = static_cast<int*>(scratch);
     p.ws = reinterpret_cast<float*>(static_cast<char*>(scratch) + ctr_bytes);
-    e = cudaMemsetAsync(p.counters, 0, ctr_bytes, stream);
-    if (e != cudaSuccess) {
-      cudaFreeAsync(scratch, stream);
-      return cuda_fail(e, "cudaMemsetAsync(split-K counters)");
+    if (ring) {
+      p.counters = ring;
+    } else {
+      p.counters = static_cast<int*>(scratch);
+      e = cudaMemsetAsync(p.counters, 0, ctr_bytes, stream);
+      if (e != cudaSuccess) {
+        cudaFreeAsync(scratch, stream);
+        return cuda_fail(e, "cudaMemsetAsync(split-K counters)");
+      }
     }
   }
   int groups = std::min(group_cap, p.num_units);
@@ -906,6 +993,7 @@ extern "C" int b2g_device_status(int clear) {
     return -1;
   }
   if (clear) {
+    if (v != 0) ring_mark_dirty();  // a kernel that gave up may have left counters set
     const int z = 0;
     e = cudaMemcpyToSymbol(g_device_error, &z, sizeof(int));
     if (e != cudaSuccess) {
@@ -941,7 +1029,7 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
   } else if (!strcmp(key, "store_hint")) {
     opt_store_hint = value ? 1 : 0;
   } else if (!strcmp(key, "tile_n")) {
-    if (value != 0 && value != 256 && value != 512) return B2G_ERR_INVALID_ARG;
+    if (value != 0 && value != 128 && value != 256 && value != 512) return B2G_ERR_INVALID_ARG;
     opt_tile_n = value;
   } else {
     return B2G_ERR_INVALID_ARG;

@@ -54,7 +54,7 @@ struct GemmParams {
   int num_m_tiles;             // 128-row tiles
   int num_pm_tiles;            // tiles of 128*CG rows (one per CTA group)
   int n_size;                  // N extent
-  int num_n_tiles;             // 256-column tiles
+  int num_n_tiles;             // BN-column tiles
   int k_blocks_per_j;          // ceil(k / 64)
   int k_iters;                 // j * k_blocks_per_j
   int num_tiles;               // num_pm_tiles * num_n_tiles
@@ -93,17 +93,19 @@ constexpr uint32_t kTmemCols = 512;      // all of TMEM
 constexpr uint32_t kCBuf = 32 * 32 * 4;  // one 32x32 fp32 staging buffer
 constexpr uint32_t kSmemLimit = 232448;  // max dynamic shared memory per CTA on sm_100
 
-// CG: CTAs per tile (1, or 2 = cta_group::2 pair).  BN: tile width in columns (256 or 512);
-// a tile is (128*CG) x BN.  BN = 256 keeps two accumulators in TMEM (the epilogue of tile t
-// overlaps the main loop of tile t+1); BN = 512 fills TMEM with one accumulator and cuts the
-// operand bytes each CTA pulls from L2 per FLOP by a quarter.
+// CG: CTAs per tile (1, or 2 = cta_group::2 pair).  BN: tile width in columns (128, 256 or
+// 512); a tile is (128*CG) x BN.  BN <= 256 keeps two accumulators in TMEM (the epilogue of
+// tile t overlaps the main loop of tile t+1); BN = 512 fills TMEM with one accumulator and cuts
+// the operand bytes each CTA pulls from L2 per FLOP by a quarter; BN = 128 (one CTA only)
+// gives small problems four times as many tiles as the 256x512 pair tile.
 template <int CG, int BN>
 struct Cfg {
   static_assert(CG == 1 || CG == 2, "CTA group");
-  static_assert(BN == 256 || BN == 512, "tile width");
-  static constexpr int NH = BN / kUN;                 // UMMA N-halves per k step
-  static constexpr int ACC_BUFS = BN == 256 ? 2 : 1;  // accumulators held in TMEM
-  static constexpr int BPH = kUN / CG;                // B columns per N-half held by one CTA
+  static_assert(BN == 256 || BN == 512 || (BN == 128 && CG == 1), "tile width");
+  static constexpr int UN = BN < kUN ? BN : kUN;      // N of one UMMA instruction
+  static constexpr int NH = BN / UN;                  // UMMA N-halves per k step
+  static constexpr int ACC_BUFS = BN <= 256 ? 2 : 1;  // accumulators held in TMEM
+  static constexpr int BPH = UN / CG;                 // B columns per N-half held by one CTA
   static constexpr int BN_CTA = BN / CG;              // B columns loaded per CTA
   static constexpr uint32_t A_BYTES = kBM * kRowBytes;  // 16 KiB
   static constexpr uint32_t B_BYTES = BN_CTA * kRowBytes;
@@ -127,6 +129,7 @@ struct Cfg {
 static_assert(Cfg<1, 256>::SMEM_BYTES <= kSmemLimit && Cfg<1, 256>::STAGES >= 4, "CG=1 budget");
 static_assert(Cfg<2, 256>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256>::STAGES >= 6, "CG=2 budget");
 static_assert(Cfg<2, 512>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512>::STAGES >= 4, "BN=512 budget");
+static_assert(Cfg<1, 128>::SMEM_BYTES <= kSmemLimit && Cfg<1, 128>::STAGES >= 6, "BN=128 budget");
 
 // Instruction descriptor (kind::f16 and kind::f8f6f4 share the layout): D fp32 (bit 4), A and
 // B format at bits 7 and 10 (kind::f16: 0 = F16, 1 = BF16; kind::f8f6f4: 0 = E4M3,
@@ -231,11 +234,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int group_id = blockIdx.x / CG;
   const int num_groups = gridDim.x / CG;
 
-  // B columns of N-half h held by this CTA start at n0 + h*256 + cta_rank*BPH.
+  // B columns of N-half h held by this CTA start at n0 + h*UN + cta_rank*BPH.
   auto issue_b = [&](uint32_t sb, uint32_t fb, int n0, int kc, int jj) {
 #pragma unroll
     for (int h = 0; h < C::NH; ++h) {
-      const int nh = n0 + h * kUN + (int)cta_rank * C::BPH;
+      const int nh = n0 + h * C::UN + (int)cta_rank * C::BPH;
       const uint32_t dst = sb + (uint32_t)h * C::HALF_BYTES;
       if constexpr (B_KMAJOR) {
         ptx::tma_load_3d<CG>(dst, &tmB, fb, kc, jj, nh);
@@ -294,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
-      const uint32_t idesc = make_idesc(kBM * CG, kUN, !B_KMAJOR, (uint32_t)p.ab_format);
+      const uint32_t idesc = make_idesc(kBM * CG, C::UN, !B_KMAJOR, (uint32_t)p.ab_format);
       int it = 0, tc = 0;
       bool ok = true;
       // Issue the MMAs of K block kb from stage s into N-halves [h_lo, h_hi).
@@ -310,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t bh = sb + (uint32_t)h * C::HALF_BYTES;
             const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(bh + 32u * k16, 16u, 1024u)
                                          : ptx::smem_desc_sw128(bh + MN_STEP * k16, ATOM_BYTES, 1024u);
-            ptx::umma<CG, ESZ>(d + (uint32_t)h * kUN, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
+            ptx::umma<CG, ESZ>(d + (uint32_t)h * C::UN, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
           }
         }
       };
@@ -318,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int t, sp, ns, kb_lo, kb_hi;
         unit_info(p, u, t, sp, ns, kb_lo, kb_hi);
         const int nkb = kb_hi - kb_lo;
-        // BN = 256: two accumulators, tempty[acc] guards accumulator acc.
+        // BN <= 256: two accumulators, tempty[acc] guards accumulator acc.
         // BN = 512: one accumulator, tempty[h] guards its N-half h (the epilogue frees the
         // halves one after the other).
         const int acc = (C::ACC_BUFS == 2) ? (tc & 1) : 0;
@@ -328,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)acc * kUN;
+        const uint32_t d = tmem_base + (uint32_t)acc * C::UN;
         int kb = 0;  // K block of this unit, relative to kb_lo
         if constexpr (C::NH == 2) {
           // Half 0 of every K block already in shared memory first, then wait for half 1 of
@@ -400,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool got = ptx::mbar_wait(tfull_bar(acc), aph, abort_flag, err, ERR_WAIT_TFULL, lim);
       if (!__all_sync(0xffffffffu, got)) break;
       ptx::tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)acc * kUN;
+      const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)acc * C::UN;
       const int n0 = tn * BN;
 
       // Stage chunk `ch` (32 columns of this warp's 32 rows) and TMA-store it.
@@ -457,22 +460,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (ns > 1) {
         // ---- split-K unit: partial tile -> workspace; the last unit of the tile reduces.
-        // Workspace block of (split unit, CTA): 128 x BN floats laid out [chunk][row][32] so each
-        // warp writes and reads 4 KiB contiguous per chunk.
+        // Workspace block of (split unit, CTA): 128 x BN floats as float4 [chunk][warp][j][lane]
+        // (lane = row within the warp's 32 rows, j = columns 4j..4j+3 of the 32-column chunk),
+        // so every warp-wide store and load covers 512 contiguous bytes.
         const size_t blk = (size_t)128 * BN;
         const int v = u - p.num_full;   // split unit index
         const int st = t - p.num_full;  // split tile index
-        float* mine = p.ws + ((size_t)v * CG + cta_rank) * blk + (size_t)(32 * q + lane) * 32;
+        float4* mine = reinterpret_cast<float4*>(p.ws + ((size_t)v * CG + cta_rank) * blk) +
+                       (size_t)q * 8 * 32 + lane;
+        uint32_t w0[32], w1[32];
+        ptx::tmem_ld_32x32b_x32(tbase, w0);
 #pragma unroll 1
-        for (int ch = 0; ch < C::CHUNKS; ++ch) {
-          uint32_t v[32];
-          ptx::tmem_ld_32x32b_x32(tbase + 32u * ch, v);
+        for (int ch = 0; ch < C::CHUNKS; ch += 2) {
           ptx::tmem_ld_wait();
-          float4* dst = reinterpret_cast<float4*>(mine + (size_t)ch * 128 * 32);
+          ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 1), w1);
+          float4* d0 = mine + (size_t)ch * 4 * 8 * 32;
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
-                                 __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            __stcg(d0 + 32 * j, make_float4(__uint_as_float(w0[4 * j]), __uint_as_float(w0[4 * j + 1]),
+                                            __uint_as_float(w0[4 * j + 2]), __uint_as_float(w0[4 * j + 3])));
+          ptx::tmem_ld_wait();
+          if (ch + 2 < C::CHUNKS) ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 2), w0);
+          float4* d1 = mine + (size_t)(ch + 1) * 4 * 8 * 32;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            __stcg(d1 + 32 * j, make_float4(__uint_as_float(w1[4 * j]), __uint_as_float(w1[4 * j + 1]),
+                                            __uint_as_float(w1[4 * j + 2]), __uint_as_float(w1[4 * j + 3])));
         }
         if constexpr (C::ACC_BUFS == 2) {
           release(acc);
@@ -480,7 +493,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           release(0);
           release(1);
         }
-        __threadfence();
+        // One thread publishes the partial: the barrier orders the epilogue threads' stores
+        // before its acq_rel (gpu scope) atomic, and its acquire, followed by the second
+        // barrier, orders the siblings' partials before every thread's loads below.
         ptx::named_barrier_sync(1, kEpiWarps * 32);
         volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
         int* ctr = p.counters + (size_t)st * CG + cta_rank;
@@ -488,49 +503,74 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.fixup_parallel) {
           // publish this partial, then wait until every split of the tile has published
           if (threadIdx.x == 64) {
-            atomicAdd(ctr, 1);
+            ptx::atom_add_acq_rel_gpu(ctr, 1);
             *last_flag = ptx::wait_counter_ge(ctr, ns, abort_flag, err, ERR_WAIT_FIXUP, lim) ? 1 : 0;
           }
           ch_first = sp;  // this unit reduces chunks sp, sp + ns, ...
           ch_step = ns;
         } else if (threadIdx.x == 64) {
-          const int old = atomicAdd(ctr, 1);
+          const int old = ptx::atom_add_acq_rel_gpu(ctr, 1);
           const int last = old == p.k_splits - 1;
           if (last) *ctr = 0;  // every split has arrived: ready for the next call
           *last_flag = last;
         }
         ptx::named_barrier_sync(1, kEpiWarps * 32);
         if (*last_flag) {
-          __threadfence();
-          const float* base_t = p.ws + ((size_t)st * p.k_splits * CG + cta_rank) * blk +
-                                (size_t)(32 * q + lane) * 32;
+          const float4* tile4 = reinterpret_cast<const float4*>(
+                                    p.ws + ((size_t)st * p.k_splits * CG + cta_rank) * blk) +
+                                (size_t)q * 8 * 32 + lane;
+          const size_t split_stride = (size_t)CG * blk / 4;  // float4s between splits
 #pragma unroll 1
           for (int ch = ch_first; ch < C::CHUNKS; ch += ch_step) {
+            const float4* src = tile4 + (size_t)ch * 4 * 8 * 32;
             float a[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) a[j] = 0.0f;
-            for (int sp = 0; sp < p.k_splits; ++sp) {  // fixed order: deterministic sums
-              const float4* src = reinterpret_cast<const float4*>(
-                  base_t + (size_t)sp * CG * blk + (size_t)ch * 128 * 32);
+            // Partials are summed in split order (deterministic); two splits' loads are in
+            // flight at a time.
+            int sp = 0;
+#pragma unroll 1
+            for (; sp + 1 < p.k_splits; sp += 2) {
+              float4 x[8], y[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) x[j] = __ldcg(src + sp * split_stride + 32 * j);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) y[j] = __ldcg(src + (sp + 1) * split_stride + 32 * j);
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
-                const float4 x = __ldcg(src + j);
+                a[4 * j] += x[j].x;
+                a[4 * j + 1] += x[j].y;
+                a[4 * j + 2] += x[j].z;
+                a[4 * j + 3] += x[j].w;
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                a[4 * j] += y[j].x;
+                a[4 * j + 1] += y[j].y;
+                a[4 * j + 2] += y[j].z;
+                a[4 * j + 3] += y[j].w;
+              }
+            }
+            if (sp < p.k_splits) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 x = __ldcg(src + sp * split_stride + 32 * j);
                 a[4 * j] += x.x;
                 a[4 * j + 1] += x.y;
                 a[4 * j + 2] += x.z;
                 a[4 * j + 3] += x.w;
               }
             }
-            uint32_t v[32];
+            uint32_t vv[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(a[j]);
-            store_chunk(v, ch);
+            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(a[j]);
+            store_chunk(vv, ch);
           }
         }
         ptx::named_barrier_sync(1, kEpiWarps * 32);
         if (p.fixup_parallel && threadIdx.x == 64) {
           // done reading the partials; the last split to get here resets the counter
-          if (atomicAdd(ctr, 1) == 2 * ns - 1) *ctr = 0;
+          if (ptx::atom_add_acq_rel_gpu(ctr, 1) == 2 * ns - 1) *ctr = 0;
         }
         continue;
       }
@@ -544,8 +584,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 1), v1);
         store_chunk(v0, ch);
         ptx::tmem_ld_wait();
-        if ((ch + 1) % 8 == 7) {
-          // An N-half (BN = 512) or the whole accumulator (BN = 256) has been read: hand it
+        if ((ch + 2) % 8 == 0 || ch + 2 >= C::CHUNKS) {
+          // An N-half (BN = 512) or the whole accumulator (BN <= 256) has been read: hand it
           // back to the MMA warp.
           release(C::ACC_BUFS == 2 ? acc : (ch + 1) / 8);
         }

@@ -132,6 +132,13 @@ __device__ __forceinline__ bool wait_counter_ge(const int* ctr, int target, vola
   }
 }
 
+// Atomic add with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ void spin_ns(uint64_t ns) {
   const uint64_t t0 = globaltimer();
   while (globaltimer() - t0 < ns) {

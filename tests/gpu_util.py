@@ -29,8 +29,8 @@ def assert_close(orc, got, ref, K, max_a=1.0, max_b=1.0, what=""):
 
 
 # kernel variants of the tensor-core path: (CTAs per tile, tile width)
-VARIANTS = [(1, 256), (2, 256), (2, 512)]
-VARIANT_IDS = ["cta1_n256", "cta2_n256", "cta2_n512"]
+VARIANTS = [(1, 128), (1, 256), (2, 256), (2, 512)]
+VARIANT_IDS = ["cta1_n128", "cta1_n256", "cta2_n256", "cta2_n512"]
 
 
 @contextlib.contextmanager

@@ -141,3 +141,36 @@ def test_tail_split_contraction_shape(b2g, cuda, orc):
     for r in (0, 4095, 6000, 7935, 8191):
         a = orc.uniform_f16((1, K), 1, r * K)
         assert_close(orc, res[1][r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, what="row %d" % r)
+
+
+def test_split_k_counters_after_timeout_and_many_calls(b2g, cuda, orc):
+    """Split-K arrival counters come from a per-device ring that every kernel leaves at zero.
+    A split call whose waits run out (host-side fault injection: the producer issues no loads)
+    is reported; clearing the error marks the ring for a full reset, and the following calls --
+    many of them, each on a fresh range of the ring -- are correct and bit-identical."""
+    torch = cuda
+    b2g.device_status(clear=True)
+    M, N, K = 256, 512, 4096
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+    dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+    b2g.fill_uniform(dA, M * K, 91)
+    b2g.fill_uniform(dB, K * N, 92)
+    dC = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    with options(b2g, fault_flags=1, timeout_ns=200_000_000, cta_group=1, tile_n=128, split_k=2):
+        b2g.gemm(dA, dB, dC, M, N, K)
+        code = b2g.device_status(clear=True)
+    assert code in (2, 3, 4, 6), code
+    first = None
+    with options(b2g, cta_group=1, tile_n=128, split_k=4):
+        for _ in range(300):
+            dC.fill_(float("nan"))
+            b2g.gemm(dA, dB, dC, M, N, K)
+            if first is None:
+                torch.cuda.synchronize()
+                first = dC.clone()
+        torch.cuda.synchronize()
+    assert b2g.device_status() == 0
+    assert torch.equal(first, dC)
+    A = orc.uniform_f16((M, K), 91)
+    B = orc.uniform_f16((K, N), 92)
+    assert_close(orc, dC.cpu().numpy(), orc.gemm_f64(A, B), K)
