@@ -53,15 +53,29 @@ def measured_peaks():
         return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profiled_traffic():
-    """dram bytes per launch of the top kernel from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "gemm_tc_kernel_8192.md")
+def profiled_traffic(M, N, K, dtype="f16"):
+    """DRAM bytes per launch of the top kernel from a committed ncu summary of this exact shape
+    and operand type (`shape: M,N,K` and `traffic_bytes_per_launch:` lines), if any."""
+    d = os.path.join(ROOT, "profiles")
     try:
-        for line in open(p):
-            if line.startswith("traffic_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].strip())
+        names = sorted(f for f in os.listdir(d) if f.endswith(".md"))
     except OSError:
-        pass
+        return None
+    for f in names:
+        shape = traffic = None
+        dt = "f16"
+        try:
+            for line in open(os.path.join(d, f)):
+                if line.startswith("shape:"):
+                    shape = tuple(int(x) for x in line.split(":", 1)[1].strip().split(","))
+                elif line.startswith("dtype:"):
+                    dt = line.split(":", 1)[1].strip()
+                elif line.startswith("traffic_bytes_per_launch:"):
+                    traffic = float(line.split(":", 1)[1].strip())
+        except (OSError, ValueError):
+            continue
+        if shape == (M, N, K) and dt == dtype and traffic is not None:
+            return traffic
     return None
 
 
@@ -326,8 +340,8 @@ def main():
     cublas = None
     if not args.kernel_only:
         e2e = e2e_run(torch, b2g, dev, M, N, K, rank, ws, args.e2e_steps, dist if ws > 1 else None)
-        if rank == 0 and ws == 1 and not args.no_cublas:
-            cublas = cublas_side_by_side(torch, dA, dB, dC, local, min(args.steps, 1000))
+    if rank == 0 and ws == 1 and not args.no_cublas and dt == 0 and (args.shape or not args.kernel_only):
+        cublas = cublas_side_by_side(torch, dA, dB, dC, local, min(args.steps, 1000))
 
     peaks, peaks_src = measured_peaks()
     # a loop of back-to-back launches longer than ~0.25 s runs under the power cap: compare with
@@ -338,6 +352,28 @@ def main():
     if dt >= 2:  # fp8 tensor rate is twice fp16/bf16 (nominal 4.5 vs 2.25 PFLOP/s dense)
         peak *= 2.0
         peak_note = " x2 (fp8 = 2x the measured 16-bit rate)"
+    # Roofline of the kernel: tensor-bound unless the shape's arithmetic intensity is below the
+    # ridge of the measured peaks (then HBM-bound, achieved = algorithmic bytes / launch time).
+    esz = 2 if dt < 2 else 1
+    alg_bytes = float(esz * M * K + esz * K * N + 4 * M * N)
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    ridge = peak * 1e12 / (hbm * 1e9)
+    if flops / alg_bytes < ridge:
+        roofline = {"bound": "hbm", "achieved": alg_bytes / (avg_launch_ms * 1e-3) / 1e9,
+                    "peak": hbm, "unit": "GB/s",
+                    "frac": alg_bytes / (avg_launch_ms * 1e-3) / 1e9 / hbm,
+                    "traffic": profiled_traffic(M, N, K, args.dtype),
+                    "peak_source": "%s hbm_gbs" % peaks_src,
+                    "bytes_per_launch": alg_bytes, "flops_per_launch": flops,
+                    "avg_launch_ms": avg_launch_ms, "tensor_tflops": achieved}
+    else:
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": profiled_traffic(M, N, K, args.dtype),
+                    "peak_source": "%s %s%s" % (peaks_src, "bf16_tflops_sustained" if sustained
+                                                else "bf16_tflops", peak_note),
+                    "flops_per_launch": flops, "bytes_per_launch": alg_bytes,
+                    "avg_launch_ms": avg_launch_ms}
+    roofline["kernel"] = "gemm_tc_kernel"
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and not args.kernel_only:
         v, rows, secs, thr = cpu_baseline(args.cpu_seconds)
@@ -379,12 +415,7 @@ def main():
                 "< : steps may hit L2"),
             "frac_of_spec_2250": value / ws / SPEC_TFLOPS,
         },
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": profiled_traffic(),
-                     "peak_source": "%s %s%s" % (peaks_src, "bf16_tflops_sustained" if sustained
-                                                 else "bf16_tflops", peak_note),
-                     "kernel": "gemm_tc_kernel", "flops_per_launch": flops,
-                     "avg_launch_ms": avg_launch_ms},
+        "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "cublas_side_by_side": cublas,

@@ -231,6 +231,8 @@ int b2g_device_status(int clear);
  *   "tail_split"   1 (default) = split only the tiles of a partial last wave; 0 = never
  *   "serial_fixup" 1 = split-K partials are always summed by the last unit to arrive
  *   "store_hint"   1 = C stores carry an L2 evict-first hint
+ *   "pdl"          1 (default) = tensor-core launches use programmatic dependent launch (the
+ *                  kernel's set-up overlaps the previous kernel in the stream); 0 = plain launch
  *   "fault_flags"  test-only fault injection: bit 0 = the TMA producer issues no loads,
  *                  so the MMA wait runs out and the call reports B2G_ERR_TIMEOUT
  * Returns B2G_OK or B2G_ERR_INVALID_ARG for an unknown key or value.  Options are

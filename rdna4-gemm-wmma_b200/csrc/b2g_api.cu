@@ -57,6 +57,7 @@ static std::atomic<int64_t> opt_tile_n{0};  // 0 = choose by shape, else 256 or 
 static std::atomic<int64_t> opt_store_hint{0};
 static std::atomic<int64_t> opt_split_k{0};  // 0 = choose by shape, else the split count
 static std::atomic<int64_t> opt_tail_split{1};  // split the tail wave's tiles (auto mode)
+static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream serialization
 static std::atomic<int64_t> opt_serial_fixup{0};  // 1 = always the last-arriver fix-up
 
 // ------------------------------------------------------------------ driver entry point
@@ -819,18 +820,26 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
                          : 0;
 
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.gridDim = dim3((unsigned)(groups * cg), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 0;
   if (cg == 2) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+    attr[cfg.numAttrs].val.clusterDim.x = 2;
+    attr[cfg.numAttrs].val.clusterDim.y = 1;
+    attr[cfg.numAttrs].val.clusterDim.z = 1;
+    ++cfg.numAttrs;
+  }
+  if (opt_pdl.load()) {
+    // programmatic dependent launch: the kernel's set-up overlaps the previous kernel's tail
+    // (the kernel waits with griddepcontrol.wait before it touches global memory)
+    attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
+    ++cfg.numAttrs;
   }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
   if (scratch) cudaFreeAsync(scratch, stream);  // stream-ordered: freed after the kernel
@@ -1021,6 +1030,8 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_fault_flags = value;
   } else if (!strcmp(key, "serial_fixup")) {
     opt_serial_fixup = value ? 1 : 0;
+  } else if (!strcmp(key, "pdl")) {
+    opt_pdl = value ? 1 : 0;
   } else if (!strcmp(key, "tail_split")) {
     opt_tail_split = value ? 1 : 0;
   } else if (!strcmp(key, "split_k")) {
@@ -1048,6 +1059,7 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "store_hint")) return opt_store_hint;
   if (!strcmp(key, "split_k")) return opt_split_k;
   if (!strcmp(key, "tail_split")) return opt_tail_split;
+  if (!strcmp(key, "pdl")) return opt_pdl;
   if (!strcmp(key, "serial_fixup")) return opt_serial_fixup;
   return -1;
 }

@@ -230,6 +230,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   if constexpr (CG == 2) ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(smem + C::OFF_MISC);
+  // Launched with programmatic stream serialization: everything above (barrier set-up, TMEM
+  // allocation, descriptor prefetch) may overlap the tail of the previous kernel in the stream;
+  // no global memory is touched before the wait below, which returns once that kernel has
+  // completed.  The next kernel may start its own set-up as soon as this one is running.
+  ptx::grid_launch_dependents();
+  ptx::grid_dependency_wait();
 
   const int group_id = blockIdx.x / CG;
   const int num_groups = gridDim.x / CG;

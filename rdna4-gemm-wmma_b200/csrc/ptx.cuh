@@ -132,6 +132,15 @@ __device__ __forceinline__ bool wait_counter_ge(const int* ctr, int target, vola
   }
 }
 
+// Programmatic dependent launch: let the next kernel of the stream start its set-up, and wait
+// until every prerequisite grid has completed and its memory operations are visible.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Atomic add with acquire-release semantics at GPU scope; returns the old value.
 __device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
   int old;

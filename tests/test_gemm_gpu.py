@@ -185,3 +185,28 @@ def test_gemm_c_larger_than_4gib(b2g, cuda, orc):
         assert_close(orc, dC[r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, what="row %d" % r)
     del dC
     torch.cuda.empty_cache()
+
+
+def test_back_to_back_launches_with_and_without_pdl(b2g, cuda, orc):
+    """Programmatic dependent launch (the default): each call of a chain C += A.B (beta = 1,
+    the epilogue's TMA reduce-add reads C) depends on the C of the call just before it, launched
+    right behind it.  The kernel waits on that dependency before it touches global memory, so
+    the chain gives the same bits with and without PDL, and 5*A.B within tolerance."""
+    torch = cuda
+    M, N, K = 512, 768, 1024
+    A = orc.uniform_f16((M, K), 31)
+    B = orc.uniform_f16((K, N), 32)
+    dA = torch.from_numpy(A.view(np.int16)).view(torch.float16).cuda()
+    dB = torch.from_numpy(B.view(np.int16)).view(torch.float16).cuda()
+    outs = {}
+    for pdl in (1, 0):
+        with options(b2g, pdl=pdl):
+            dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+            b2g.gemm(dA, dB, dC, M, N, K)
+            for _ in range(4):
+                b2g.gemm_ex(dA, dB, dC, M, N, K, 1.0, 1.0)
+            torch.cuda.synchronize()
+            outs[pdl] = dC.clone()
+    assert b2g.device_status() == 0
+    assert torch.equal(outs[0], outs[1])
+    assert_close(orc, outs[1].cpu().numpy(), 5.0 * orc.gemm_f64(A, B), K, 5.0, 1.0)
