@@ -231,6 +231,10 @@ int b2g_device_status(int clear);
  *   "tail_split"   1 (default) = split only the tiles of a partial last wave; 0 = never
  *   "serial_fixup" 1 = split-K partials are always summed by the last unit to arrive
  *   "store_hint"   1 = C stores carry an L2 evict-first hint
+ *   "cluster_fixup" 1 (default) = when every tile of a one-CTA-tile launch is split in K (at
+ *                  most 8 ways, one unit per CTA), the splits of a tile run as one thread-block
+ *                  cluster and reduce their partials through distributed shared memory; 0 = the
+ *                  partials go through a global workspace
  *   "pdl"          1 (default) = tensor-core launches use programmatic dependent launch (the
  *                  kernel's set-up overlaps the previous kernel in the stream); 0 = plain launch
  *   "fault_flags"  test-only fault injection: bit 0 = the TMA producer issues no loads,

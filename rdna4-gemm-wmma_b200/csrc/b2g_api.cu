@@ -58,6 +58,7 @@ static std::atomic<int64_t> opt_store_hint{0};
 static std::atomic<int64_t> opt_split_k{0};  // 0 = choose by shape, else the split count
 static std::atomic<int64_t> opt_tail_split{1};  // split the tail wave's tiles (auto mode)
 static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream serialization
+static std::atomic<int64_t> opt_cluster_fixup{1};  // split-K fix-up through distributed smem
 static std::atomic<int64_t> opt_serial_fixup{0};  // 1 = always the last-arriver fix-up
 
 // ------------------------------------------------------------------ driver entry point
@@ -133,6 +134,7 @@ struct DevState {
   int cc_major = 0, cc_minor = 0;
   bool attr_set[2][4][2][2] = {};  // [fp8][variant][b_kmajor][c_mcontig]
   int max_clusters[2][4][2][2] = {};
+  int max_clusters_cg1[2][4][2][2][9] = {};  // one-CTA tiles launched in clusters of s (cluster fix-up)
 };
 static std::mutex g_dev_mu;
 static DevState g_dev[64];
@@ -761,10 +763,42 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.num_units = full + (p.num_tiles - full) * p.k_splits;
   p.ws = nullptr;
   p.counters = nullptr;
+  // Cluster fix-up: one-CTA tiles, every tile split, at most 8 splits, and one unit per CTA
+  // with every cluster resident at once (checked against the cluster occupancy).
+  p.cluster_fixup = 0;
+  if (cg == 1 && p.k_splits > 1 && p.k_splits <= 8 && p.num_full == 0 && opt_cluster_fixup.load() &&
+      !opt_serial_fixup.load()) {
+    const int S = p.k_splits;
+    int nclu = 0;
+    {
+      std::lock_guard<std::mutex> lk(g_dev_mu);
+      nclu = ds->max_clusters_cg1[e8][variant][bk][cm][S];
+      if (nclu == 0) {
+        cudaLaunchConfig_t qc = {};
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = (unsigned)S;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        qc.gridDim = dim3((unsigned)(S * (ds->sm_count / S)), 1, 1);
+        qc.blockDim = dim3(kThreads, 1, 1);
+        qc.dynamicSmemBytes = smem;
+        qc.attrs = qa;
+        qc.numAttrs = 1;
+        cudaError_t e = cudaOccupancyMaxActiveClusters(&nclu, (void*)kern, &qc);
+        if (e != cudaSuccess || nclu <= 0) {
+          cudaGetLastError();
+          nclu = -1;  // not launchable in clusters of S: never use this mode for S
+        }
+        ds->max_clusters_cg1[e8][variant][bk][cm][S] = nclu;
+      }
+    }
+    if (nclu > 0 && p.num_units <= nclu * S) p.cluster_fixup = 1;
+  }
   void* scratch = nullptr;
   const size_t split_tiles = (size_t)(p.num_tiles - p.num_full);
   int* ring = nullptr;  // counters from the ring: no memset
-  if (p.k_splits > 1) {
+  if (p.k_splits > 1 && !p.cluster_fixup) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaError_t e = cudaStreamIsCapturing(stream, &cap);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
@@ -773,7 +807,9 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
       if (rrc != B2G_OK) return rrc;
     }
   }
-  if (p.k_splits > 1 && fixed) {
+  if (p.cluster_fixup) {
+    // partials stay in shared memory: no workspace, no counters
+  } else if (p.k_splits > 1 && fixed) {
     // caller-supplied scratch (b2g_gemm_f16_f32_noalloc): no allocation
     const size_t ws_bytes = split_tiles * p.k_splits * cg * 128 * bn * sizeof(float);
     const size_t ctr_bytes = ring ? 0 : (split_tiles * cg * sizeof(int) + 255) / 256 * 256;
@@ -814,6 +850,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   if (groups < 1) groups = 1;
   // parallel fix-up only when each CTA group holds at most one split unit (all split units of
   // the launch then run at the same time, so their mutual waits always end)
+  if (p.cluster_fixup) groups = p.num_units;  // one unit per CTA, whole clusters
   p.fixup_parallel = (p.k_splits > 1 && p.num_full % groups == 0 &&
                       p.num_units - p.num_full <= groups && !opt_serial_fixup.load())
                          ? 1
@@ -827,9 +864,9 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 0;
-  if (cg == 2) {
+  if (cg == 2 || p.cluster_fixup) {
     attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
-    attr[cfg.numAttrs].val.clusterDim.x = 2;
+    attr[cfg.numAttrs].val.clusterDim.x = cg == 2 ? 2u : (unsigned)p.k_splits;
     attr[cfg.numAttrs].val.clusterDim.y = 1;
     attr[cfg.numAttrs].val.clusterDim.z = 1;
     ++cfg.numAttrs;
@@ -1032,6 +1069,8 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_serial_fixup = value ? 1 : 0;
   } else if (!strcmp(key, "pdl")) {
     opt_pdl = value ? 1 : 0;
+  } else if (!strcmp(key, "cluster_fixup")) {
+    opt_cluster_fixup = value ? 1 : 0;
   } else if (!strcmp(key, "tail_split")) {
     opt_tail_split = value ? 1 : 0;
   } else if (!strcmp(key, "split_k")) {
@@ -1060,6 +1099,7 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "split_k")) return opt_split_k;
   if (!strcmp(key, "tail_split")) return opt_tail_split;
   if (!strcmp(key, "pdl")) return opt_pdl;
+  if (!strcmp(key, "cluster_fixup")) return opt_cluster_fixup;
   if (!strcmp(key, "serial_fixup")) return opt_serial_fixup;
   return -1;
 }

@@ -79,6 +79,10 @@ struct GemmParams {
   // run at the same time; each waits (bounded) for the tile's partials and reduces 1/k_splits
   // of it.  0 = the unit that arrives last reduces the whole tile (no waiting).
   int fixup_parallel;
+  // 1 = cluster fix-up (CG = 1, num_full = 0, one unit per CTA): the k_splits splits of a tile
+  // are the CTAs of one cluster; each leaves its partial in its own shared memory and reduces
+  // 1/k_splits of the tile from all of them through distributed shared memory.  No workspace.
+  int cluster_fixup;
   int ab_format;               // UMMA operand format code (see make_idesc)
   unsigned long long timeout_ns;
   int fault_flags;             // test-only: bit 0 = producer issues no loads (forces a timeout)
@@ -111,7 +115,7 @@ struct Cfg {
   static constexpr uint32_t B_BYTES = BN_CTA * kRowBytes;
   static constexpr uint32_t HALF_BYTES = BPH * kRowBytes;  // one N-half of B in shared memory
   static constexpr uint32_t EPI_BYTES = kEpiWarps * 2 * kCBuf;
-  static constexpr int NUM_BARS_FIXED = 2 + 2 + 1;
+  static constexpr int NUM_BARS_FIXED = 2 + 2 + 1 + 1;
   static constexpr int STAGES =
       (int)((kSmemLimit - 1024 - EPI_BYTES - 256) / (A_BYTES + B_BYTES)) > 8
           ? 8
@@ -130,6 +134,9 @@ static_assert(Cfg<1, 256>::SMEM_BYTES <= kSmemLimit && Cfg<1, 256>::STAGES >= 4,
 static_assert(Cfg<2, 256>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256>::STAGES >= 6, "CG=2 budget");
 static_assert(Cfg<2, 512>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512>::STAGES >= 4, "BN=512 budget");
 static_assert(Cfg<1, 128>::SMEM_BYTES <= kSmemLimit && Cfg<1, 128>::STAGES >= 6, "BN=128 budget");
+// the cluster fix-up keeps a CTA's 128 x BN fp32 partial in its (then idle) operand stages
+static_assert(Cfg<1, 128>::OFF_C >= 128u * 128u * 4u && Cfg<1, 256>::OFF_C >= 128u * 256u * 4u,
+              "partial tile fits in the operand stages");
 
 // Instruction descriptor (kind::f16 and kind::f8f6f4 share the layout): D fp32 (bit 4), A and
 // B format at bits 7 and 10 (kind::f16: 0 = F16, 1 = BF16; kind::f8f6f4: 0 = E4M3,
@@ -197,6 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto tfull_bar = [&](int a) { return base + C::OFF_BAR + 8u * (2 * C::STAGES + a); };
   auto tempty_bar = [&](int a) { return base + C::OFF_BAR + 8u * (2 * C::STAGES + 2 + a); };
   const uint32_t mma_done_bar = base + C::OFF_BAR + 8u * (2 * C::STAGES + 4);
+  const uint32_t ready_bar = base + C::OFF_BAR + 8u * (2 * C::STAGES + 5);  // cluster fix-up
   const uint32_t tmem_slot = base + C::OFF_MISC;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   int* err = &g_device_error;
@@ -212,6 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(tempty_bar(a), kEpiWarps * CG);
     }
     ptx::mbar_init(mma_done_bar, 1);
+    ptx::mbar_init(ready_bar, p.cluster_fixup ? (uint32_t)p.k_splits : 1u);
     *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
@@ -227,7 +236,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   ptx::tc_fence_before();
   __syncthreads();
-  if constexpr (CG == 2) ptx::cluster_sync();
+  // CTA pairs, and the clusters of the cluster fix-up, start only once every CTA of the cluster
+  // has initialised its barriers (peers arrive on them remotely).
+  if (CG == 2 || p.cluster_fixup) ptx::cluster_sync();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t*>(smem + C::OFF_MISC);
   // Launched with programmatic stream serialization: everything above (barrier set-up, TMEM
@@ -464,6 +475,80 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
 
+      if (CG == 1 && ns > 1 && p.cluster_fixup) {
+        // ---- cluster fix-up: partial tile -> this CTA's shared memory (the operand stages,
+        // idle after its only unit's main loop) as float4 [chunk][warp][j][lane]; then split sp
+        // sums chunks sp, sp + ns, ... over the ns CTAs of the cluster (distributed shared
+        // memory, in split order) and stores them.  The split index is the CTA's cluster rank.
+        const uint32_t part = base + (uint32_t)(q * 8 * 32 + lane) * 16u;
+        ptx::fence_proxy_async_smem();
+        uint32_t w0[32], w1[32];
+        ptx::tmem_ld_32x32b_x32(tbase, w0);
+#pragma unroll 1
+        for (int ch = 0; ch < C::CHUNKS; ch += 2) {
+          ptx::tmem_ld_wait();
+          ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 1), w1);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            ptx::st_shared_v4(part + (uint32_t)((ch * 4 * 8 + j) * 32) * 16u, w0[4 * j],
+                              w0[4 * j + 1], w0[4 * j + 2], w0[4 * j + 3]);
+          ptx::tmem_ld_wait();
+          if (ch + 2 < C::CHUNKS) ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 2), w0);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            ptx::st_shared_v4(part + (uint32_t)(((ch + 1) * 4 * 8 + j) * 32) * 16u, w1[4 * j],
+                              w1[4 * j + 1], w1[4 * j + 2], w1[4 * j + 3]);
+        }
+        release(acc);
+        // Publish: after the epilogue warps' barrier one thread arrives (release, cluster
+        // scope) on the ready barrier of every CTA of the cluster, then waits (acquire) until
+        // all ns partials of the tile are in place.
+        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        volatile int* ready_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
+        if (threadIdx.x == 64) {
+          for (int r = 0; r < ns; ++r) ptx::mbar_arrive_cluster(ready_bar, (uint32_t)r);
+          *ready_flag = ptx::mbar_wait_cluster(ready_bar, 0u, abort_flag, err, ERR_WAIT_FIXUP, lim)
+                            ? 1 : 0;
+        }
+        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        if (*ready_flag) {
+#pragma unroll 1
+          for (int ch = sp; ch < C::CHUNKS; ch += ns) {
+            float a[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) a[j] = 0.0f;
+            // Splits in order (deterministic sums); split r+1's loads are in flight while
+            // split r is added.
+            const uint32_t off = part + (uint32_t)(ch * 4 * 8 * 32) * 16u;
+            float4 x[8], y[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              x[j] = ptx::ld_shared_cluster_v4(ptx::mapa(off, 0u) + (uint32_t)(j * 32) * 16u);
+#pragma unroll 1
+            for (int r = 0; r < ns; ++r) {
+              if (r + 1 < ns) {
+                const uint32_t src = ptx::mapa(off, (uint32_t)(r + 1));
+#pragma unroll
+                for (int j = 0; j < 8; ++j) y[j] = ptx::ld_shared_cluster_v4(src + (uint32_t)(j * 32) * 16u);
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                a[4 * j] += x[j].x;
+                a[4 * j + 1] += x[j].y;
+                a[4 * j + 2] += x[j].z;
+                a[4 * j + 3] += x[j].w;
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) x[j] = y[j];
+            }
+            uint32_t vv[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) vv[j] = __float_as_uint(a[j]);
+            store_chunk(vv, ch);
+          }
+        }
+        continue;
+      }
       if (ns > 1) {
         // ---- split-K unit: partial tile -> workspace; the last unit of the tile reduces.
         // Workspace block of (split unit, CTA): 128 x BN floats as float4 [chunk][warp][j][lane]
@@ -607,7 +692,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   ptx::tc_fence_before();
   __syncthreads();
-  if constexpr (CG == 2) {
+  if (CG == 2 || p.cluster_fixup) {
+    // no CTA of the cluster leaves (freeing its shared memory and TMEM) while a peer may
+    // still read its shared memory or signal its barriers
     __syncwarp();
     ptx::cluster_sync();
   }

@@ -98,6 +98,43 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Bounded wait with acquire semantics at cluster scope (arrivals come from other CTAs of the
+// cluster with release.cluster semantics).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
+                                                  volatile int* abort_flag, int* err, int code,
+                                                  uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer();
+  for (uint32_t n = 0;; ++n) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((n & 63u) == 63u) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > limit_ns) {
+        *abort_flag = 1;
+        atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+// 16 bytes from shared::cluster address `addr` (possibly another CTA's shared memory).
+__device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 // Teardown variant: ignores the abort flag (the copies or MMAs being waited for finish
 // on their own) and is bounded by time only.
 __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err, int code,

@@ -24,7 +24,7 @@ def test_options_roundtrip_and_validation(b2g):
     for key, val in [("cta_group", 2), ("raster_group", 4), ("timeout_ns", 123456789),
                      ("force_generic", 1), ("fault_flags", 0), ("tile_n", 512), ("tile_n", 128),
                      ("store_hint", 1), ("split_k", 3), ("tail_split", 0), ("serial_fixup", 1),
-                     ("pdl", 0)]:
+                     ("pdl", 0), ("cluster_fixup", 0)]:
         old = b2g.get_option(key)
         b2g.set_option(key, val)
         assert b2g.get_option(key) == val

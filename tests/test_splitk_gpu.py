@@ -174,3 +174,31 @@ def test_split_k_counters_after_timeout_and_many_calls(b2g, cuda, orc):
     A = orc.uniform_f16((M, K), 91)
     B = orc.uniform_f16((K, N), 92)
     assert_close(orc, dC.cpu().numpy(), orc.gemm_f64(A, B), K)
+
+
+@pytest.mark.parametrize("tn,splits,MNK", [(128, 2, (128, 8192, 2048)), (256, 4, (128, 4096, 4096)),
+                                           (128, 3, (200, 1000, 3000)), (256, 8, (256, 512, 8192)),
+                                           (128, 5, (384, 1024, 2240))])
+def test_cluster_fixup_matches_global_fixup(b2g, cuda, orc, tn, splits, MNK):
+    """The cluster fix-up (partials reduced through distributed shared memory) and the global
+    workspace fix-up sum the same partials in split order: identical bits, and correct."""
+    torch = cuda
+    M, N, K = MNK
+    r8 = lambda x: (x + 7) // 8 * 8
+    A = orc.uniform_f16((M, K), 71)
+    B = orc.uniform_f16((K, N), 72)
+    Ap = np.zeros((M, r8(K)), np.float16)
+    Ap[:, :K] = A
+    Bp = np.zeros((K, r8(N)), np.float16)
+    Bp[:, :N] = B
+    dA, dB = to_dev(torch, Ap), to_dev(torch, Bp)
+    outs = []
+    for cf in (1, 0):
+        dC = torch.full((M, r8(N)), float("nan"), dtype=torch.float32, device="cuda")
+        with options(b2g, cta_group=1, tile_n=tn, split_k=splits, cluster_fixup=cf):
+            b2g.gemm(dA, dB, dC, M, N, K, lda=r8(K), ldb=r8(N), ldc=r8(N))
+        torch.cuda.synchronize()
+        assert b2g.device_status() == 0
+        outs.append(dC[:, :N].clone())
+    assert torch.equal(outs[0], outs[1])
+    assert_close(orc, outs[0].cpu().numpy(), orc.gemm_f64(A, B), K)
