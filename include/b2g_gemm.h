@@ -171,6 +171,27 @@ int b2g_gemm_sharded(const void* A_slab, void* B, float* C_slab, int64_t M, int6
                      void* stream);
 
 /*
+ * Copy-engine broadcast chain for the M-row-slab GEMM (collective: every rank of `comm` calls
+ * it with its own B buffer of `bytes` bytes; the root's holds B).  Ranks form a chain
+ * root -> root+1 -> ...; each pulls K panels from the previous rank's buffer with peer copies
+ * (CUDA IPC) and signals the next rank through epoch flags written by stream memory
+ * operations, so the broadcast uses no SM and overlaps the slab GEMMs.  Destroy after every
+ * rank's last call has completed.
+ */
+int b2g_chain_plan_create(void* comm, void* B, int64_t bytes, int root, void** plan);
+int b2g_chain_plan_destroy(void* plan);
+
+/*
+ * b2g_gemm_sharded over a chain plan: B is the plan's buffer (ldb, K rows); A_slab / C_slab
+ * as in b2g_gemm_sharded.  Panel p's GEMM waits only for panel p to arrive.  The call
+ * completes on `stream` once this rank's copies are done and the next rank has pulled every
+ * panel from this rank's buffer, so the caller may then overwrite B.
+ */
+int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_slab, int64_t M, int64_t N,
+                           int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int k_panels,
+                           void* stream);
+
+/*
  * Tensor-parallel variants for shapes whose B is too large to replicate (no reference
  * counterpart).
  *

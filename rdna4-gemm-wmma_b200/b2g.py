@@ -95,6 +95,12 @@ def load(path=None):
     L.b2g_gemm_sharded_n.restype = ctypes.c_int
     L.b2g_gemm_sharded_n.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp, ctypes.c_int,
                                      ctypes.c_int, vp, vp]
+    L.b2g_chain_plan_create.restype = ctypes.c_int
+    L.b2g_chain_plan_create.argtypes = [vp, vp, i64, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
+    L.b2g_chain_plan_destroy.restype = ctypes.c_int
+    L.b2g_chain_plan_destroy.argtypes = [vp]
+    L.b2g_gemm_sharded_chain.restype = ctypes.c_int
+    L.b2g_gemm_sharded_chain.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, vp]
     L.b2g_slab_rows.restype = ctypes.c_int
     L.b2g_slab_rows.argtypes = [i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64),
                                 ctypes.POINTER(ctypes.c_int64)]
@@ -285,6 +291,25 @@ def gemm_sharded_n(A, B_nslab, C_nslab, M, N, K, comm, root=0, m_panels=4, C_ful
                                      _ld(A, lda, "lda"), _ld(B_nslab, ldb, "ldb"),
                                      _ld(C_nslab, ldc, "ldc"), comm, root, m_panels,
                                      _ptr(C_full), _stream(stream)))
+
+
+def chain_plan_create(comm, B, nbytes, root=0):
+    """Collective: copy-engine broadcast chain over `comm` for this rank's B buffer."""
+    plan = ctypes.c_void_p()
+    _check(load().b2g_chain_plan_create(comm, _ptr(B), nbytes, root, ctypes.byref(plan)))
+    return plan.value
+
+
+def chain_plan_destroy(plan):
+    _check(load().b2g_chain_plan_destroy(plan))
+
+
+def gemm_sharded_chain(plan, A_slab, C_slab, M, N, K, k_panels=8, lda=None, ldb=None, ldc=None,
+                       stream=None):
+    """This rank's part of the M-row-slab GEMM with B arriving through the chain plan."""
+    _check(load().b2g_gemm_sharded_chain(plan, _ptr(A_slab), _ptr(C_slab), M, N, K,
+                                         K if lda is None else lda, N if ldb is None else ldb,
+                                         N if ldc is None else ldc, k_panels, _stream(stream)))
 
 
 def version():

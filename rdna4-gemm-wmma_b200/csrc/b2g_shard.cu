@@ -10,6 +10,7 @@
 // stream; the slab GEMM of panel p waits only for that panel, so the transfer of panel p+1
 // overlaps the GEMM of panel p.  Panel 0 overwrites C, later panels add into it (beta = 1, TMA
 // reduce-add), each element receiving one addition per panel in panel order: deterministic.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 #include <nccl.h>
@@ -19,6 +20,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/b2g_gemm.h"
 #include "errors.h"
@@ -356,5 +358,306 @@ extern "C" int b2g_gemm_sharded_n(void* A, const void* B_nslab, float* C_nslab, 
     if (e != cudaSuccess) rc = sfail(B2G_ERR_CUDA, cudaGetErrorString(e));
   }
   cudaFreeAsync(scratch, s);
+  return rc;
+}
+
+// ------------------------------------------------------------------ copy-engine broadcast chain
+// B reaches the ranks along a chain root -> root+1 -> ... through the copy engines: rank
+// r pulls each K panel from the previous rank's buffer (CUDA IPC mapping, peer copy over
+// NVLink) as soon as that rank has it, and tells the next rank so.  The signalling is done by
+// stream memory operations on 32-bit epoch flags -- the upstream rank writes "panel p of call
+// e is here" into the downstream rank's flag array, the downstream copy stream waits for it --
+// so the broadcast occupies no SM and never waits on a kernel: the slab GEMMs keep every SM
+// while the next panels travel.  (An NCCL broadcast kernel cannot be resident beside the
+// persistent GEMM, which holds each SM's shared memory, so it only runs between GEMMs.)
+namespace {
+
+constexpr int kMaxPanels = 64;
+
+using PFN_wait32 = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+using PFN_write32 = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+using PFN_range = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+struct DrvApi {
+  PFN_wait32 wait32 = nullptr;
+  PFN_write32 write32 = nullptr;
+  PFN_range range = nullptr;
+};
+
+const DrvApi* drv() {
+  static DrvApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    auto get = [](const char* name) -> void* {
+      void* p = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) == cudaSuccess &&
+          q == cudaDriverEntryPointSuccess)
+        return p;
+      return nullptr;
+    };
+    api.wait32 = reinterpret_cast<PFN_wait32>(get("cuStreamWaitValue32"));
+    api.write32 = reinterpret_cast<PFN_write32>(get("cuStreamWriteValue32"));
+    api.range = reinterpret_cast<PFN_range>(get("cuMemGetAddressRange"));
+  });
+  return (api.wait32 && api.write32 && api.range) ? &api : nullptr;
+}
+
+// What every rank publishes at plan creation (gathered over NCCL).
+struct PeerInfo {
+  cudaIpcMemHandle_t buf_handle;    // allocation holding the rank's B buffer
+  uint64_t buf_offset;              // B buffer offset inside that allocation
+  cudaIpcMemHandle_t flag_handle;   // the rank's flag array
+  int64_t bytes;                    // B buffer size
+  int32_t dev;
+};
+
+}  // namespace
+
+struct b2g_chain_plan {
+  ncclComm_t comm = nullptr;
+  int world = 1, rank = 0, root = 0, prev = -1, next = -1, dev = 0;
+  char* buf = nullptr;
+  int64_t bytes = 0;
+  uint32_t* flags = nullptr;          // [kMaxPanels] panel arrived (written by prev),
+                                      // [kMaxPanels] done (written by next)
+  char* prev_buf = nullptr;           // prev's B buffer, mapped here
+  uint32_t* prev_flags = nullptr;     // prev's flag array, mapped here
+  uint32_t* next_flags = nullptr;     // next's flag array, mapped here
+  void* opened[3] = {nullptr, nullptr, nullptr};
+  uint32_t epoch = 0;
+  cudaStream_t cs = nullptr;
+  cudaEvent_t start = nullptr, done_ev = nullptr, panel_ev[kMaxPanels] = {};
+};
+
+namespace {
+
+void plan_free(b2g_chain_plan* p) {
+  if (!p) return;
+  for (void* o : p->opened)
+    if (o) cudaIpcCloseMemHandle(o);
+  if (p->flags) cudaFree(p->flags);
+  if (p->cs) cudaStreamDestroy(p->cs);
+  if (p->start) cudaEventDestroy(p->start);
+  if (p->done_ev) cudaEventDestroy(p->done_ev);
+  for (cudaEvent_t e : p->panel_ev)
+    if (e) cudaEventDestroy(e);
+  delete p;
+}
+
+int cuda_sfail(cudaError_t e, const char* what) {
+  return sfail(B2G_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+extern "C" int b2g_chain_plan_create(void* comm, void* B, int64_t bytes, int root, void** plan_out) {
+  b2g::set_error("");
+  if (!comm || !plan_out || bytes < 0 || (bytes > 0 && !B))
+    return sfail(B2G_ERR_INVALID_ARG, "bad chain-plan arguments");
+  *plan_out = nullptr;
+  NcclApi* n = nccl();
+  if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
+  const DrvApi* d = drv();
+  if (!d) return sfail(B2G_ERR_UNSUPPORTED, "stream memory operations unavailable");
+  auto* p = new b2g_chain_plan();
+  p->comm = static_cast<ncclComm_t>(comm);
+  ncclResult_t r = n->count(p->comm, &p->world);
+  if (r == ncclSuccess) r = n->user_rank(p->comm, &p->rank);
+  if (r != ncclSuccess) {
+    plan_free(p);
+    return nccl_fail(r, "ncclCommCount/UserRank");
+  }
+  if (root < 0 || root >= p->world) {
+    plan_free(p);
+    return sfail(B2G_ERR_INVALID_ARG, "root out of range");
+  }
+  p->root = root;
+  p->buf = static_cast<char*>(B);
+  p->bytes = bytes;
+  cudaGetDevice(&p->dev);
+  const int pos = (p->rank - root + p->world) % p->world;
+  p->prev = pos > 0 ? (p->rank - 1 + p->world) % p->world : -1;
+  p->next = pos < p->world - 1 ? (p->rank + 1) % p->world : -1;
+
+  cudaError_t e = cudaMalloc(&p->flags, 2 * kMaxPanels * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(p->flags, 0, 2 * kMaxPanels * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->cs, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->start, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->done_ev, cudaEventDisableTiming);
+  for (int i = 0; i < kMaxPanels && e == cudaSuccess; ++i)
+    e = cudaEventCreateWithFlags(&p->panel_ev[i], cudaEventDisableTiming);
+  if (e != cudaSuccess) {
+    plan_free(p);
+    return cuda_sfail(e, "chain plan set-up");
+  }
+  int rc = B2G_OK;
+  if (p->world > 1) {
+    PeerInfo mine = {};
+    CUdeviceptr base = 0;
+    size_t sz = 0;
+    if (bytes > 0 && d->range(&base, &sz, reinterpret_cast<CUdeviceptr>(B)) != CUDA_SUCCESS)
+      rc = sfail(B2G_ERR_INVALID_ARG, "B is not device memory");
+    if (rc == B2G_OK && bytes > 0) {
+      e = cudaIpcGetMemHandle(&mine.buf_handle, reinterpret_cast<void*>(base));
+      mine.buf_offset = reinterpret_cast<CUdeviceptr>(B) - base;
+      if (e != cudaSuccess) rc = cuda_sfail(e, "cudaIpcGetMemHandle(B)");
+    }
+    if (rc == B2G_OK) {
+      e = cudaIpcGetMemHandle(&mine.flag_handle, p->flags);
+      if (e != cudaSuccess) rc = cuda_sfail(e, "cudaIpcGetMemHandle(flags)");
+    }
+    mine.bytes = bytes;
+    mine.dev = p->dev;
+    // gather everyone's handles (every rank takes part even after a local failure, so that no
+    // rank is left waiting in the collective)
+    void* dbuf = nullptr;
+    const size_t one = sizeof(PeerInfo);
+    e = cudaMalloc(&dbuf, one * (p->world + 1));
+    if (e != cudaSuccess) {
+      plan_free(p);
+      return cuda_sfail(e, "cudaMalloc(handle exchange)");
+    }
+    cudaMemcpy(static_cast<char*>(dbuf) + one * p->world, &mine, one, cudaMemcpyHostToDevice);
+    r = n->all_gather(static_cast<char*>(dbuf) + one * p->world, dbuf, one, ncclUint8, p->comm,
+                      p->cs);
+    std::vector<PeerInfo> all(p->world);
+    if (r == ncclSuccess) {
+      e = cudaStreamSynchronize(p->cs);
+      if (e == cudaSuccess)
+        e = cudaMemcpy(all.data(), dbuf, one * p->world, cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess && rc == B2G_OK) rc = cuda_sfail(e, "handle exchange");
+    } else if (rc == B2G_OK) {
+      rc = nccl_fail(r, "ncclAllGather(handles)");
+    }
+    cudaFree(dbuf);
+    if (rc == B2G_OK) {
+      for (const PeerInfo& q : all)
+        if (q.bytes != bytes) rc = sfail(B2G_ERR_INVALID_ARG, "B buffer sizes differ across ranks");
+    }
+    if (rc == B2G_OK && p->prev >= 0) {
+      void* q = nullptr;
+      if (bytes > 0) {
+        e = cudaIpcOpenMemHandle(&q, all[p->prev].buf_handle, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) rc = cuda_sfail(e, "cudaIpcOpenMemHandle(previous rank's B)");
+        p->opened[0] = q;
+        p->prev_buf = static_cast<char*>(q) + all[p->prev].buf_offset;
+      }
+      if (rc == B2G_OK) {
+        e = cudaIpcOpenMemHandle(&q, all[p->prev].flag_handle, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) rc = cuda_sfail(e, "cudaIpcOpenMemHandle(previous rank's flags)");
+        p->opened[1] = q;
+        p->prev_flags = static_cast<uint32_t*>(q);
+      }
+    }
+    if (rc == B2G_OK && p->next >= 0) {
+      void* q = nullptr;
+      e = cudaIpcOpenMemHandle(&q, all[p->next].flag_handle, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) rc = cuda_sfail(e, "cudaIpcOpenMemHandle(next rank's flags)");
+      p->opened[2] = q;
+      p->next_flags = static_cast<uint32_t*>(q);
+    }
+  }
+  if (rc != B2G_OK) {
+    plan_free(p);
+    return rc;
+  }
+  *plan_out = p;
+  return B2G_OK;
+}
+
+extern "C" int b2g_chain_plan_destroy(void* plan) {
+  auto* p = static_cast<b2g_chain_plan*>(plan);
+  if (!p) return B2G_OK;
+  cudaStreamSynchronize(p->cs);
+  plan_free(p);
+  return B2G_OK;
+}
+
+extern "C" int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_slab, int64_t M,
+                                      int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                                      int k_panels, void* stream) {
+  b2g::set_error("");
+  auto* p = static_cast<b2g_chain_plan*>(plan);
+  if (!p || M < 0 || N < 0 || K < 0) return sfail(B2G_ERR_INVALID_ARG, "bad sharded arguments");
+  if (ldb < std::max<int64_t>(N, 1)) return sfail(B2G_ERR_INVALID_ARG, "ldb < N");
+  if (K * ldb * 2 > p->bytes) return sfail(B2G_ERR_INVALID_ARG, "B exceeds the plan's buffer");
+  const DrvApi* d = drv();
+  if (!d) return sfail(B2G_ERR_UNSUPPORTED, "stream memory operations unavailable");
+  int64_t row0 = 0, rows = 0;
+  b2g_slab_rows(M, p->world, p->rank, &row0, &rows);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUstream ccs = reinterpret_cast<CUstream>(p->cs);
+
+  // K panels (multiples of 64 rows except the last), the first two a quarter of the others so
+  // that the first GEMM starts early
+  int P = std::max(1, std::min(k_panels, kMaxPanels - 2));
+  int64_t kp = K > 0 ? (K + P - 1) / P : 0;
+  kp = std::max<int64_t>(64, (kp + 63) / 64 * 64);
+  std::vector<std::pair<int64_t, int64_t>> panels;
+  {
+    int64_t k0 = 0;
+    const int64_t small = std::max<int64_t>(64, (kp / 4 + 63) / 64 * 64);
+    for (int i = 0; k0 < K; ++i) {
+      const int64_t len = (i < 2 && p->world > 1) ? small : kp;
+      panels.emplace_back(k0, std::min(K, k0 + len));
+      k0 += len;
+    }
+    if (panels.empty()) panels.emplace_back(0, 0);
+  }
+  if ((int)panels.size() > kMaxPanels) return sfail(B2G_ERR_INVALID_ARG, "too many panels");
+  const uint32_t ep = ++p->epoch;
+  const bool has_prev = p->prev >= 0, has_next = p->next >= 0;
+  auto flag_ptr = [](uint32_t* base, int i) { return reinterpret_cast<CUdeviceptr>(base + i); };
+  int rc = B2G_OK;
+  auto cu = [&](CUresult r, const char* what) {
+    if (r != CUDA_SUCCESS && rc == B2G_OK) {
+      const char* msg = nullptr;
+      rc = sfail(B2G_ERR_CUDA, std::string(what) + " failed (CUresult " + std::to_string((int)r) + ")");
+      (void)msg;
+    }
+  };
+  auto rt = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && rc == B2G_OK) rc = cuda_sfail(e, what);
+  };
+  // the chain starts after everything queued on the caller's stream (the root writing B, the
+  // previous call's GEMMs reading it)
+  rt(cudaEventRecord(p->start, s), "cudaEventRecord");
+  rt(cudaStreamWaitEvent(p->cs, p->start, 0), "cudaStreamWaitEvent");
+  // this rank's B is overwritten only after the next rank finished pulling the previous call's
+  if (has_prev && has_next)
+    cu(d->wait32(ccs, flag_ptr(p->flags, kMaxPanels), ep - 1, CU_STREAM_WAIT_VALUE_GEQ),
+       "cuStreamWaitValue32(done)");
+  for (size_t i = 0; i < panels.size() && rc == B2G_OK; ++i) {
+    const int64_t k0 = panels[i].first, k1 = panels[i].second;
+    const size_t off = (size_t)(k0 * ldb * 2), len = (size_t)((k1 - k0) * ldb * 2);
+    if (has_prev) {
+      cu(d->wait32(ccs, flag_ptr(p->flags, (int)i), ep, CU_STREAM_WAIT_VALUE_GEQ),
+         "cuStreamWaitValue32(panel)");
+      if (len) rt(cudaMemcpyAsync(p->buf + off, p->prev_buf + off, len, cudaMemcpyDeviceToDevice, p->cs),
+                  "cudaMemcpyAsync(peer panel)");
+    }
+    if (has_next)
+      cu(d->write32(ccs, flag_ptr(p->next_flags, (int)i), ep, 0), "cuStreamWriteValue32(panel)");
+    if (has_prev) {
+      rt(cudaEventRecord(p->panel_ev[i], p->cs), "cudaEventRecord(panel)");
+      rt(cudaStreamWaitEvent(s, p->panel_ev[i], 0), "cudaStreamWaitEvent(panel)");
+    }
+    if (rc == B2G_OK && rows > 0) {
+      const char* ap = static_cast<const char*>(A_slab) + k0 * 2;
+      const char* bp = p->buf + off;
+      rc = b2g_gemm_ex(ap, bp, C_slab, rows, N, k1 - k0, lda, ldb, ldc, 1.0f, i == 0 ? 0.0f : 1.0f, s);
+    }
+  }
+  if (has_prev)  // tell the previous rank that its buffer is free again
+    cu(d->write32(ccs, flag_ptr(p->prev_flags, kMaxPanels), ep, 0), "cuStreamWriteValue32(done)");
+  // the call completes (on the caller's stream) once the copy stream is done and the next rank
+  // has pulled everything from this rank's buffer
+  rt(cudaEventRecord(p->done_ev, p->cs), "cudaEventRecord(done)");
+  rt(cudaStreamWaitEvent(s, p->done_ev, 0), "cudaStreamWaitEvent(done)");
+  if (has_next)
+    cu(d->wait32(reinterpret_cast<CUstream>(s), flag_ptr(p->flags, kMaxPanels), ep,
+                 CU_STREAM_WAIT_VALUE_GEQ),
+       "cuStreamWaitValue32(next done)");
   return rc;
 }

@@ -252,3 +252,39 @@ def nccl_tp_rank(mode, rank, world, uid_path, M, N, K, panels, out_q):
         out_q.put((rank, bad, gbad, status, a_ok, None))
     except Exception:
         out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))
+
+
+def nccl_chain_rank(rank, world, uid_path, M, N, K, panels, calls, out_q):
+    """b2g_gemm_sharded_chain on `world` GPUs: `calls` calls in a row, the root writing a new B
+    (another seed) before each; every call checked on sampled rows, and B bit-exact."""
+    try:
+        import torch
+        from oracle import orc
+        b2g = _load_pkg("b2g")
+        torch.cuda.set_device(rank)
+        comm = _nccl_comm(b2g, rank, world, uid_path)
+        row0, rows = b2g.slab_rows(M, world, rank)
+        dA = torch.empty((max(rows, 1), K), dtype=torch.float16, device="cuda")
+        b2g.fill_uniform(dA, rows * K, 1, row0 * K)
+        dB = torch.full((K, N), float("nan"), dtype=torch.float16, device="cuda")
+        plan = b2g.chain_plan_create(comm, dB, K * N * 2, 0)
+        stream = torch.cuda.current_stream()
+        worst, b_ok = 0, True
+        for c in range(calls):
+            seed = 100 + c
+            if rank == 0:
+                b2g.fill_uniform(dB, K * N, seed, 0, stream.cuda_stream)
+            dC = torch.full((max(rows, 1), N), float("nan"), dtype=torch.float32, device="cuda")
+            b2g.gemm_sharded_chain(plan, dA, dC, M, N, K, k_panels=panels, stream=stream.cuda_stream)
+            torch.cuda.synchronize()
+            B = orc.uniform_f16((K, N), seed)
+            for r in sorted(set([0, rows - 1, rows // 2])) if rows else []:
+                a = orc.uniform_f16((1, K), 1, (row0 + r) * K)
+                worst = max(worst, orc.check(dC[r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, 1.0, 1.0)[0])
+            b_ok = b_ok and bool(torch.equal(dB.cpu().view(torch.int16), torch.from_numpy(B.view(np.int16))))
+        status = b2g.device_status()
+        b2g.chain_plan_destroy(plan)
+        b2g.comm_destroy(comm)
+        out_q.put((rank, rows, worst, status, b_ok, None))
+    except Exception:
+        out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))

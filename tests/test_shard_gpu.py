@@ -123,3 +123,35 @@ def test_tp_two_ranks(b2g, cuda, mode):
     for rank, bad, gbad, status, a_ok, tb in res:
         assert tb is None, tb
         assert bad == 0 and gbad == 0 and status == 0 and a_ok, (rank, bad, gbad, status, a_ok)
+
+
+def test_chain_single_rank(b2g, cuda):
+    with tempfile.TemporaryDirectory() as d:
+        q = _ListQueue()
+        shard_worker.nccl_chain_rank(0, 1, os.path.join(d, "id"), 512, 768, 1024, 3, 2, q)
+    rank, rows, worst, status, b_ok, tb = q[0]
+    assert tb is None, tb
+    assert worst == 0 and status == 0 and b_ok
+
+
+@pytest.mark.parametrize("M,N,K,panels", [(2048, 1536, 4096, 6), (640, 512, 200, 3)])
+def test_chain_two_ranks(b2g, cuda, M, N, K, panels):
+    """Copy-engine chain broadcast on two GPUs: three calls, the root rewriting B before each
+    (the epoch flags and the 'done' handshake keep the panels of consecutive calls apart)."""
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=shard_worker.nccl_chain_rank,
+                             args=(r, 2, os.path.join(d, "id"), M, N, K, panels, 3, q))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        res = sorted(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=120)
+    for rank, rows, worst, status, b_ok, tb in res:
+        assert tb is None, tb
+        assert worst == 0 and status == 0 and b_ok, (rank, rows, worst, status, b_ok)
+    assert sum(r[1] for r in res) == M
