@@ -261,7 +261,8 @@ int b2g_device_status(int clear);
  *   "fault_flags"  test-only fault injection: bit 0 = the TMA producer issues no loads,
  *                  so the MMA wait runs out and the call reports B2G_ERR_TIMEOUT
  * Returns B2G_OK or B2G_ERR_INVALID_ARG for an unknown key or value.  Options are
- * process-wide.
+ * process-wide.  b2g_get_option("launches") (read-only) returns how many kernels the library
+ * has launched in this process.
  */
 int b2g_set_option(const char* key, int64_t value);
 int64_t b2g_get_option(const char* key);

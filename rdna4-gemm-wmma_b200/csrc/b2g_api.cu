@@ -58,6 +58,9 @@ static std::atomic<int64_t> opt_store_hint{0};
 static std::atomic<int64_t> opt_split_k{0};  // 0 = choose by shape, else the split count
 static std::atomic<int64_t> opt_tail_split{1};  // split the tail wave's tiles (auto mode)
 static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream serialization
+// Kernels this library has launched (every GEMM, scale and fill kernel), for callers that
+// count launches (b2g_get_option("launches")).
+static std::atomic<int64_t> g_launches{0};
 static std::atomic<int64_t> opt_cluster_fixup{1};  // split-K fix-up through distributed smem
 static std::atomic<int64_t> opt_serial_fixup{0};  // 1 = always the last-arriver fix-up
 
@@ -471,6 +474,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "generic kernel launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     t_path = path;
     return B2G_OK;
   };
@@ -666,6 +670,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     scale_c_kernel<<<eblocks, eth, 0, stream>>>(Cp, make_geo(), beta);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e, "scale kernel launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
   }
   p.timeout_ns = (unsigned long long)opt_timeout_ns.load();
   p.fault_flags = (int)opt_fault_flags.load();
@@ -881,6 +886,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
   if (scratch) cudaFreeAsync(scratch, stream);  // stream-ordered: freed after the kernel
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 kernel launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   t_path = cg == 1 ? B2G_PATH_TC_1CTA : B2G_PATH_TC_2CTA;
   return B2G_OK;
 }
@@ -988,6 +994,7 @@ extern "C" int b2g_fill_uniform(void* dst, int64_t n, int dtype, uint64_t seed, 
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "fill kernel launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return B2G_OK;
 }
 
@@ -1089,6 +1096,7 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
 
 extern "C" int64_t b2g_get_option(const char* key) {
   if (!key) return -1;
+  if (!strcmp(key, "launches")) return g_launches.load();
   if (!strcmp(key, "cta_group")) return opt_cta_group;
   if (!strcmp(key, "raster_group")) return opt_raster_group;
   if (!strcmp(key, "timeout_ns")) return opt_timeout_ns;

@@ -210,3 +210,16 @@ def test_back_to_back_launches_with_and_without_pdl(b2g, cuda, orc):
     assert b2g.device_status() == 0
     assert torch.equal(outs[0], outs[1])
     assert_close(orc, outs[1].cpu().numpy(), 5.0 * orc.gemm_f64(A, B), K, 5.0, 1.0)
+
+
+def test_launch_counter(b2g, cuda):
+    """b2g_get_option("launches") counts the kernels the library launched (one per GEMM here)."""
+    torch = cuda
+    dA = torch.zeros((256, 512), dtype=torch.float16, device="cuda")
+    dB = torch.zeros((512, 256), dtype=torch.float16, device="cuda")
+    dC = torch.empty((256, 256), dtype=torch.float32, device="cuda")
+    n0 = b2g.get_option("launches")
+    for _ in range(5):
+        b2g.gemm(dA, dB, dC, 256, 256, 512)
+    torch.cuda.synchronize()
+    assert b2g.get_option("launches") - n0 == 5
