@@ -160,7 +160,7 @@ def test_gemm_timeout_reports_error(b2g, cuda, orc):
     with options(b2g, fault_flags=1, timeout_ns=200_000_000, cta_group=1):
         b2g.gemm(dA, dA, dC, M, N, K)
         code = b2g.device_status(clear=True)
-    assert code in (2, 3, 4), code  # a wait of the MMA or epilogue role gave up
+    assert code in (1, 2, 3, 4), code  # a wait of the producer, MMA or epilogue role gave up
     # the device still works
     A, B, C, path = _run_gemm(b2g, cuda, orc, 256, 256, 256)
     assert_close(orc, C, orc.gemm_f64(A, B), 256)

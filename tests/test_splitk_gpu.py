@@ -159,7 +159,7 @@ def test_split_k_counters_after_timeout_and_many_calls(b2g, cuda, orc):
     with options(b2g, fault_flags=1, timeout_ns=200_000_000, cta_group=1, tile_n=128, split_k=2):
         b2g.gemm(dA, dB, dC, M, N, K)
         code = b2g.device_status(clear=True)
-    assert code in (2, 3, 4, 6), code
+    assert code in (1, 2, 3, 4, 6), code  # whichever bounded wait gave up first
     first = None
     with options(b2g, cta_group=1, tile_n=128, split_k=4):
         for _ in range(300):
