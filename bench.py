@@ -490,9 +490,13 @@ def run_sharded(args, torch, dist, b2g, ws, rank, local, dev):
     if ws > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    # spot check: first row of this rank's slab (B on this rank arrived through the broadcast)
+    # spot check: first row of every rank's slab (B on each rank arrived through the broadcast)
     bad = row_out_of_tolerance(torch, dC[:1], dA[:1], dB, K)
     status = b2g.device_status()
+    if ws > 1:
+        chk = torch.tensor([bad, abs(status)], dtype=torch.int64, device=dev)
+        dist.all_reduce(chk, op=dist.ReduceOp.MAX)
+        bad, status = int(chk[0].item()), int(chk[1].item())
     if ws > 1:
         dist.barrier()
     if plan is not None:

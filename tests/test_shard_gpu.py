@@ -134,18 +134,20 @@ def test_chain_single_rank(b2g, cuda):
     assert worst == 0 and status == 0 and b_ok
 
 
-@pytest.mark.parametrize("M,N,K,panels", [(2048, 1536, 4096, 6), (640, 512, 200, 3)])
-def test_chain_two_ranks(b2g, cuda, M, N, K, panels):
-    """Copy-engine chain broadcast on two GPUs: three calls, the root rewriting B before each
-    (the epoch flags and the 'done' handshake keep the panels of consecutive calls apart)."""
-    if cuda.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world,M,N,K,panels", [(2, 2048, 1536, 4096, 6), (2, 640, 512, 200, 3),
+                                                (4, 4096, 1024, 4096, 8), (8, 4096, 2048, 8192, 8)])
+def test_chain_multi_rank(b2g, cuda, world, M, N, K, panels):
+    """Copy-engine chain broadcast over `world` GPUs (skipped with fewer): three calls, the root
+    rewriting B before each (the epoch flags and the 'done' handshake keep the panels of
+    consecutive calls apart); every rank's slab rows checked and B bit-exact on every rank."""
+    if cuda.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with tempfile.TemporaryDirectory() as d:
         procs = [ctx.Process(target=shard_worker.nccl_chain_rank,
-                             args=(r, 2, os.path.join(d, "id"), M, N, K, panels, 3, q))
-                 for r in range(2)]
+                             args=(r, world, os.path.join(d, "id"), M, N, K, panels, 3, q))
+                 for r in range(world)]
         for p in procs:
             p.start()
         res = sorted(q.get(timeout=300) for _ in procs)
