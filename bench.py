@@ -18,6 +18,8 @@ port of GEMM_Naive, mmm.cpp:52-62; the HIP reference cannot run here).
 import argparse
 import datetime
 import json
+
+import numpy as np
 import os
 import statistics
 import subprocess
@@ -235,8 +237,11 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
-    ap.add_argument("--workload", default="gemm8192", choices=["gemm8192", "sharded32768"],
+    ap.add_argument("--workload", default="gemm8192",
+                    choices=["gemm8192", "sharded32768", "contraction5d"],
                     help="gemm8192: BASELINE configs[1] per GPU (the default line); "
+                         "contraction5d: BASELINE configs[2] through the contraction entry point "
+                         "(C[a,b,i,n] = sum A[a,b,i,j,k] B[j,k,n], a8 b16 i64 j64 k128 n4096); "
                          "sharded32768: BASELINE configs[4], one 32768^3 GEMM as M-row slabs "
                          "over the N GPUs, B broadcast in K panels inside every step")
     ap.add_argument("--bcast", default="chain", choices=["chain", "nccl"],
@@ -270,6 +275,16 @@ def main():
         return run_sharded(args, torch, dist, b2g, ws, rank, local, dev)
 
     M, N, K = M_PER_GPU, N_DIM, K_DIM
+    contraction = args.workload == "contraction5d"
+    if contraction:
+        # the contraction's GEMM view is M = a*b*i, K = j*k, N = n
+        c5 = dict(a=8, b=16, i=64, j=64, k=128, n=4096)
+        M, N, K = c5["a"] * c5["b"] * c5["i"], c5["n"], c5["j"] * c5["k"]
+        a_shape = (c5["a"], c5["b"], c5["i"], c5["j"], c5["k"])
+        b_shape = (c5["j"], c5["k"], c5["n"])
+        c_shape = (c5["a"], c5["b"], c5["i"], c5["n"])
+        rowmajor = lambda sh: tuple(int(np.prod(sh[d + 1:])) for d in range(len(sh)))
+        args.kernel_only = True
     if args.shape:
         # another BASELINE shape (configs[0], [2] as its GEMM view, [3]); kernel loop only
         M, N, K = (int(x) for x in args.shape.split(","))
@@ -292,7 +307,10 @@ def main():
     torch.cuda.synchronize()
 
     def step():
-        if dt:
+        if contraction:
+            b2g.contract5d(dA, a_shape, rowmajor(a_shape), dB, b_shape, rowmajor(b_shape), dC,
+                           c_shape, rowmajor(c_shape), stream)
+        elif dt:
             b2g.gemm_typed(dA, dB, dC, M, N, K, dt, stream=stream)
         else:
             b2g.gemm(dA, dB, dC, M, N, K, K, N, N, stream)
@@ -401,6 +419,8 @@ def main():
     if rank != 0:
         return 0
     metric = "gemm_tflops_8192cubed_fp16_fp32"
+    if contraction:
+        metric = "contraction_tflops_a8b16i64j64k128n4096_fp16_fp32"
     if args.shape:
         metric = "gemm_tflops_%dx%dx%d_fp16_fp32" % (M, N, K)
     if dt:
@@ -419,7 +439,10 @@ def main():
         "dtype": "%s in, f32 accumulate/out" % args.dtype,
         "data": "synthetic: seeded U[-1,1] %s generated on the device (b2g_fill_uniform)" % args.dtype,
         "config": {
-            "workload": ("gemm %dx%dx%d row-major fp16->fp32 (kernel loop)" % (M, N, K)) if args.shape
+            "workload": ("contraction C[a,b,i,n] = sum_{j,k} A[a,b,i,j,k] B[j,k,n], a8 b16 i64 j64 "
+                         "k128 n4096, contiguous operands through b2g_contract5d (BASELINE "
+                         "configs[2]; GEMM view %dx%dx%d)" % (M, N, K)) if contraction
+                        else ("gemm %dx%dx%d row-major fp16->fp32 (kernel loop)" % (M, N, K)) if args.shape
                         else "gemm 8192x8192x8192 row-major fp16->fp32 per GPU (BASELINE configs[1]);"
                              " N>1: M-row slabs of a (8192N)x8192x8192 GEMM, B broadcast once",
             "M": M, "N": N, "K": K, "world_size": ws, "path": path,
