@@ -583,11 +583,23 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   int bn = (int)opt_tile_n.load();
   if (bn == 128) cg = 1;  // the 128-column tile exists for one CTA only
   if (cg != 1 && cg != 2) {
-    // Small problems (fewer 128x256 tiles than SMs) take 128x128 tiles: four times as many
-    // tiles as the pair tile, so more SMs share the work.
+    // Small problems (fewer 128x256 tiles than SMs) take one-CTA tiles.  The width is the one
+    // whose work units (tiles times the split count the split-K rule below would choose) fill
+    // the SMs best; on a tie the 128x256 tile, which moves a quarter fewer bytes per FLOP.
     if (bn == 0 && nmt64 * ((N + 255) / 256) < ds->sm_count) {
       cg = 1;
-      bn = 128;
+      const int64_t kit = ((ksz + kb_elems - 1) / kb_elems) * jsz;  // K blocks
+      auto fill = [&](int w) {
+        const int64_t tiles = nmt64 * ((N + w - 1) / w);
+        int64_t sp = std::min<int64_t>({(int64_t)ds->sm_count / std::max<int64_t>(1, tiles),
+                                        kit / 16, 8});
+        if (2 * tiles > ds->sm_count || kit < 32) sp = 1;
+        sp = std::max<int64_t>(1, sp);
+        const int64_t units = tiles * sp;
+        const int64_t waves = (units + ds->sm_count - 1) / ds->sm_count;
+        return (double)units / (double)(waves * ds->sm_count);
+      };
+      bn = fill(128) > fill(256) + 1e-9 ? 128 : 256;
     } else {
       cg = (nmt64 >= 2) ? 2 : 1;
     }
@@ -739,10 +751,10 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     const int waves = p.num_tiles / std::max(1, group_cap);
     const int rem = p.num_tiles - waves * group_cap;
     // every split keeps >= 16 K blocks: below that the fixed cost of a unit (pipeline fill,
-    // partial write and fence, fix-up) outweighs the shorter main loop (1024^3 runs 15.6 us
-    // unsplit, 27.8 us split two ways)
+    // partial write, fix-up) outweighs the shorter main loop.  One-CTA tiles split at most 8
+    // ways, the largest cluster of the cluster fix-up.
     if (2 * p.num_tiles <= group_cap && p.k_iters >= 32) {
-      splits = std::min({group_cap / std::max(1, p.num_tiles), p.k_iters / 16, 16});
+      splits = std::min({group_cap / std::max(1, p.num_tiles), p.k_iters / 16, cg == 1 ? 8 : 16});
       full = 0;
     } else if (opt_tail_split.load() && waves >= 1 && rem > 0 && group_cap / rem >= 2 &&
                p.k_iters >= 32) {
