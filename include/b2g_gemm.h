@@ -215,6 +215,15 @@ int b2g_gemm_sharded_n(void* A, const void* B_nslab, float* C_nslab, int64_t M, 
                        int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* comm, int root,
                        int m_panels, float* C_full, void* stream);
 
+/*
+ * Launch plan the library would choose for a row-major M x N x K GEMM of operand type `dtype`
+ * on a GPU with `sm_count` SMs (full cluster occupancy assumed), under the current options:
+ * CTAs per tile, tile width, K splits per split tile, and how many tiles run unsplit.  No GPU
+ * needed (no reference counterpart; for tests and tuning).
+ */
+int b2g_plan_preview(int64_t M, int64_t N, int64_t K, int dtype, int sm_count, int* cta_group,
+                     int* tile_n, int* k_splits, int* num_full);
+
 /* Balanced contiguous row partition: rank r gets M/world rows, the first M%world ranks one more. */
 int b2g_slab_rows(int64_t M, int world, int rank, int64_t* row0, int64_t* rows);
 

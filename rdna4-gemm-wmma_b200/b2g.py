@@ -101,6 +101,9 @@ def load(path=None):
     L.b2g_chain_plan_destroy.argtypes = [vp]
     L.b2g_gemm_sharded_chain.restype = ctypes.c_int
     L.b2g_gemm_sharded_chain.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, vp]
+    L.b2g_plan_preview.restype = ctypes.c_int
+    L.b2g_plan_preview.argtypes = [i64, i64, i64, ctypes.c_int, ctypes.c_int] + \
+        [ctypes.POINTER(ctypes.c_int)] * 4
     L.b2g_slab_rows.restype = ctypes.c_int
     L.b2g_slab_rows.argtypes = [i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64),
                                 ctypes.POINTER(ctypes.c_int64)]
@@ -310,6 +313,13 @@ def gemm_sharded_chain(plan, A_slab, C_slab, M, N, K, k_panels=8, lda=None, ldb=
     _check(load().b2g_gemm_sharded_chain(plan, _ptr(A_slab), _ptr(C_slab), M, N, K,
                                          K if lda is None else lda, N if ldb is None else ldb,
                                          N if ldc is None else ldc, k_panels, _stream(stream)))
+
+
+def plan_preview(M, N, K, dtype=0, sm_count=148):
+    """(cta_group, tile_n, k_splits, num_full) the library would choose (no GPU needed)."""
+    out = [ctypes.c_int() for _ in range(4)]
+    _check(load().b2g_plan_preview(M, N, K, dtype, sm_count, *[ctypes.byref(x) for x in out]))
+    return tuple(x.value for x in out)
 
 
 def version():

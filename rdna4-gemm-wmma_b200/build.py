@@ -16,7 +16,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libb2g_gemm.so")
 SOURCES = ["b2g_api.cu", "b2g_shard.cu"]
-HEADERS = ["ptx.cuh", "gemm_sm100.cuh", "sched.h", "errors.h"]
+HEADERS = ["ptx.cuh", "gemm_sm100.cuh", "sched.h", "errors.h", "plan.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -24,6 +24,7 @@
 
 #include "../../include/b2g_gemm.h"
 #include "errors.h"
+#include "plan.h"
 #include "gemm_sm100.cuh"
 
 namespace b2g {
@@ -579,40 +580,9 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   const int num_m_tiles_b = (int)((bsz + bb - 1) / bb);
   const int num_m_tiles_a = (int)((asz + ba - 1) / ba);
   const int64_t nmt64 = (int64_t)num_m_tiles_i * num_m_tiles_b * num_m_tiles_a;
-  int cg = (int)opt_cta_group.load();
-  int bn = (int)opt_tile_n.load();
-  if (bn == 128) cg = 1;  // the 128-column tile exists for one CTA only
-  if (cg != 1 && cg != 2) {
-    // Small problems (fewer 128x256 tiles than SMs) take one-CTA tiles.  The width is the one
-    // whose work units (tiles times the split count the split-K rule below would choose) fill
-    // the SMs best; on a tie the 128x256 tile, which moves a quarter fewer bytes per FLOP.
-    if (bn == 0 && nmt64 * ((N + 255) / 256) < ds->sm_count) {
-      cg = 1;
-      const int64_t kit = ((ksz + kb_elems - 1) / kb_elems) * jsz;  // K blocks
-      auto fill = [&](int w) {
-        const int64_t tiles = nmt64 * ((N + w - 1) / w);
-        int64_t sp = std::min<int64_t>({(int64_t)ds->sm_count / std::max<int64_t>(1, tiles),
-                                        kit / 16, 8});
-        if (2 * tiles > ds->sm_count || kit < 32) sp = 1;
-        sp = std::max<int64_t>(1, sp);
-        const int64_t units = tiles * sp;
-        const int64_t waves = (units + ds->sm_count - 1) / ds->sm_count;
-        return (double)units / (double)(waves * ds->sm_count);
-      };
-      bn = fill(128) > fill(256) + 1e-9 ? 128 : 256;
-    } else {
-      cg = (nmt64 >= 2) ? 2 : 1;
-    }
-  }
-  if (bn != 128 && bn != 256 && bn != 512) {
-    // 512-wide pair tiles pull a quarter fewer operand bytes from L2 per FLOP; use them when
-    // there are enough of them to fill every CTA pair at least twice.
-    const int64_t pairs = std::max(1, ds->sm_count / 2);
-    const int64_t t512 = ((nmt64 + 1) / 2) * ((N + 511) / 512);
-    bn = (cg == 2 && t512 >= 2 * pairs) ? 512 : 256;
-  }
-  if (cg == 1 && bn == 512) bn = 256;  // one CTA: at most 256 columns (two accumulators)
-  if (cg == 2 && bn == 128) bn = 256;
+  const TileChoice tc = choose_tiles(nmt64, N, ((ksz + kb_elems - 1) / kb_elems) * jsz, ds->sm_count,
+                                     (int)opt_cta_group.load(), (int)opt_tile_n.load());
+  const int cg = tc.cg, bn = tc.bn;
   const int64_t nnt64 = (N + bn - 1) / bn;
   if (nmt64 * nnt64 > INT32_MAX / 4) return launch_generic(B2G_PATH_GENERIC);
   const int bph = std::min(bn, 256) / cg;  // B columns of one N-half held by one CTA
@@ -743,29 +713,11 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   // unit; each split keeps at least 8 K blocks.
   // Tail split: when the tiles fill whole waves plus a partial one, split only the tiles of
   // the partial wave so that its units fill the CTA groups.
-  int splits = (int)opt_split_k.load();
-  int full = 0;
-  if (splits <= 0) {
-    splits = 1;
-    full = p.num_tiles;
-    const int waves = p.num_tiles / std::max(1, group_cap);
-    const int rem = p.num_tiles - waves * group_cap;
-    // every split keeps >= 16 K blocks: below that the fixed cost of a unit (pipeline fill,
-    // partial write, fix-up) outweighs the shorter main loop.  One-CTA tiles split at most 8
-    // ways, the largest cluster of the cluster fix-up.
-    if (2 * p.num_tiles <= group_cap && p.k_iters >= 32) {
-      splits = std::min({group_cap / std::max(1, p.num_tiles), p.k_iters / 16, cg == 1 ? 8 : 16});
-      full = 0;
-    } else if (opt_tail_split.load() && waves >= 1 && rem > 0 && group_cap / rem >= 2 &&
-               p.k_iters >= 32) {
-      splits = std::min({group_cap / rem, 4, p.k_iters / 16});
-      full = waves * group_cap;
-    }
-  }
-  splits = std::max(1, std::min(splits, p.k_iters));
-  p.k_per_split = (p.k_iters + splits - 1) / splits;
-  p.k_splits = (p.k_iters + p.k_per_split - 1) / p.k_per_split;  // no empty split
-  if (p.k_splits == 1) full = p.num_tiles;
+  const SplitChoice sc = choose_splits(p.num_tiles, p.k_iters, group_cap, cg, (int)opt_split_k.load(),
+                                       opt_tail_split.load() != 0);
+  p.k_per_split = sc.k_per_split;
+  p.k_splits = sc.k_splits;
+  int full = sc.num_full;
   if (fixed && full > 0 && full < p.num_tiles) {
     // the tail split is an optimisation: under a fixed scratch it is dropped if it does not fit
     const size_t need = (size_t)(p.num_tiles - full) * p.k_splits * cg * 128 * bn * sizeof(float) +
@@ -1129,3 +1081,25 @@ extern "C" void b2g_tile_coord(int t, int num_m, int num_n, int group, int* tm, 
 }
 
 extern "C" const char* b2g_version(void) { return "b2g_gemm 0.1 (sm_100a tcgen05)"; }
+
+extern "C" int b2g_plan_preview(int64_t M, int64_t N, int64_t K, int dtype, int sm_count, int* cg,
+                                int* bn, int* k_splits, int* num_full) {
+  if (M < 1 || N < 1 || K < 1 || sm_count < 2 || !cg || !bn || !k_splits || !num_full)
+    return fail(B2G_ERR_INVALID_ARG, "bad plan-preview arguments");
+  if (dtype < B2G_DTYPE_F16 || dtype > B2G_DTYPE_E5M2)
+    return fail(B2G_ERR_INVALID_ARG, "unknown operand type code %d", dtype);
+  const int64_t kb = dtype >= B2G_DTYPE_E4M3 ? 128 : 64;  // K elements per 128-byte stage row
+  const int64_t nmt = (M + 127) / 128;
+  const TileChoice t = choose_tiles(nmt, N, (K + kb - 1) / kb, sm_count, (int)opt_cta_group.load(),
+                                    (int)opt_tile_n.load());
+  const int64_t tiles = ((nmt + t.cg - 1) / t.cg) * ((N + t.bn - 1) / t.bn);
+  if (tiles > INT32_MAX / 4) return fail(B2G_ERR_UNSUPPORTED, "too many tiles");
+  const int group_cap = t.cg == 1 ? sm_count : sm_count / 2;  // CTA pairs: full occupancy assumed
+  const SplitChoice s = choose_splits((int)tiles, (int)((K + kb - 1) / kb), group_cap, t.cg,
+                                      (int)opt_split_k.load(), opt_tail_split.load() != 0);
+  *cg = t.cg;
+  *bn = t.bn;
+  *k_splits = s.k_splits;
+  *num_full = s.num_full;
+  return B2G_OK;
+}

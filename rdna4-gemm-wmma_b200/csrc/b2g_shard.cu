@@ -557,6 +557,29 @@ extern "C" int b2g_chain_plan_create(void* comm, void* B, int64_t bytes, int roo
       p->opened[2] = q;
       p->next_flags = static_cast<uint32_t*>(q);
     }
+    // Every rank learns every rank's outcome, so that all of them either keep the plan or
+    // free it: a rank left holding a plan whose peer failed would wait for flags that never
+    // come.
+    int32_t* dst = nullptr;
+    e = cudaMalloc(&dst, sizeof(int32_t) * (p->world + 1));
+    if (e == cudaSuccess) {
+      const int32_t mine_rc = rc;
+      cudaMemcpy(dst + p->world, &mine_rc, sizeof(int32_t), cudaMemcpyHostToDevice);
+      r = n->all_gather(dst + p->world, dst, 1, ncclInt32, p->comm, p->cs);
+      std::vector<int32_t> rcs(p->world, 0);
+      if (r == ncclSuccess && cudaStreamSynchronize(p->cs) == cudaSuccess &&
+          cudaMemcpy(rcs.data(), dst, sizeof(int32_t) * p->world, cudaMemcpyDeviceToHost) ==
+              cudaSuccess) {
+        for (int q = 0; q < p->world; ++q)
+          if (rcs[q] != B2G_OK && rc == B2G_OK)
+            rc = sfail(rcs[q], "chain plan set-up failed on rank " + std::to_string(q));
+      } else if (rc == B2G_OK) {
+        rc = sfail(B2G_ERR_NCCL, "chain plan status exchange failed");
+      }
+      cudaFree(dst);
+    } else if (rc == B2G_OK) {
+      rc = cuda_sfail(e, "cudaMalloc(status exchange)");
+    }
   }
   if (rc != B2G_OK) {
     plan_free(p);

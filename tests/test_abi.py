@@ -137,3 +137,31 @@ int main() {
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0, (run.returncode, run.stdout, run.stderr)
     assert "sm_100a" in run.stdout
+
+
+@pytest.mark.parametrize("shape,plan", [
+    # (M, N, K) -> (CTAs per tile, tile width, K splits, unsplit tiles) on 148 SMs
+    ((8192, 8192, 8192), (2, 512, 1, 512)),         # 256x512 pair tiles
+    ((8192, 4096, 8192), (2, 512, 2, 222)),         # configs[2] GEMM view: tail wave split 2 ways
+    ((8192, 28672, 8192), (2, 512, 4, 1776)),       # configs[3]: 16 tail tiles split 4 ways
+    ((16384, 16384, 4096), (2, 512, 1, 2048)),      # configs[3]: whole waves
+    ((128, 8192, 8192), (1, 256, 4, 0)),            # configs[3] skinny: 32 tiles x 4 splits
+    ((1024, 1024, 1024), (1, 128, 1, 64)),          # configs[0]: 64 tiles, K too short to split
+    ((256, 8192, 8192), (1, 256, 2, 0)),
+    ((128, 2048, 8192), (1, 128, 8, 0)),
+    ((2048, 2048, 2048), (1, 256, 1, 128)),
+])
+def test_plan_preview_choices(b2g, shape, plan):
+    """The launch plan for the BASELINE shapes and the small shapes whose choice was measured
+    (the width whose split units fill the SMs best; ties to 128x256)."""
+    assert b2g.plan_preview(*shape) == plan
+
+
+def test_plan_preview_follows_options(b2g):
+    from gpu_util import options
+    with options(b2g, cta_group=1, tile_n=256, split_k=3):
+        assert b2g.plan_preview(384, 1024, 2240) == (1, 256, 3, 0)
+    with options(b2g, tail_split=0):
+        assert b2g.plan_preview(8192, 4096, 8192) == (2, 512, 1, 256)
+    with pytest.raises(b2g.B2GError):
+        b2g.plan_preview(0, 8, 8)
