@@ -55,7 +55,7 @@ struct GemmParams {
   int num_pm_tiles;            // tiles of 128*CG rows (one per CTA group)
   int n_size;                  // N extent
   int num_n_tiles;             // BN-column tiles
-  int k_blocks_per_j;          // ceil(k / 64)
+  int k_blocks_per_j;          // K blocks (128 bytes of k: 64 16-bit or 128 8-bit elements) per j
   int k_iters;                 // j * k_blocks_per_j
   int num_tiles;               // num_pm_tiles * num_n_tiles
   int raster_group;            // strip height of the tile order, in CTA-group tiles
@@ -65,10 +65,10 @@ struct GemmParams {
   // Work units: the first num_full tiles (in tile order) are one unit each over all of K; each
   // remaining tile is split into k_splits units, split s covering the K blocks
   // [s*k_per_split, min(k_iters, (s+1)*k_per_split)).  num_full = 0 is plain split-K (too few
-  // tiles to fill the GPU); num_full = (waves)*(CTA groups) splits only the tail wave.  A split
-  // unit writes its fp32 partial tile to `ws` and bumps counters[split tile*CG + cta]; the unit
-  // that arrives last sums the partials in split order (deterministic), stores C and resets
-  // the counter.
+  // tiles to fill the GPU); num_full = (waves)*(CTA groups) splits only the tail wave.  Unless
+  // cluster_fixup is set, a split unit writes its fp32 partial tile to `ws` and bumps
+  // counters[split tile*CG + cta]; the partials are summed in split order (deterministic) by the
+  // parallel or the serial fix-up below, which also return the counter to zero.
   int num_full;
   int k_splits;
   int k_per_split;
@@ -550,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       if (ns > 1) {
-        // ---- split-K unit: partial tile -> workspace; the last unit of the tile reduces.
+        // ---- split-K unit: partial tile -> workspace, then the fix-up reduces the tile.
         // Workspace block of (split unit, CTA): 128 x BN floats as float4 [chunk][warp][j][lane]
         // (lane = row within the warp's 32 rows, j = columns 4j..4j+3 of the 32-column chunk),
         // so every warp-wide store and load covers 512 contiguous bytes.
