@@ -104,3 +104,43 @@ def test_contraction_fuzz(b2g, cuda, orc, case):
     assert_close(orc, dC.cpu().numpy(), ref, j * k, abs(alpha), 1.0,
                  what="case %d: A%r%r B%r%r C%r%r path=%d" % (case, a_shape, a_ord, b_shape, b_ord,
                                                              c_shape, c_ord, b2g.last_path()))
+
+
+@pytest.mark.parametrize("case", range(24))
+def test_typed_gemm_fuzz(b2g, cuda, orc, case):
+    """bf16 / e4m3 / e5m2 operands on random ragged shapes, pitches, alpha/beta and kernel
+    choices (8-bit pitches that are not multiples of 16 bytes take the generic kernel)."""
+    torch = cuda
+    rng = random.Random(9000 + case)
+    dt = (1, 2, 3)[case % 3]
+    M = rng.choice([1, 100, 128, 300, 512])
+    N = rng.choice([16, 200, 256, 528])
+    K = rng.choice([16, 64, 200, 512, 1040])
+    pad = lambda x: x + rng.choice([0, 0, 16, 7])
+    lda, ldb, ldc = pad(K), pad(N), pad(N)
+    opts = {}
+    v = rng.choice([None] + VARIANTS)
+    if v is not None:
+        opts.update(cta_group=v[0], tile_n=v[1])
+    opts["split_k"] = rng.choice([0, 0, 2])
+    alpha, beta = rng.choice([1.0, -0.5]), rng.choice([0.0, 1.0])
+    A = orc.uniform((M, lda), 300 + case, dt)
+    B = orc.uniform((K, ldb), 400 + case, dt)
+    C0 = orc.uniform_f16((M, N), 500 + case).astype(np.float32)
+    Cp = np.full((M, ldc), np.nan, np.float32)
+    Cp[:, :N] = C0
+    dA, dB, dC = to_dev(torch, A), to_dev(torch, B), to_dev(torch, Cp)
+    with options(b2g, **opts):
+        b2g.gemm_typed(dA, dB, dC, M, N, K, dt, alpha, beta, lda=lda, ldb=ldb, ldc=ldc)
+        torch.cuda.synchronize()
+        path = b2g.last_path()
+    assert b2g.device_status() == 0
+    A, B = A[:, :K], B[:, :N]
+    Af, Bf = orc.to_f32(A, dt), orc.to_f32(B, dt)
+    ref = alpha * orc.gemm_f64_typed(A, B, dt) + beta * C0.astype(np.float64)
+    out = dC.cpu().numpy()
+    what = "case %d dtype %d: %dx%dx%d ld=(%d,%d,%d) a=%g b=%g %r path=%d" % (
+        case, dt, M, N, K, lda, ldb, ldc, alpha, beta, opts, path)
+    assert_close(orc, out[:, :N], ref, K, abs(alpha) * float(np.abs(Af).max()),
+                 float(np.abs(Bf).max()), what=what)
+    assert np.isnan(out[:, N:]).all(), what
