@@ -175,8 +175,9 @@ int b2g_gemm_sharded(const void* A_slab, void* B, float* C_slab, int64_t M, int6
  * it with its own B buffer of `bytes` bytes; the root's holds B).  Ranks form a chain
  * root -> root+1 -> ...; each pulls K panels from the previous rank's buffer with peer copies
  * (CUDA IPC) and signals the next rank through epoch flags written by stream memory
- * operations, so the broadcast uses no SM and overlaps the slab GEMMs.  Destroy after every
- * rank's last call has completed.
+ * operations, so the broadcast uses no SM and overlaps the slab GEMMs.  b2g_chain_plan_destroy
+ * is collective too (every rank calls it); it waits for this rank's queued calls, and frees
+ * memory only after every rank has dropped its mappings of it.
  */
 int b2g_chain_plan_create(void* comm, void* B, int64_t bytes, int root, void** plan);
 int b2g_chain_plan_destroy(void* plan);

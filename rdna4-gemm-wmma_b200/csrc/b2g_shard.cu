@@ -592,9 +592,33 @@ extern "C" int b2g_chain_plan_create(void* comm, void* B, int64_t bytes, int roo
 extern "C" int b2g_chain_plan_destroy(void* plan) {
   auto* p = static_cast<b2g_chain_plan*>(plan);
   if (!p) return B2G_OK;
-  cudaStreamSynchronize(p->cs);
+  // Collective.  Every queued call (its copies and its final waits on the caller's stream)
+  // finishes first; then each rank drops its mappings of the neighbours' memory, and only after
+  // all ranks have done so (a small NCCL exchange) does anyone free the flag array the others
+  // had mapped.
+  cudaDeviceSynchronize();
+  for (void*& o : p->opened) {
+    if (o) cudaIpcCloseMemHandle(o);
+    o = nullptr;
+  }
+  int rc = B2G_OK;
+  if (p->world > 1) {
+    NcclApi* n = nccl();
+    int32_t* d = nullptr;
+    if (!n) {
+      rc = sfail(B2G_ERR_NCCL, "NCCL unavailable");
+    } else if (cudaMalloc(&d, sizeof(int32_t) * (p->world + 1)) != cudaSuccess) {
+      rc = sfail(B2G_ERR_CUDA, "cudaMalloc(chain plan barrier)");
+    } else {
+      ncclResult_t r = n->all_gather(d + p->world, d, 1, ncclInt32, p->comm, p->cs);
+      if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather(chain plan barrier)");
+      else if (cudaStreamSynchronize(p->cs) != cudaSuccess)
+        rc = sfail(B2G_ERR_CUDA, "chain plan barrier");
+      cudaFree(d);
+    }
+  }
   plan_free(p);
-  return B2G_OK;
+  return rc;
 }
 
 extern "C" int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_slab, int64_t M,
