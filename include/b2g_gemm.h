@@ -193,6 +193,16 @@ int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_slab, int64_
                            void* stream);
 
 /*
+ * b2g_gemm_sharded_n over a chain plan whose buffer is A (M x K, lda; the root's holds A): A
+ * arrives in row panels along the chain, and panel p's GEMM writes rows of this rank's column
+ * slab of C (B_nslab: K x n_r, C_nslab: M x n_r with (n0, n_r) = b2g_slab_rows(N, world,
+ * rank)) as soon as that panel is here.  No NCCL kernel and no SM are used for A.
+ */
+int b2g_gemm_sharded_n_chain(void* plan, const void* B_nslab, float* C_nslab, int64_t M,
+                             int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                             int m_panels, void* stream);
+
+/*
  * Tensor-parallel variants for shapes whose B is too large to replicate (no reference
  * counterpart).
  *

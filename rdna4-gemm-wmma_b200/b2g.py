@@ -104,6 +104,8 @@ def load(path=None):
     L.b2g_plan_preview.restype = ctypes.c_int
     L.b2g_plan_preview.argtypes = [i64, i64, i64, ctypes.c_int, ctypes.c_int] + \
         [ctypes.POINTER(ctypes.c_int)] * 4
+    L.b2g_gemm_sharded_n_chain.restype = ctypes.c_int
+    L.b2g_gemm_sharded_n_chain.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, vp]
     L.b2g_slab_rows.restype = ctypes.c_int
     L.b2g_slab_rows.argtypes = [i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64),
                                 ctypes.POINTER(ctypes.c_int64)]
@@ -320,6 +322,14 @@ def plan_preview(M, N, K, dtype=0, sm_count=148):
     out = [ctypes.c_int() for _ in range(4)]
     _check(load().b2g_plan_preview(M, N, K, dtype, sm_count, *[ctypes.byref(x) for x in out]))
     return tuple(x.value for x in out)
+
+
+def gemm_sharded_n_chain(plan, B_nslab, C_nslab, M, N, K, m_panels=4, lda=None, ldb=None,
+                         ldc=None, stream=None):
+    """N-slab GEMM with A (the plan's buffer) arriving in row panels through the chain."""
+    _check(load().b2g_gemm_sharded_n_chain(plan, _ptr(B_nslab), _ptr(C_nslab), M, N, K,
+                                           K if lda is None else lda, _ld(B_nslab, ldb, "ldb"),
+                                           _ld(C_nslab, ldc, "ldc"), m_panels, _stream(stream)))
 
 
 def version():

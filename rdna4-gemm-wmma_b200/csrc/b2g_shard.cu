@@ -621,68 +621,67 @@ extern "C" int b2g_chain_plan_destroy(void* plan) {
   return rc;
 }
 
-extern "C" int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_slab, int64_t M,
-                                      int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
-                                      int k_panels, void* stream) {
-  b2g::set_error("");
-  auto* p = static_cast<b2g_chain_plan*>(plan);
-  if (!p || M < 0 || N < 0 || K < 0) return sfail(B2G_ERR_INVALID_ARG, "bad sharded arguments");
-  if (ldb < std::max<int64_t>(N, 1)) return sfail(B2G_ERR_INVALID_ARG, "ldb < N");
-  if (K * ldb * 2 > p->bytes) return sfail(B2G_ERR_INVALID_ARG, "B exceeds the plan's buffer");
+namespace {
+
+// Row panels [r0, r1) of a buffer of `rows` rows: multiples of 64 rows except the last, the
+// first two a quarter of the others (so that the first GEMM starts early) when there are peers.
+std::vector<std::pair<int64_t, int64_t>> chain_panels(int64_t rows, int panels, int world) {
+  const int P = std::max(1, std::min(panels, kMaxPanels - 2));
+  int64_t kp = rows > 0 ? (rows + P - 1) / P : 0;
+  kp = std::max<int64_t>(64, (kp + 63) / 64 * 64);
+  std::vector<std::pair<int64_t, int64_t>> out;
+  int64_t r0 = 0;
+  const int64_t small = std::max<int64_t>(64, (kp / 4 + 63) / 64 * 64);
+  for (int i = 0; r0 < rows; ++i) {
+    const int64_t len = (i < 2 && world > 1) ? small : kp;
+    out.emplace_back(r0, std::min(rows, r0 + len));
+    r0 += len;
+  }
+  if (out.empty()) out.emplace_back(0, 0);
+  return out;
+}
+
+// One call of the chain: rows [r0, r1) of panel i (row pitch `row_bytes`) are pulled from the
+// previous rank (unless this is the root), announced to the next rank, and then handed to
+// `on_panel(i, r0, r1)`, which queues its work on `s` after the panel has arrived.
+template <typename F>
+int chain_pipeline(b2g_chain_plan* p, const std::vector<std::pair<int64_t, int64_t>>& panels,
+                   int64_t row_bytes, cudaStream_t s, F&& on_panel) {
   const DrvApi* d = drv();
   if (!d) return sfail(B2G_ERR_UNSUPPORTED, "stream memory operations unavailable");
-  int64_t row0 = 0, rows = 0;
-  b2g_slab_rows(M, p->world, p->rank, &row0, &rows);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CUstream ccs = reinterpret_cast<CUstream>(p->cs);
-
-  // K panels (multiples of 64 rows except the last), the first two a quarter of the others so
-  // that the first GEMM starts early
-  int P = std::max(1, std::min(k_panels, kMaxPanels - 2));
-  int64_t kp = K > 0 ? (K + P - 1) / P : 0;
-  kp = std::max<int64_t>(64, (kp + 63) / 64 * 64);
-  std::vector<std::pair<int64_t, int64_t>> panels;
-  {
-    int64_t k0 = 0;
-    const int64_t small = std::max<int64_t>(64, (kp / 4 + 63) / 64 * 64);
-    for (int i = 0; k0 < K; ++i) {
-      const int64_t len = (i < 2 && p->world > 1) ? small : kp;
-      panels.emplace_back(k0, std::min(K, k0 + len));
-      k0 += len;
-    }
-    if (panels.empty()) panels.emplace_back(0, 0);
-  }
   if ((int)panels.size() > kMaxPanels) return sfail(B2G_ERR_INVALID_ARG, "too many panels");
+  if (!panels.empty() && panels.back().second * row_bytes > p->bytes)
+    return sfail(B2G_ERR_INVALID_ARG, "the broadcast operand exceeds the plan's buffer");
+  CUstream ccs = reinterpret_cast<CUstream>(p->cs);
   const uint32_t ep = ++p->epoch;
   const bool has_prev = p->prev >= 0, has_next = p->next >= 0;
   auto flag_ptr = [](uint32_t* base, int i) { return reinterpret_cast<CUdeviceptr>(base + i); };
   int rc = B2G_OK;
   auto cu = [&](CUresult r, const char* what) {
-    if (r != CUDA_SUCCESS && rc == B2G_OK) {
-      const char* msg = nullptr;
+    if (r != CUDA_SUCCESS && rc == B2G_OK)
       rc = sfail(B2G_ERR_CUDA, std::string(what) + " failed (CUresult " + std::to_string((int)r) + ")");
-      (void)msg;
-    }
   };
   auto rt = [&](cudaError_t e, const char* what) {
     if (e != cudaSuccess && rc == B2G_OK) rc = cuda_sfail(e, what);
   };
-  // the chain starts after everything queued on the caller's stream (the root writing B, the
-  // previous call's GEMMs reading it)
+  // the chain starts after everything queued on the caller's stream (the root writing the
+  // operand, the previous call's GEMMs reading it)
   rt(cudaEventRecord(p->start, s), "cudaEventRecord");
   rt(cudaStreamWaitEvent(p->cs, p->start, 0), "cudaStreamWaitEvent");
-  // this rank's B is overwritten only after the next rank finished pulling the previous call's
+  // this rank's buffer is overwritten only after the next rank finished pulling the previous
+  // call's panels from it
   if (has_prev && has_next)
     cu(d->wait32(ccs, flag_ptr(p->flags, kMaxPanels), ep - 1, CU_STREAM_WAIT_VALUE_GEQ),
        "cuStreamWaitValue32(done)");
   for (size_t i = 0; i < panels.size() && rc == B2G_OK; ++i) {
-    const int64_t k0 = panels[i].first, k1 = panels[i].second;
-    const size_t off = (size_t)(k0 * ldb * 2), len = (size_t)((k1 - k0) * ldb * 2);
+    const int64_t r0 = panels[i].first, r1 = panels[i].second;
+    const size_t off = (size_t)(r0 * row_bytes), len = (size_t)((r1 - r0) * row_bytes);
     if (has_prev) {
       cu(d->wait32(ccs, flag_ptr(p->flags, (int)i), ep, CU_STREAM_WAIT_VALUE_GEQ),
          "cuStreamWaitValue32(panel)");
-      if (len) rt(cudaMemcpyAsync(p->buf + off, p->prev_buf + off, len, cudaMemcpyDeviceToDevice, p->cs),
-                  "cudaMemcpyAsync(peer panel)");
+      if (len)
+        rt(cudaMemcpyAsync(p->buf + off, p->prev_buf + off, len, cudaMemcpyDeviceToDevice, p->cs),
+           "cudaMemcpyAsync(peer panel)");
     }
     if (has_next)
       cu(d->write32(ccs, flag_ptr(p->next_flags, (int)i), ep, 0), "cuStreamWriteValue32(panel)");
@@ -690,11 +689,7 @@ extern "C" int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_s
       rt(cudaEventRecord(p->panel_ev[i], p->cs), "cudaEventRecord(panel)");
       rt(cudaStreamWaitEvent(s, p->panel_ev[i], 0), "cudaStreamWaitEvent(panel)");
     }
-    if (rc == B2G_OK && rows > 0) {
-      const char* ap = static_cast<const char*>(A_slab) + k0 * 2;
-      const char* bp = p->buf + off;
-      rc = b2g_gemm_ex(ap, bp, C_slab, rows, N, k1 - k0, lda, ldb, ldc, 1.0f, i == 0 ? 0.0f : 1.0f, s);
-    }
+    if (rc == B2G_OK) rc = on_panel(i, r0, r1);
   }
   if (has_prev)  // tell the previous rank that its buffer is free again
     cu(d->write32(ccs, flag_ptr(p->prev_flags, kMaxPanels), ep, 0), "cuStreamWriteValue32(done)");
@@ -707,4 +702,46 @@ extern "C" int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_s
                  CU_STREAM_WAIT_VALUE_GEQ),
        "cuStreamWaitValue32(next done)");
   return rc;
+}
+
+}  // namespace
+
+extern "C" int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_slab, int64_t M,
+                                      int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                                      int k_panels, void* stream) {
+  b2g::set_error("");
+  auto* p = static_cast<b2g_chain_plan*>(plan);
+  if (!p || M < 0 || N < 0 || K < 0) return sfail(B2G_ERR_INVALID_ARG, "bad sharded arguments");
+  if (ldb < std::max<int64_t>(N, 1)) return sfail(B2G_ERR_INVALID_ARG, "ldb < N");
+  int64_t row0 = 0, rows = 0;
+  b2g_slab_rows(M, p->world, p->rank, &row0, &rows);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // B arrives in K-row panels; the slab GEMM of panel i covers that K range (panel 0
+  // overwrites C, the others add into it)
+  return chain_pipeline(p, chain_panels(K, k_panels, p->world), ldb * 2, s,
+                        [&](size_t i, int64_t k0, int64_t k1) -> int {
+                          if (rows <= 0) return B2G_OK;
+                          return b2g_gemm_ex(static_cast<const char*>(A_slab) + k0 * 2,
+                                             p->buf + k0 * ldb * 2, C_slab, rows, N, k1 - k0, lda,
+                                             ldb, ldc, 1.0f, i == 0 ? 0.0f : 1.0f, s);
+                        });
+}
+
+extern "C" int b2g_gemm_sharded_n_chain(void* plan, const void* B_nslab, float* C_nslab, int64_t M,
+                                        int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                                        int64_t ldc, int m_panels, void* stream) {
+  b2g::set_error("");
+  auto* p = static_cast<b2g_chain_plan*>(plan);
+  if (!p || M < 0 || N < 0 || K < 0) return sfail(B2G_ERR_INVALID_ARG, "bad sharded arguments");
+  if (lda < std::max<int64_t>(K, 1)) return sfail(B2G_ERR_INVALID_ARG, "lda < K");
+  int64_t n0 = 0, nr = 0;
+  b2g_slab_rows(N, p->world, p->rank, &n0, &nr);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // A arrives in row panels; panel i's GEMM writes rows [m0, m1) of this rank's column slab
+  return chain_pipeline(p, chain_panels(M, m_panels, p->world), lda * 2, s,
+                        [&](size_t, int64_t m0, int64_t m1) -> int {
+                          if (nr <= 0 || m1 <= m0) return B2G_OK;
+                          return b2g_gemm_ex(p->buf + m0 * lda * 2, B_nslab, C_nslab + m0 * ldc,
+                                             m1 - m0, nr, K, lda, ldb, ldc, 1.0f, 0.0f, s);
+                        });
 }

@@ -288,3 +288,44 @@ def nccl_chain_rank(rank, world, uid_path, M, N, K, panels, calls, out_q):
         out_q.put((rank, rows, worst, status, b_ok, None))
     except Exception:
         out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))
+
+
+def nccl_n_chain_rank(rank, world, uid_path, M, N, K, panels, calls, out_q):
+    """b2g_gemm_sharded_n_chain on `world` GPUs: A (filled on the root only, a new seed before
+    each call) reaches every rank through the copy-engine chain; this rank's column slab of C
+    is checked on sampled rows, and A must be bit-exact on every rank."""
+    try:
+        import torch
+        from oracle import orc
+        b2g = _load_pkg("b2g")
+        torch.cuda.set_device(rank)
+        comm = _nccl_comm(b2g, rank, world, uid_path)
+        n0, nr = b2g.slab_rows(N, world, rank)
+        dA = torch.full((M, K), float("nan"), dtype=torch.float16, device="cuda")
+        dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+        b2g.fill_uniform(dB, K * N, 2)
+        dBn = dB[:, n0:n0 + nr].contiguous()
+        plan = b2g.chain_plan_create(comm, dA, M * K * 2, 0)
+        stream = torch.cuda.current_stream()
+        B = orc.uniform_f16((K, N), 2)
+        worst, a_ok = 0, True
+        for c in range(calls):
+            seed = 200 + c
+            if rank == 0:
+                b2g.fill_uniform(dA, M * K, seed, 0, stream.cuda_stream)
+            dCn = torch.full((M, max(nr, 1)), float("nan"), dtype=torch.float32, device="cuda")
+            b2g.gemm_sharded_n_chain(plan, dBn, dCn, M, N, K, m_panels=panels, ldc=max(nr, 1),
+                                     stream=stream.cuda_stream)
+            torch.cuda.synchronize()
+            for r in sorted(set([0, M - 1, M // 2, M // 3])):
+                a = orc.uniform_f16((1, K), seed, r * K)
+                ref = orc.gemm_f64(a, B)[:, n0:n0 + nr]
+                worst = max(worst, orc.check(dCn[r:r + 1, :nr].cpu().numpy(), ref, K, 1.0, 1.0)[0])
+            a_ok = a_ok and bool(torch.equal(dA.cpu().view(torch.int16),
+                                             torch.from_numpy(orc.uniform_f16((M, K), seed).view(np.int16))))
+        status = b2g.device_status()
+        b2g.chain_plan_destroy(plan)
+        b2g.comm_destroy(comm)
+        out_q.put((rank, nr, worst, status, a_ok, None))
+    except Exception:
+        out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))

@@ -157,3 +157,35 @@ def test_chain_multi_rank(b2g, cuda, world, M, N, K, panels):
         assert tb is None, tb
         assert worst == 0 and status == 0 and b_ok, (rank, rows, worst, status, b_ok)
     assert sum(r[1] for r in res) == M
+
+
+def test_n_chain_single_rank(b2g, cuda):
+    with tempfile.TemporaryDirectory() as d:
+        q = _ListQueue()
+        shard_worker.nccl_n_chain_rank(0, 1, os.path.join(d, "id"), 512, 768, 1024, 3, 2, q)
+    rank, nr, worst, status, a_ok, tb = q[0]
+    assert tb is None, tb
+    assert worst == 0 and status == 0 and a_ok
+
+
+@pytest.mark.parametrize("world,M,N,K,panels", [(2, 2048, 1536, 2048, 6), (2, 300, 520, 200, 3)])
+def test_n_chain_multi_rank(b2g, cuda, world, M, N, K, panels):
+    """N-slab GEMM with A arriving through the copy-engine chain: three calls, the root
+    rewriting A before each; every rank's column slab checked and A bit-exact on every rank."""
+    if cuda.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=shard_worker.nccl_n_chain_rank,
+                             args=(r, world, os.path.join(d, "id"), M, N, K, panels, 3, q))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        res = sorted(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=120)
+    for rank, nr, worst, status, a_ok, tb in res:
+        assert tb is None, tb
+        assert worst == 0 and status == 0 and a_ok, (rank, nr, worst, status, a_ok)
+    assert sum(r[1] for r in res) == N
