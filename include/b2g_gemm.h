@@ -47,6 +47,7 @@ enum {
   B2G_DTYPE_BF16 = 1, /* bfloat16 */
   B2G_DTYPE_E4M3 = 2, /* fp8 e4m3 (OCP / NVIDIA __nv_fp8_e4m3) */
   B2G_DTYPE_E5M2 = 3, /* fp8 e5m2 */
+  B2G_DTYPE_F32 = 4,  /* IEEE binary32: output (C) type only */
 };
 
 /* Which kernel the calling thread's last successful compute call ran. */
@@ -234,6 +235,22 @@ int b2g_gemm_sharded_n(void* A, const void* B_nslab, float* C_nslab, int64_t M, 
  */
 int b2g_plan_preview(int64_t M, int64_t N, int64_t K, int dtype, int sm_count, int* cta_group,
                      int* tile_n, int* k_splits, int* num_full);
+
+/*
+ * Fused epilogue variants: C = alpha*A.B + beta*C + bias, with C stored as fp32
+ * (B2G_DTYPE_F32), fp16 (B2G_DTYPE_F16) or bf16 (B2G_DTYPE_BF16).  `bias` is an optional
+ * (NULL = none) fp32 vector of N elements added to every row; `dtype` is the A/B operand type
+ * as in b2g_gemm_typed.  A 16-bit C is rounded to nearest even from the fp32 result and takes
+ * beta = 0 only; C's leading dimension (ldc) and strides are in C elements.  No reference
+ * counterpart (the reference's kernels always write fp32 C with no bias).
+ */
+int b2g_gemm_epilogue(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                      int64_t lda, int64_t ldb, int64_t ldc, int dtype, float alpha, float beta,
+                      const float* bias, int c_dtype, void* stream);
+int b2g_contract5d_epilogue(const void* A, const int64_t a_shape[5], const int64_t a_stride[5],
+                            const void* B, const int64_t b_shape[3], const int64_t b_stride[3],
+                            void* C, const int64_t c_shape[4], const int64_t c_stride[4], int dtype,
+                            float alpha, float beta, const float* bias, int c_dtype, void* stream);
 
 /* Balanced contiguous row partition: rank r gets M/world rows, the first M%world ranks one more. */
 int b2g_slab_rows(int64_t M, int world, int rank, int64_t* row0, int64_t* rows);

@@ -24,7 +24,7 @@ ERR_CUDA = 3
 ERR_TIMEOUT = 4
 ERR_NCCL = 5
 
-DTYPE_F16, DTYPE_BF16, DTYPE_E4M3, DTYPE_E5M2 = 0, 1, 2, 3
+DTYPE_F16, DTYPE_BF16, DTYPE_E4M3, DTYPE_E5M2, DTYPE_F32 = 0, 1, 2, 3, 4
 
 PATH_NONE, PATH_TC_1CTA, PATH_TC_2CTA, PATH_GENERIC, PATH_ZERO, PATH_EMPTY = range(6)
 PATH_NAMES = {0: "none", 1: "tc_1cta", 2: "tc_2cta", 3: "generic", 4: "zero", 5: "empty"}
@@ -106,6 +106,13 @@ def load(path=None):
         [ctypes.POINTER(ctypes.c_int)] * 4
     L.b2g_gemm_sharded_n_chain.restype = ctypes.c_int
     L.b2g_gemm_sharded_n_chain.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, vp]
+    L.b2g_gemm_epilogue.restype = ctypes.c_int
+    L.b2g_gemm_epilogue.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int,
+                                    ctypes.c_float, ctypes.c_float, vp, ctypes.c_int, vp]
+    L.b2g_contract5d_epilogue.restype = ctypes.c_int
+    L.b2g_contract5d_epilogue.argtypes = [vp, i64p, i64p, vp, i64p, i64p, vp, i64p, i64p,
+                                          ctypes.c_int, ctypes.c_float, ctypes.c_float, vp,
+                                          ctypes.c_int, vp]
     L.b2g_slab_rows.restype = ctypes.c_int
     L.b2g_slab_rows.argtypes = [i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64),
                                 ctypes.POINTER(ctypes.c_int64)]
@@ -330,6 +337,23 @@ def gemm_sharded_n_chain(plan, B_nslab, C_nslab, M, N, K, m_panels=4, lda=None, 
     _check(load().b2g_gemm_sharded_n_chain(plan, _ptr(B_nslab), _ptr(C_nslab), M, N, K,
                                            K if lda is None else lda, _ld(B_nslab, ldb, "ldb"),
                                            _ld(C_nslab, ldc, "ldc"), m_panels, _stream(stream)))
+
+
+def gemm_epilogue(A, B, C, M, N, K, dtype=0, alpha=1.0, beta=0.0, bias=None, c_dtype=4,
+                  lda=None, ldb=None, ldc=None, stream=None):
+    """C = alpha*A.B + beta*C + bias with C of type c_dtype (DTYPE_F32 / DTYPE_F16 / DTYPE_BF16)."""
+    _check(load().b2g_gemm_epilogue(_ptr(A), _ptr(B), _ptr(C), M, N, K, K if lda is None else lda,
+                                    N if ldb is None else ldb, N if ldc is None else ldc, dtype,
+                                    float(alpha), float(beta), _ptr(bias), c_dtype,
+                                    _stream(stream)))
+
+
+def contract5d_epilogue(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, dtype=0,
+                        alpha=1.0, beta=0.0, bias=None, c_dtype=4, stream=None):
+    _check(load().b2g_contract5d_epilogue(_ptr(A), _arr(a_shape, 5), _arr(a_stride, 5), _ptr(B),
+                                          _arr(b_shape, 3), _arr(b_stride, 3), _ptr(C),
+                                          _arr(c_shape, 4), _arr(c_stride, 4), dtype, float(alpha),
+                                          float(beta), _ptr(bias), c_dtype, _stream(stream)))
 
 
 def version():

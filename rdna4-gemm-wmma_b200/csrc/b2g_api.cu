@@ -181,9 +181,12 @@ __device__ __forceinline__ float elem_f32(const void* base, int64_t i) {
     return float(static_cast<const __nv_fp8_e5m2*>(base)[i]);
 }
 
+// c_type: 0 = fp32 C (C = alpha*A.B + bias + beta*C), 1 = fp16 C, 2 = bf16 C (beta is 0 for
+// the 16-bit types: C = round(alpha*A.B + bias)).  bias: per-column fp32 vector or null.
 template <int DT>
 __global__ void gemm_generic_kernel(const void* __restrict__ A, const void* __restrict__ B,
-                                    float* __restrict__ C, const Geo g, float alpha, float beta) {
+                                    void* __restrict__ C, const Geo g, float alpha, float beta,
+                                    const float* __restrict__ bias, int c_type) {
   const int64_t rows = g.as[0] * g.as[1] * g.as[2];
   const int64_t total = rows * g.n;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -199,9 +202,17 @@ __global__ void gemm_generic_kernel(const void* __restrict__ A, const void* __re
       for (int64_t k = 0; k < g.as[4]; ++k)
         acc += elem_f32<DT>(A, ar + j * g.ast[3] + k * g.ast[4]) *
                elem_f32<DT>(B, bc + j * g.bst[0] + k * g.bst[1]);
-    float* c = C + ia * g.cst[0] + ib * g.cst[1] + ii * g.cst[2] + col * g.cst[3];
-    const float out = alpha == 1.0f ? acc : alpha * acc;
-    *c = beta == 0.0f ? out : out + beta * *c;  // beta == 0: C is not read
+    const int64_t ci = ia * g.cst[0] + ib * g.cst[1] + ii * g.cst[2] + col * g.cst[3];
+    float out = alpha == 1.0f ? acc : alpha * acc;
+    if (bias) out += bias[col];
+    if (c_type == 0) {
+      float* c = static_cast<float*>(C) + ci;
+      *c = beta == 0.0f ? out : out + beta * *c;  // beta == 0: C is not read
+    } else if (c_type == 1) {
+      static_cast<__half*>(C)[ci] = __float2half_rn(out);
+    } else {
+      static_cast<__nv_bfloat16*>(C)[ci] = __float2bfloat16_rn(out);
+    }
   }
 }
 
@@ -408,12 +419,19 @@ static inline CUtensorMapDataType dt_map(int dt) {
 }
 
 // ------------------------------------------------------------------ core dispatch
+// c_type: 0 = fp32 C, 1 = fp16 C, 2 = bf16 C (16-bit C requires beta == 0); bias: optional
+// per-column fp32 vector of N elements added once to every row of alpha*A.B.
 static int run(const void* A, const int64_t as[5], const int64_t ast[5], const void* B,
-               const int64_t bs[3], const int64_t bst[3], float* Cp, const int64_t cs[4],
+               const int64_t bs[3], const int64_t bst[3], void* Cv, const int64_t cs[4],
                const int64_t cst[4], int dtype, float alpha, float beta, cudaStream_t stream,
-               const FixedScratch* fixed = nullptr) {
+               const FixedScratch* fixed = nullptr, const float* bias = nullptr, int c_type = 0) {
   if (dtype < B2G_DTYPE_F16 || dtype > B2G_DTYPE_E5M2)
     return fail(B2G_ERR_INVALID_ARG, "unknown operand type code %d", dtype);
+  if (c_type < 0 || c_type > 2) return fail(B2G_ERR_INVALID_ARG, "unknown output type");
+  if (c_type != 0 && beta != 0.0f)
+    return fail(B2G_ERR_INVALID_ARG, "a 16-bit C takes beta = 0 only (got %g)", (double)beta);
+  float* Cp = static_cast<float*>(Cv);
+  const int c_esz = c_type == 0 ? 4 : 2;
   const int esz = dt_size(dtype);
   const int kb_elems = kRowBytes / esz;  // K elements per 128-byte stage row
   const CUtensorMapDataType map_type = dt_map(dtype);
@@ -461,16 +479,16 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     const Geo g = make_geo();
     switch (dtype) {
       case B2G_DTYPE_F16:
-        gemm_generic_kernel<B2G_DTYPE_F16><<<eblocks, eth, 0, stream>>>(A, B, Cp, g, alpha, beta);
+        gemm_generic_kernel<B2G_DTYPE_F16><<<eblocks, eth, 0, stream>>>(A, B, Cv, g, alpha, beta, bias, c_type);
         break;
       case B2G_DTYPE_BF16:
-        gemm_generic_kernel<B2G_DTYPE_BF16><<<eblocks, eth, 0, stream>>>(A, B, Cp, g, alpha, beta);
+        gemm_generic_kernel<B2G_DTYPE_BF16><<<eblocks, eth, 0, stream>>>(A, B, Cv, g, alpha, beta, bias, c_type);
         break;
       case B2G_DTYPE_E4M3:
-        gemm_generic_kernel<B2G_DTYPE_E4M3><<<eblocks, eth, 0, stream>>>(A, B, Cp, g, alpha, beta);
+        gemm_generic_kernel<B2G_DTYPE_E4M3><<<eblocks, eth, 0, stream>>>(A, B, Cv, g, alpha, beta, bias, c_type);
         break;
       default:
-        gemm_generic_kernel<B2G_DTYPE_E5M2><<<eblocks, eth, 0, stream>>>(A, B, Cp, g, alpha, beta);
+        gemm_generic_kernel<B2G_DTYPE_E5M2><<<eblocks, eth, 0, stream>>>(A, B, Cv, g, alpha, beta, bias, c_type);
         break;
     }
     cudaError_t e = cudaGetLastError();
@@ -480,8 +498,8 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     return B2G_OK;
   };
 
-  if (K == 0 || alpha == 0.0f) {  // C = beta*C
-    if (beta == 1.0f) {
+  if (K == 0 || alpha == 0.0f) {  // C = beta*C (+ bias)
+    if (beta == 1.0f && !bias) {
       t_path = B2G_PATH_ZERO;
       return B2G_OK;
     }
@@ -513,6 +531,9 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   const bool c_n = (c_sn == 1) || N == 1;           // N contiguous
   const bool c_m = !c_n && M3[2].sc == 1;           // innermost M mode contiguous
   if (!a_ok || !(b_mn || b_k) || !(c_n || c_m)) return launch_generic(B2G_PATH_GENERIC);
+  // 16-bit C: row-major (N-contiguous) layouts only; the bias is read 16 bytes at a time
+  if ((c_type != 0 && !c_n) || (bias && !al16((int64_t)(uintptr_t)bias)))
+    return launch_generic(B2G_PATH_GENERIC);
 
   // ---- M decomposition: 128-row load box over (i, b, a)
   const int64_t isz = M3[2].size, bsz = M3[1].size, asz = M3[0].size;
@@ -546,11 +567,11 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   // every M mode is an outer dimension of A; of C too, except the innermost one when C is
   // M-contiguous (it is then the map's unit-stride dimension 0)
   for (int t = 0; t < 3; ++t)
-    tma_ok = tma_ok && stride_ok(M3[t], true, esz) && ((c_m && t == 2) || stride_ok(M3[t], false, 4));
+    tma_ok = tma_ok && stride_ok(M3[t], true, esz) && ((c_m && t == 2) || stride_ok(M3[t], false, c_esz));
   tma_ok = tma_ok && stride_ok(K2[0], true, esz) && stride_ok(K2[0], false, esz);
   if (b_mn) tma_ok = tma_ok && stride_ok(K2[1], false, esz);
   if (b_k) tma_ok = tma_ok && (N == 1 || al16(b_sn * esz));
-  if (c_m) tma_ok = tma_ok && (N == 1 || al16(c_sn * 4));
+  if (c_m) tma_ok = tma_ok && (N == 1 || al16(c_sn * c_esz));
   if (!tma_ok) return launch_generic(B2G_PATH_GENERIC);
 
   if (!get_encode()) return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
@@ -605,14 +626,19 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map B (K-major) not encodable
   }
   // C
-  if (c_n) {  // dims (n, i, b, a), 128-byte swizzled 32x32 boxes
+  if (c_n) {  // dims (n, i, b, a), 32x32 boxes: fp32 rows of 128 bytes (128-byte swizzle) or
+              // 16-bit rows of 64 bytes (64-byte swizzle)
     cuuint64_t dims[4] = {(cuuint64_t)N, (cuuint64_t)isz, (cuuint64_t)bsz, (cuuint64_t)asz};
     cuuint64_t st[3];
-    st[0] = fill(M3[2].sc * 4, isz, N * 4);
-    st[1] = fill(M3[1].sc * 4, bsz, (int64_t)st[0] * isz);
-    st[2] = fill(M3[0].sc * 4, asz, (int64_t)st[1] * bsz);
+    st[0] = fill(M3[2].sc * c_esz, isz, N * c_esz);
+    st[1] = fill(M3[1].sc * c_esz, bsz, (int64_t)st[0] * isz);
+    st[2] = fill(M3[0].sc * c_esz, asz, (int64_t)st[1] * bsz);
     cuuint32_t box[4] = {32, (cuuint32_t)si, (cuuint32_t)sb, (cuuint32_t)sa};
-    CUresult r = encode_cached(&tmC, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Cp, dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B,
+    const CUtensorMapDataType ct = c_type == 0 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : c_type == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    CUresult r = encode_cached(&tmC, ct, 4, Cv, dims, st, box,
+                               c_type == 0 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                                CU_TENSOR_MAP_L2_PROMOTION_NONE);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map C (N-major) not encodable
   } else {  // dims (i, n, b, a), unswizzled si x 32 boxes
@@ -646,6 +672,8 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   int rg = (int)opt_raster_group.load();
   p.raster_group = rg > 0 ? rg : (cg == 2 ? 8 : 16);  // measured best on 8192^3
   p.store_hint = (int)opt_store_hint.load();
+  p.c_type = c_type;
+  p.bias = bias;
   p.alpha = alpha;
   p.accumulate = beta != 0.0f ? 1 : 0;
   if (beta != 0.0f && beta != 1.0f) {  // C = beta*C first; the kernel then adds alpha*A.B
@@ -991,6 +1019,49 @@ extern "C" int b2g_contract5d_typed(const void* A, const int64_t a_shape[5],
     return fail(B2G_ERR_INVALID_ARG, "null shape/stride array");
   return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, dtype, alpha, beta,
              static_cast<cudaStream_t>(stream));
+}
+
+static int out_type(int c_dtype, int* c_type) {
+  switch (c_dtype) {
+    case B2G_DTYPE_F32: *c_type = 0; return B2G_OK;
+    case B2G_DTYPE_F16: *c_type = 1; return B2G_OK;
+    case B2G_DTYPE_BF16: *c_type = 2; return B2G_OK;
+    default: return fail(B2G_ERR_INVALID_ARG, "unsupported output type code %d", c_dtype);
+  }
+}
+
+extern "C" int b2g_gemm_epilogue(const void* A, const void* B, void* C, int64_t M, int64_t N,
+                                 int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int dtype,
+                                 float alpha, float beta, const float* bias, int c_dtype,
+                                 void* stream) {
+  t_err.clear();
+  int c_type = 0;
+  int rc = out_type(c_dtype, &c_type);
+  if (rc) return rc;
+  if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
+  if (lda < std::max<int64_t>(K, 1) || ldb < std::max<int64_t>(N, 1) || ldc < std::max<int64_t>(N, 1))
+    return fail(B2G_ERR_INVALID_ARG, "leading dimension smaller than the row length");
+  const int64_t as[5] = {1, 1, M, 1, K}, ast[5] = {0, 0, lda, 0, 1};
+  const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
+  const int64_t cs[4] = {1, 1, M, N}, cst[4] = {0, 0, ldc, 1};
+  return run(A, as, ast, B, bs, bst, C, cs, cst, dtype, alpha, beta,
+             static_cast<cudaStream_t>(stream), nullptr, bias, c_type);
+}
+
+extern "C" int b2g_contract5d_epilogue(const void* A, const int64_t a_shape[5],
+                                       const int64_t a_stride[5], const void* B,
+                                       const int64_t b_shape[3], const int64_t b_stride[3], void* C,
+                                       const int64_t c_shape[4], const int64_t c_stride[4],
+                                       int dtype, float alpha, float beta, const float* bias,
+                                       int c_dtype, void* stream) {
+  t_err.clear();
+  int c_type = 0;
+  int rc = out_type(c_dtype, &c_type);
+  if (rc) return rc;
+  if (!a_shape || !a_stride || !b_shape || !b_stride || !c_shape || !c_stride)
+    return fail(B2G_ERR_INVALID_ARG, "null shape/stride array");
+  return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, dtype, alpha, beta,
+             static_cast<cudaStream_t>(stream), nullptr, bias, c_type);
 }
 
 extern "C" const char* b2g_last_error_string(void) { return t_err.c_str(); }

@@ -21,6 +21,8 @@
 // warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. 32*(w%4)+31).
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cstdint>
 
 #include "ptx.cuh"
@@ -62,6 +64,9 @@ struct GemmParams {
   int store_hint;              // 1 = C stores carry an L2 evict-first hint
   int accumulate;              // 1 = C += alpha*A.B (TMA reduce-add), 0 = C = alpha*A.B
   float alpha;                 // scale of A.B
+  int c_type;                  // C element type: 0 = fp32, 1 = fp16, 2 = bf16 (16-bit: row-major
+                               // C, no accumulate)
+  const float* bias;           // per-column fp32 bias added to alpha*A.B, or null
   // Work units: the first num_full tiles (in tile order) are one unit each over all of K; each
   // remaining tile is split into k_splits units, split s covering the K blocks
   // [s*k_per_split, min(k_iters, (s+1)*k_per_split)).  num_full = 0 is plain split-K (too few
@@ -434,7 +439,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           w[j] = p.alpha == 1.0f ? v[j] : __float_as_uint(__uint_as_float(v[j]) * p.alpha);
-        if constexpr (!C_MCONTIG) {
+        if (p.bias) {
+          // the same 32 bias values for every lane (broadcast loads); columns past N are not
+          // read (the store clips them)
+          if (gcol + 32 <= p.n_size) {
+            const float4* bq = reinterpret_cast<const float4*>(p.bias + gcol);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 b = __ldg(bq + j);
+              w[4 * j] = __float_as_uint(__uint_as_float(w[4 * j]) + b.x);
+              w[4 * j + 1] = __float_as_uint(__uint_as_float(w[4 * j + 1]) + b.y);
+              w[4 * j + 2] = __float_as_uint(__uint_as_float(w[4 * j + 2]) + b.z);
+              w[4 * j + 3] = __float_as_uint(__uint_as_float(w[4 * j + 3]) + b.w);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (gcol + j < p.n_size)
+                w[j] = __float_as_uint(__uint_as_float(w[j]) + __ldg(p.bias + gcol + j));
+          }
+        }
+        if (p.c_type != 0) {
+          // 16-bit C: row `lane` as 4 16-byte chunks (32 values rounded to nearest), 64-byte
+          // swizzle: chunk j -> j ^ ((row / 2) % 4)
+          uint32_t h[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float x0 = __uint_as_float(w[2 * j]), x1 = __uint_as_float(w[2 * j + 1]);
+            if (p.c_type == 1) {
+              const __half2 t = __floats2half2_rn(x0, x1);
+              h[j] = *reinterpret_cast<const uint32_t*>(&t);
+            } else {
+              const __nv_bfloat162 t = __floats2bfloat162_rn(x0, x1);
+              h[j] = *reinterpret_cast<const uint32_t*>(&t);
+            }
+          }
+          const uint32_t row = buf + (uint32_t)lane * 64u;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            ptx::st_shared_v4(row + (uint32_t)((j ^ ((lane >> 1) & 3)) << 4), h[4 * j],
+                              h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
+        } else         if constexpr (!C_MCONTIG) {
           // Row `lane` as 8 16-byte chunks, 128-byte swizzle: chunk j -> j ^ (row % 8).
           const uint32_t row = buf + (uint32_t)lane * 128u;
 #pragma unroll
