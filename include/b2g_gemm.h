@@ -252,6 +252,23 @@ int b2g_contract5d_epilogue(const void* A, const int64_t a_shape[5], const int64
                             void* C, const int64_t c_shape[4], const int64_t c_stride[4], int dtype,
                             float alpha, float beta, const float* bias, int c_dtype, void* stream);
 
+/*
+ * Batch modes: the contraction with mode a shared by B,
+ *   C[a,b,i,n] = alpha * sum_{j,k} A[a,b,i,j,k] B[a,j,k,n] + beta * C[a,b,i,n],
+ * B's element (a, j, k, n) at a*b_batch_stride + j*b_stride[0] + k*b_stride[1] +
+ * n*b_stride[2].  b2g_gemm_batched is the strided-batched GEMM C[l] = A[l].B[l] (fp16 in,
+ * fp32 out) over l < L with batch strides in elements.  Batched calls use one-CTA tiles.  No
+ * reference counterpart (generalises mmmTensor.cpp's fixed (a,b,i | j,k | n) roles).
+ */
+int b2g_contract5d_batched(const void* A, const int64_t a_shape[5], const int64_t a_stride[5],
+                           const void* B, const int64_t b_shape[3], const int64_t b_stride[3],
+                           int64_t b_batch_stride, float* C, const int64_t c_shape[4],
+                           const int64_t c_stride[4], int dtype, float alpha, float beta,
+                           void* stream);
+int b2g_gemm_batched(const void* A, const void* B, float* C, int64_t L, int64_t M, int64_t N,
+                     int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a,
+                     int64_t stride_b, int64_t stride_c, void* stream);
+
 /* Balanced contiguous row partition: rank r gets M/world rows, the first M%world ranks one more. */
 int b2g_slab_rows(int64_t M, int world, int rank, int64_t* row0, int64_t* rows);
 

@@ -113,6 +113,11 @@ def load(path=None):
     L.b2g_contract5d_epilogue.argtypes = [vp, i64p, i64p, vp, i64p, i64p, vp, i64p, i64p,
                                           ctypes.c_int, ctypes.c_float, ctypes.c_float, vp,
                                           ctypes.c_int, vp]
+    L.b2g_contract5d_batched.restype = ctypes.c_int
+    L.b2g_contract5d_batched.argtypes = [vp, i64p, i64p, vp, i64p, i64p, i64, vp, i64p, i64p,
+                                         ctypes.c_int, ctypes.c_float, ctypes.c_float, vp]
+    L.b2g_gemm_batched.restype = ctypes.c_int
+    L.b2g_gemm_batched.argtypes = [vp, vp, vp] + [i64] * 10 + [vp]
     L.b2g_slab_rows.restype = ctypes.c_int
     L.b2g_slab_rows.argtypes = [i64, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int64),
                                 ctypes.POINTER(ctypes.c_int64)]
@@ -354,6 +359,24 @@ def contract5d_epilogue(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, 
                                           _arr(b_shape, 3), _arr(b_stride, 3), _ptr(C),
                                           _arr(c_shape, 4), _arr(c_stride, 4), dtype, float(alpha),
                                           float(beta), _ptr(bias), c_dtype, _stream(stream)))
+
+
+def gemm_batched(A, B, C, L, M, N, K, stride_a, stride_b, stride_c, lda=None, ldb=None,
+                 ldc=None, stream=None):
+    """C[l] = A[l].B[l] for l < L (batch strides in elements)."""
+    _check(load().b2g_gemm_batched(_ptr(A), _ptr(B), _ptr(C), L, M, N, K,
+                                   K if lda is None else lda, N if ldb is None else ldb,
+                                   N if ldc is None else ldc, stride_a, stride_b, stride_c,
+                                   _stream(stream)))
+
+
+def contract5d_batched(A, a_shape, a_stride, B, b_shape, b_stride, b_batch_stride, C, c_shape,
+                       c_stride, dtype=0, alpha=1.0, beta=0.0, stream=None):
+    """C[a,b,i,n] = alpha*sum_{j,k} A[a,b,i,j,k] B[a,j,k,n] + beta*C (mode a is a batch mode)."""
+    _check(load().b2g_contract5d_batched(_ptr(A), _arr(a_shape, 5), _arr(a_stride, 5), _ptr(B),
+                                         _arr(b_shape, 3), _arr(b_stride, 3), b_batch_stride,
+                                         _ptr(C), _arr(c_shape, 4), _arr(c_stride, 4), dtype,
+                                         float(alpha), float(beta), _stream(stream)))
 
 
 def version():

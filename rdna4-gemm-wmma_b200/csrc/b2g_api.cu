@@ -164,6 +164,7 @@ static int device_state(int dev, DevState** out) {
 struct Geo {
   int64_t as[5], ast[5];  // a,b,i,j,k
   int64_t bst[3];         // j,k,n strides
+  int64_t b_batch;        // B stride along mode a (0: B is shared by every a)
   int64_t n;              // N
   int64_t cst[4];         // a,b,i,n strides
 };
@@ -196,7 +197,7 @@ __global__ void gemm_generic_kernel(const void* __restrict__ A, const void* __re
     const int64_t ib = (row / g.as[2]) % g.as[1];
     const int64_t ia = row / (g.as[2] * g.as[1]);
     const int64_t ar = ia * g.ast[0] + ib * g.ast[1] + ii * g.ast[2];
-    const int64_t bc = col * g.bst[2];
+    const int64_t bc = col * g.bst[2] + ia * g.b_batch;
     float acc = 0.0f;
     for (int64_t j = 0; j < g.as[3]; ++j)
       for (int64_t k = 0; k < g.as[4]; ++k)
@@ -424,7 +425,9 @@ static inline CUtensorMapDataType dt_map(int dt) {
 static int run(const void* A, const int64_t as[5], const int64_t ast[5], const void* B,
                const int64_t bs[3], const int64_t bst[3], void* Cv, const int64_t cs[4],
                const int64_t cst[4], int dtype, float alpha, float beta, cudaStream_t stream,
-               const FixedScratch* fixed = nullptr, const float* bias = nullptr, int c_type = 0) {
+               const FixedScratch* fixed = nullptr, const float* bias = nullptr, int c_type = 0,
+               int64_t b_batch = -1) {
+  // b_batch >= 0: mode a is a batch mode, B[a][j][k][n] with stride b_batch along a
   if (dtype < B2G_DTYPE_F16 || dtype > B2G_DTYPE_E5M2)
     return fail(B2G_ERR_INVALID_ARG, "unknown operand type code %d", dtype);
   if (c_type < 0 || c_type > 2) return fail(B2G_ERR_INVALID_ARG, "unknown output type");
@@ -468,6 +471,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     }
     for (int t = 0; t < 3; ++t) g.bst[t] = bst[t];
     for (int t = 0; t < 4; ++t) g.cst[t] = cst[t];
+    g.b_batch = b_batch >= 0 ? b_batch : 0;
     g.n = N;
     return g;
   };
@@ -509,8 +513,10 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   if (ds->cc_major != 10) return launch_generic(B2G_PATH_GENERIC);
 
   // ---- coalesce modes
+  const bool batched = b_batch >= 0 && as[0] > 1;
   Mode mm[3] = {{as[0], ast[0], cst[0]}, {as[1], ast[1], cst[1]}, {as[2], ast[2], cst[2]}};
-  int nm = coalesce(mm, 3);
+  // a batch mode stays a mode of its own (B follows it), only (b, i) may merge
+  int nm = batched ? 1 + coalesce(mm + 1, 2) : coalesce(mm, 3);
   Mode km[2] = {{as[3], ast[3], bst[0]}, {as[4], ast[4], bst[1]}};
   int nk = coalesce(km, 2);
   // pad to fixed arity: M -> (a, b, i), K -> (j, k); padded modes have size 1
@@ -518,9 +524,17 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   for (int t = 0; t < 3; ++t) M3[t] = {1, 0, 0};
   for (int t = 0; t < 2; ++t) K2[t] = {1, 0, 0};
   if (nm > 3 || nk > 2) return launch_generic(B2G_PATH_GENERIC);
-  for (int t = 0; t < nm; ++t) M3[3 - nm + t] = mm[t];
+  if (batched) {
+    // the batch mode keeps the a slot (the kernel indexes B with the tile's a coordinate);
+    // the compacted (b, i) modes are right-aligned after it
+    M3[0] = mm[0];
+    for (int t = 1; t < nm; ++t) M3[3 - (nm - 1) + (t - 1)] = mm[t];
+    if (nm == 1) M3[2] = {1, 1, 1};
+  } else {
+    for (int t = 0; t < nm; ++t) M3[3 - nm + t] = mm[t];
+    if (nm == 0) M3[2] = {1, 1, 1};
+  }
   for (int t = 0; t < nk; ++t) K2[2 - nk + t] = km[t];
-  if (nm == 0) M3[2] = {1, 1, 1};
   if (nk == 0) K2[1] = {1, 1, 1};
   const int64_t b_sn = bst[2], c_sn = cst[3];
 
@@ -542,7 +556,13 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
       jsz > INT32_MAX / 2 || ksz > INT32_MAX / 2)
     return launch_generic(B2G_PATH_GENERIC);
   int bi, bb, ba;
-  if (isz >= 128 || (128 % isz) != 0 || bsz * asz == 1) {
+  if (batched) {
+    // a tile never spans two batch entries: the 128-row box covers (i, b) only, rows past
+    // b's extent are zero-filled on load and clipped on store
+    bi = (isz >= 128 || (128 % isz) != 0) ? 128 : (int)isz;
+    bb = 128 / bi;
+    ba = 1;
+  } else if (isz >= 128 || (128 % isz) != 0 || bsz * asz == 1) {
     bi = 128; bb = 1; ba = 1;
   } else {
     bi = (int)isz;
@@ -572,6 +592,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   if (b_mn) tma_ok = tma_ok && stride_ok(K2[1], false, esz);
   if (b_k) tma_ok = tma_ok && (N == 1 || al16(b_sn * esz));
   if (c_m) tma_ok = tma_ok && (N == 1 || al16(c_sn * c_esz));
+  if (batched) tma_ok = tma_ok && al16(b_batch * esz);
   if (!tma_ok) return launch_generic(B2G_PATH_GENERIC);
 
   if (!get_encode()) return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
@@ -601,28 +622,34 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   const int num_m_tiles_b = (int)((bsz + bb - 1) / bb);
   const int num_m_tiles_a = (int)((asz + ba - 1) / ba);
   const int64_t nmt64 = (int64_t)num_m_tiles_i * num_m_tiles_b * num_m_tiles_a;
+  // batched: one-CTA tiles (the two CTAs of a pair could hold rows of different batch
+  // entries, while their MMA shares both halves of B)
   const TileChoice tc = choose_tiles(nmt64, N, ((ksz + kb_elems - 1) / kb_elems) * jsz, ds->sm_count,
-                                     (int)opt_cta_group.load(), (int)opt_tile_n.load());
+                                     batched ? 1 : (int)opt_cta_group.load(), (int)opt_tile_n.load());
   const int cg = tc.cg, bn = tc.bn;
   const int64_t nnt64 = (N + bn - 1) / bn;
   if (nmt64 * nnt64 > INT32_MAX / 4) return launch_generic(B2G_PATH_GENERIC);
   const int bph = std::min(bn, 256) / cg;  // B columns of one N-half held by one CTA
   // B
-  if (b_mn) {  // dims (n, k, j)
-    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)ksz, (cuuint64_t)jsz};
-    cuuint64_t st[2];
+  // B: a batch mode adds a 4th dimension (the batch, stride b_batch) after the others
+  const cuuint32_t b_rank = batched ? 4 : 3;
+  if (b_mn) {  // dims (n, k, j[, l])
+    cuuint64_t dims[4] = {(cuuint64_t)N, (cuuint64_t)ksz, (cuuint64_t)jsz, (cuuint64_t)asz};
+    cuuint64_t st[3];
     st[0] = fill(K2[1].sc * esz, ksz, N * esz);
     st[1] = fill(K2[0].sc * esz, jsz, (int64_t)st[0] * ksz);
-    cuuint32_t box[3] = {(cuuint32_t)kb_elems, (cuuint32_t)kb_elems, 1};  // one MN-major atom
-    CUresult r = encode_cached(&tmB, map_type, 3, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    st[2] = (cuuint64_t)(batched ? b_batch * esz : 16);
+    cuuint32_t box[4] = {(cuuint32_t)kb_elems, (cuuint32_t)kb_elems, 1, 1};  // one MN-major atom
+    CUresult r = encode_cached(&tmB, map_type, b_rank, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map B (N-major) not encodable
-  } else {  // dims (k, j, n)
-    cuuint64_t dims[3] = {(cuuint64_t)ksz, (cuuint64_t)jsz, (cuuint64_t)N};
-    cuuint64_t st[2];
+  } else {  // dims (k, j, n[, l])
+    cuuint64_t dims[4] = {(cuuint64_t)ksz, (cuuint64_t)jsz, (cuuint64_t)N, (cuuint64_t)asz};
+    cuuint64_t st[3];
     st[0] = fill(K2[0].sc * esz, jsz, ksz * esz);
     st[1] = fill(b_sn * esz, N, (int64_t)st[0] * jsz);
-    cuuint32_t box[3] = {(cuuint32_t)kb_elems, 1, (cuuint32_t)bph};
-    CUresult r = encode_cached(&tmB, map_type, 3, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+    st[2] = (cuuint64_t)(batched ? b_batch * esz : 16);
+    cuuint32_t box[4] = {(cuuint32_t)kb_elems, 1, (cuuint32_t)bph, 1};
+    CUresult r = encode_cached(&tmB, map_type, b_rank, const_cast<void*>(B), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map B (K-major) not encodable
   }
   // C
@@ -674,6 +701,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.store_hint = (int)opt_store_hint.load();
   p.c_type = c_type;
   p.bias = bias;
+  p.b_batched = batched ? 1 : 0;
   p.alpha = alpha;
   p.accumulate = beta != 0.0f ? 1 : 0;
   if (beta != 0.0f && beta != 1.0f) {  // C = beta*C first; the kernel then adds alpha*A.B
@@ -1062,6 +1090,37 @@ extern "C" int b2g_contract5d_epilogue(const void* A, const int64_t a_shape[5],
     return fail(B2G_ERR_INVALID_ARG, "null shape/stride array");
   return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, dtype, alpha, beta,
              static_cast<cudaStream_t>(stream), nullptr, bias, c_type);
+}
+
+extern "C" int b2g_contract5d_batched(const void* A, const int64_t a_shape[5],
+                                      const int64_t a_stride[5], const void* B,
+                                      const int64_t b_shape[3], const int64_t b_stride[3],
+                                      int64_t b_batch_stride, float* C, const int64_t c_shape[4],
+                                      const int64_t c_stride[4], int dtype, float alpha,
+                                      float beta, void* stream) {
+  t_err.clear();
+  if (!a_shape || !a_stride || !b_shape || !b_stride || !c_shape || !c_stride)
+    return fail(B2G_ERR_INVALID_ARG, "null shape/stride array");
+  if (b_batch_stride < 0) return fail(B2G_ERR_INVALID_ARG, "negative batch stride");
+  return run(A, a_shape, a_stride, B, b_shape, b_stride, C, c_shape, c_stride, dtype, alpha, beta,
+             static_cast<cudaStream_t>(stream), nullptr, nullptr, 0, b_batch_stride);
+}
+
+extern "C" int b2g_gemm_batched(const void* A, const void* B, float* C, int64_t L, int64_t M,
+                                int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                                int64_t stride_a, int64_t stride_b, int64_t stride_c,
+                                void* stream) {
+  t_err.clear();
+  if (L < 0 || M < 0 || N < 0 || K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
+  if (lda < std::max<int64_t>(K, 1) || ldb < std::max<int64_t>(N, 1) || ldc < std::max<int64_t>(N, 1))
+    return fail(B2G_ERR_INVALID_ARG, "leading dimension smaller than the row length");
+  if (stride_a < 0 || stride_b < 0 || stride_c < 0)
+    return fail(B2G_ERR_INVALID_ARG, "negative batch stride");
+  const int64_t as[5] = {L, 1, M, 1, K}, ast[5] = {stride_a, 0, lda, 0, 1};
+  const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
+  const int64_t cs[4] = {L, 1, M, N}, cst[4] = {stride_c, 0, ldc, 1};
+  return run(A, as, ast, B, bs, bst, C, cs, cst, B2G_DTYPE_F16, 1.0f, 0.0f,
+             static_cast<cudaStream_t>(stream), nullptr, nullptr, 0, stride_b);
 }
 
 extern "C" const char* b2g_last_error_string(void) { return t_err.c_str(); }

@@ -67,6 +67,8 @@ struct GemmParams {
   int c_type;                  // C element type: 0 = fp32, 1 = fp16, 2 = bf16 (16-bit: row-major
                                // C, no accumulate)
   const float* bias;           // per-column fp32 bias added to alpha*A.B, or null
+  int b_batched;               // 1 = mode a is a batch mode: B has a 4th tensor-map dimension
+                               // indexed by the tile's a (a tile then spans a single a)
   // Work units: the first num_full tiles (in tile order) are one unit each over all of K; each
   // remaining tile is split into k_splits units, split s covering the K blocks
   // [s*k_per_split, min(k_iters, (s+1)*k_per_split)).  num_full = 0 is plain split-K (too few
@@ -257,17 +259,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_groups = gridDim.x / CG;
 
   // B columns of N-half h held by this CTA start at n0 + h*UN + cta_rank*BPH.
-  auto issue_b = [&](uint32_t sb, uint32_t fb, int n0, int kc, int jj) {
+  auto issue_b = [&](uint32_t sb, uint32_t fb, int n0, int kc, int jj, int lb) {
 #pragma unroll
     for (int h = 0; h < C::NH; ++h) {
       const int nh = n0 + h * C::UN + (int)cta_rank * C::BPH;
       const uint32_t dst = sb + (uint32_t)h * C::HALF_BYTES;
       if constexpr (B_KMAJOR) {
-        ptx::tma_load_3d<CG>(dst, &tmB, fb, kc, jj, nh);
+        if (p.b_batched)
+          ptx::tma_load_4d<CG>(dst, &tmB, fb, kc, jj, nh, lb);
+        else
+          ptx::tma_load_3d<CG>(dst, &tmB, fb, kc, jj, nh);
       } else {
 #pragma unroll
         for (int c = 0; c < C::BPH / ATOM; ++c)
-          ptx::tma_load_3d<CG>(dst + (uint32_t)c * ATOM_BYTES, &tmB, fb, nh + ATOM * c, kc, jj);
+          if (p.b_batched)
+            ptx::tma_load_4d<CG>(dst + (uint32_t)c * ATOM_BYTES, &tmB, fb, nh + ATOM * c, kc, jj, lb);
+          else
+            ptx::tma_load_3d<CG>(dst + (uint32_t)c * ATOM_BYTES, &tmB, fb, nh + ATOM * c, kc, jj);
       }
     }
   };
@@ -299,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int jj = kb / p.k_blocks_per_j;
           const int kc = (kb - jj * p.k_blocks_per_j) * KB;
           ptx::tma_load_5d<CG>(base + s * C::A_BYTES, &tmA, fb, kc, jj, i0, b0, a0);
-          issue_b(base + C::OFF_B + s * C::B_BYTES, fb, n0, kc, jj);
+          issue_b(base + C::OFF_B + s * C::B_BYTES, fb, n0, kc, jj, a0);
         }
       }
       // Teardown: every load this thread issued must land before the CTA can exit.  With
