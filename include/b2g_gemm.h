@@ -257,7 +257,8 @@ int b2g_contract5d_epilogue(const void* A, const int64_t a_shape[5], const int64
  *   C[a,b,i,n] = alpha * sum_{j,k} A[a,b,i,j,k] B[a,j,k,n] + beta * C[a,b,i,n],
  * B's element (a, j, k, n) at a*b_batch_stride + j*b_stride[0] + k*b_stride[1] +
  * n*b_stride[2].  b2g_gemm_batched is the strided-batched GEMM C[l] = A[l].B[l] (fp16 in,
- * fp32 out) over l < L with batch strides in elements.  Batched calls use one-CTA tiles.  No
+ * fp32 out) over l < L with batch strides in elements.  Batched calls use CTA-pair tiles only
+ * when every batch entry has an even number of 128-row M tiles.  No
  * reference counterpart (generalises mmmTensor.cpp's fixed (a,b,i | j,k | n) roles).
  */
 int b2g_contract5d_batched(const void* A, const int64_t a_shape[5], const int64_t a_stride[5],

@@ -622,10 +622,12 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   const int num_m_tiles_b = (int)((bsz + bb - 1) / bb);
   const int num_m_tiles_a = (int)((asz + ba - 1) / ba);
   const int64_t nmt64 = (int64_t)num_m_tiles_i * num_m_tiles_b * num_m_tiles_a;
-  // batched: one-CTA tiles (the two CTAs of a pair could hold rows of different batch
-  // entries, while their MMA shares both halves of B)
+  // batched: a CTA pair holds M tiles 2p and 2p+1, whose rows must be of one batch entry (the
+  // pair's MMA shares both halves of B); with an odd number of M tiles per batch entry, tiles
+  // are one-CTA
+  const bool pair_ok = !batched || ((int64_t)num_m_tiles_i * num_m_tiles_b) % 2 == 0;
   const TileChoice tc = choose_tiles(nmt64, N, ((ksz + kb_elems - 1) / kb_elems) * jsz, ds->sm_count,
-                                     batched ? 1 : (int)opt_cta_group.load(), (int)opt_tile_n.load());
+                                     pair_ok ? (int)opt_cta_group.load() : 1, (int)opt_tile_n.load());
   const int cg = tc.cg, bn = tc.bn;
   const int64_t nnt64 = (N + bn - 1) / bn;
   if (nmt64 * nnt64 > INT32_MAX / 4) return launch_generic(B2G_PATH_GENERIC);

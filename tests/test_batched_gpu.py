@@ -29,7 +29,7 @@ def test_gemm_batched(b2g, cuda, orc, opts):
                          lda=lda, ldb=ldb, ldc=ldc)
     torch.cuda.synchronize()
     assert b2g.device_status() == 0
-    assert b2g.last_path() == b2g.PATH_TC_1CTA
+    assert b2g.last_path() in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)  # 2 M tiles per batch: pairs allowed
     C = dC.cpu().numpy()
     for l in range(L):
         Al = A[l * sa: l * sa + M * lda].reshape(M, lda)[:, :K]
@@ -67,9 +67,32 @@ def test_contraction_batched(b2g, cuda, orc, shape):
                            st((a, b, i, n)))
     torch.cuda.synchronize()
     assert b2g.device_status() == 0
-    assert b2g.last_path() == b2g.PATH_TC_1CTA
+    assert b2g.last_path() in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)  # 2 M tiles per batch: pairs allowed
     C = dC.cpu().numpy().reshape(a, b * i, n)
     A4 = A.reshape(a, b * i, j * k)
     B4 = B.reshape(a, j * k, n)
     for l in range(a):
         assert_close(orc, C[l], orc.gemm_f64(A4[l], B4[l]), j * k, what="batch %d %r" % (l, shape))
+
+
+@pytest.mark.parametrize("M", [2048, 2176])
+def test_gemm_batched_large(b2g, cuda, orc, M):
+    """Large batch entries: CTA-pair tiles when the M tiles per batch entry are even (2048 rows
+    = 16 tiles), one-CTA tiles when odd (2176 rows = 17 tiles); rows sampled per batch."""
+    torch = cuda
+    L, N, K = 3, 2048, 1024
+    dA = torch.empty((L, M, K), dtype=torch.float16, device="cuda")
+    dB = torch.empty((L, K, N), dtype=torch.float16, device="cuda")
+    b2g.fill_uniform(dA, L * M * K, 21)
+    b2g.fill_uniform(dB, L * K * N, 22)
+    dC = torch.empty((L, M, N), dtype=torch.float32, device="cuda")
+    b2g.gemm_batched(dA, dB, dC, L, M, N, K, M * K, K * N, M * N)
+    torch.cuda.synchronize()
+    assert b2g.device_status() == 0
+    assert b2g.last_path() == (b2g.PATH_TC_2CTA if M % 256 == 0 else b2g.PATH_TC_1CTA)
+    for l in range(L):
+        B = orc.uniform_f16((K * N,), 22, l * K * N).reshape(K, N)
+        for r in (0, 127, 128, M // 2, M - 1):
+            a = orc.uniform_f16((1, K), 21, (l * M + r) * K)
+            assert_close(orc, dC[l, r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K,
+                         what="batch %d row %d" % (l, r))
