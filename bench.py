@@ -252,6 +252,10 @@ def main():
                          "kernel loop only; used for the other BASELINE shapes and for profiling)")
     ap.add_argument("--dtype", default="f16", choices=["f16", "bf16", "e4m3", "e5m2"],
                     help="operand type (f16 = BASELINE's; the others are secondary lines)")
+    ap.add_argument("--out", default="f32", choices=["f32", "f16", "bf16"],
+                    help="type C is stored in (the fused epilogue; f32 = BASELINE's). Kernel loop only")
+    ap.add_argument("--bias", action="store_true",
+                    help="add a per-column fp32 bias in the epilogue. Kernel loop only")
     ap.add_argument("--kernel-only", action="store_true",
                     help="device-resident GEMM steps only (no e2e, CPU baseline or clock "
                          "sampling): the command profiled with ncu")
@@ -293,11 +297,15 @@ def main():
     stream = torch.cuda.current_stream()
     dt = {"f16": 0, "bf16": 1, "e4m3": 2, "e5m2": 3}[args.dtype]
     tdt = {0: torch.float16, 1: torch.bfloat16, 2: torch.uint8, 3: torch.uint8}[dt]
-    if dt:
-        args.kernel_only = True  # secondary operand types: device-resident kernel loop only
+    epilogue = args.out != "f32" or args.bias
+    if dt or epilogue:
+        args.kernel_only = True  # secondary types and epilogues: device-resident kernel loop only
     dA = torch.empty((M, K), dtype=tdt, device=dev)
     dB = torch.empty((K, N), dtype=tdt, device=dev)
-    dC = torch.empty((M, N), dtype=torch.float32, device=dev)
+    c_dt = {"f32": 4, "f16": 0, "bf16": 1}[args.out]
+    dC = torch.empty((M, N), device=dev,
+                     dtype={"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.out])
+    dBias = torch.randn(N, device=dev) if args.bias else None
     # rank r's slab of the (M*ws) x K matrix A; B generated on rank 0 and broadcast once
     b2g.fill_uniform(dA, M * K, 1, rank * M * K, stream, dtype=dt)
     if rank == 0:
@@ -310,6 +318,9 @@ def main():
         if contraction:
             b2g.contract5d(dA, a_shape, rowmajor(a_shape), dB, b_shape, rowmajor(b_shape), dC,
                            c_shape, rowmajor(c_shape), stream)
+        elif epilogue:
+            b2g.gemm_epilogue(dA, dB, dC, M, N, K, dtype=dt, bias=dBias, c_dtype=c_dt,
+                              stream=stream)
         elif dt:
             b2g.gemm_typed(dA, dB, dC, M, N, K, dt, stream=stream)
         else:
@@ -372,7 +383,7 @@ def main():
     cublas = None
     if not args.kernel_only:
         e2e = e2e_run(torch, b2g, dev, M, N, K, rank, ws, args.e2e_steps, dist if ws > 1 else None)
-    if rank == 0 and ws == 1 and not args.no_cublas and dt == 0 and (args.shape or not args.kernel_only):
+    if rank == 0 and ws == 1 and not args.no_cublas and dt == 0 and not epilogue and (args.shape or not args.kernel_only):
         cublas = cublas_side_by_side(torch, dA, dB, dC, local, min(args.steps, 1000))
 
     peaks, peaks_src = measured_peaks()
@@ -387,20 +398,22 @@ def main():
     # Roofline of the kernel: tensor-bound unless the shape's arithmetic intensity is below the
     # ridge of the measured peaks (then HBM-bound, achieved = algorithmic bytes / launch time).
     esz = 2 if dt < 2 else 1
-    alg_bytes = float(esz * M * K + esz * K * N + 4 * M * N)
+    c_esz = 4 if args.out == "f32" else 2
+    alg_bytes = float(esz * M * K + esz * K * N + c_esz * M * N + (4 * N if args.bias else 0))
     hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
     ridge = peak * 1e12 / (hbm * 1e9)
     if flops / alg_bytes < ridge:
         roofline = {"bound": "hbm", "achieved": alg_bytes / (avg_launch_ms * 1e-3) / 1e9,
                     "peak": hbm, "unit": "GB/s",
                     "frac": alg_bytes / (avg_launch_ms * 1e-3) / 1e9 / hbm,
-                    "traffic": profiled_traffic(M, N, K, args.dtype),
+                    "traffic": None if epilogue else profiled_traffic(M, N, K, args.dtype),
                     "peak_source": "%s hbm_gbs" % peaks_src,
                     "bytes_per_launch": alg_bytes, "flops_per_launch": flops,
                     "avg_launch_ms": avg_launch_ms, "tensor_tflops": achieved}
     else:
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak, "traffic": profiled_traffic(M, N, K, args.dtype),
+                    "frac": achieved / peak,
+                    "traffic": None if epilogue else profiled_traffic(M, N, K, args.dtype),
                     "peak_source": "%s %s%s" % (peaks_src, "bf16_tflops_sustained" if sustained
                                                 else "bf16_tflops", peak_note),
                     "flops_per_launch": flops, "bytes_per_launch": alg_bytes,
@@ -425,6 +438,10 @@ def main():
         metric = "gemm_tflops_%dx%dx%d_fp16_fp32" % (M, N, K)
     if dt:
         metric = metric.replace("fp16", args.dtype)
+    if args.out != "f32":
+        metric = metric.replace("_fp32", "_" + args.out + "out")
+    if args.bias:
+        metric += "_bias"
     line = {
         "metric": metric,
         "value": value,
@@ -436,7 +453,8 @@ def main():
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "%s in, f32 accumulate/out" % args.dtype,
+        "dtype": "%s in, f32 accumulate, %s out%s" % (args.dtype, args.out,
+                                                       " + f32 column bias" if args.bias else ""),
         "data": "synthetic: seeded U[-1,1] %s generated on the device (b2g_fill_uniform)" % args.dtype,
         "config": {
             "workload": ("contraction C[a,b,i,n] = sum_{j,k} A[a,b,i,j,k] B[j,k,n], a8 b16 i64 j64 "
@@ -447,8 +465,7 @@ def main():
                              " N>1: M-row slabs of a (8192N)x8192x8192 GEMM, B broadcast once",
             "M": M, "N": N, "K": K, "world_size": ws, "path": path,
             "l2": "inputs+output %.0f MiB per GPU (%s 126 MB L2)" % (
-                (2 * M * K + 2 * K * N + 4 * M * N) / 2**20,
-                "> : no flush needed" if 2 * M * K + 2 * K * N + 4 * M * N > 126e6 else
+                alg_bytes / 2**20, "> : no flush needed" if alg_bytes > 126e6 else
                 "< : steps may hit L2"),
             "frac_of_spec_2250": value / ws / SPEC_TFLOPS,
         },
