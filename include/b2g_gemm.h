@@ -217,6 +217,22 @@ int b2g_gemm_sharded_k(const void* A_kslab, const void* B_kslab, float* C_slab, 
                        void* stream);
 
 /*
+ * The same K-split GEMM with the reduce-scatter fused into the GEMMs over peer memory (no
+ * NCCL kernel).  b2g_rs_plan_create (collective, once per M x N) allocates every rank's
+ * receive slots (world x M/world x N fp32) and maps every peer's through CUDA IPC.  In
+ * b2g_gemm_sharded_k_p2p, rank r's GEMM of row slab q stores its tiles straight into rank q's
+ * slot r over NVLink, and rank r sums its slots in rank order into C_slab.  Epoch flags
+ * written and waited for by stream memory operations order the ranks.  Every rank of the
+ * plan calls it with the same M, N, K, in the same order.  b2g_rs_plan_destroy is collective.
+ * The ranks are processes on one node with CUDA IPC between their GPUs.
+ */
+int b2g_rs_plan_create(void* comm, int64_t M, int64_t N, void** plan);
+int b2g_rs_plan_destroy(void* plan);
+int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const void* B_kslab, float* C_slab,
+                           int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                           void* stream);
+
+/*
  * N-slabs with all-gather: rank r holds the column slab b2g_slab_rows(N, world, r) of B
  * (K x n_r, ldb) and of C (M x n_r, ldc); A (M x K, lda, every rank) is broadcast from `root`
  * in `m_panels` row panels, each followed by the GEMM of its rows.  With C_full != NULL

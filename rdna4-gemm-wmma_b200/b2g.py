@@ -95,6 +95,12 @@ def load(path=None):
     L.b2g_gemm_sharded_n.restype = ctypes.c_int
     L.b2g_gemm_sharded_n.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp, ctypes.c_int,
                                      ctypes.c_int, vp, vp]
+    L.b2g_rs_plan_create.restype = ctypes.c_int
+    L.b2g_rs_plan_create.argtypes = [vp, i64, i64, ctypes.POINTER(ctypes.c_void_p)]
+    L.b2g_rs_plan_destroy.restype = ctypes.c_int
+    L.b2g_rs_plan_destroy.argtypes = [vp]
+    L.b2g_gemm_sharded_k_p2p.restype = ctypes.c_int
+    L.b2g_gemm_sharded_k_p2p.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
     L.b2g_chain_plan_create.restype = ctypes.c_int
     L.b2g_chain_plan_create.argtypes = [vp, vp, i64, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
     L.b2g_chain_plan_destroy.restype = ctypes.c_int
@@ -308,6 +314,25 @@ def gemm_sharded_n(A, B_nslab, C_nslab, M, N, K, comm, root=0, m_panels=4, C_ful
                                      _ld(A, lda, "lda"), _ld(B_nslab, ldb, "ldb"),
                                      _ld(C_nslab, ldc, "ldc"), comm, root, m_panels,
                                      _ptr(C_full), _stream(stream)))
+
+
+def rs_plan_create(comm, M, N):
+    """Collective: receive slots for the peer-memory reduce-scatter of an M x N product."""
+    plan = ctypes.c_void_p()
+    _check(load().b2g_rs_plan_create(comm, M, N, ctypes.byref(plan)))
+    return plan.value
+
+
+def rs_plan_destroy(plan):
+    _check(load().b2g_rs_plan_destroy(plan))
+
+
+def gemm_sharded_k_p2p(plan, A_kslab, B_kslab, C_slab, M, N, K, lda=None, ldb=None, ldc=None,
+                       stream=None):
+    """gemm_sharded_k with the reduce-scatter fused into the GEMMs over peer memory."""
+    _check(load().b2g_gemm_sharded_k_p2p(plan, _ptr(A_kslab), _ptr(B_kslab), _ptr(C_slab), M, N, K,
+                                         _ld(A_kslab, lda, "lda"), _ld(B_kslab, ldb, "ldb"),
+                                         _ld(C_slab, ldc, "ldc"), _stream(stream)))
 
 
 def chain_plan_create(comm, B, nbytes, root=0):

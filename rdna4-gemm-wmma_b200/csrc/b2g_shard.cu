@@ -745,3 +745,291 @@ extern "C" int b2g_gemm_sharded_n_chain(void* plan, const void* B_nslab, float* 
                                              m1 - m0, nr, K, lda, ldb, ldc, 1.0f, 0.0f, s);
                         });
 }
+
+// ------------------------------------------------------------------ peer-memory reduce-scatter
+// K-split tensor parallelism with the reduce-scatter fused into the GEMMs.  Rank r computes its
+// partial product A_r.B_r one row slab at a time, and the GEMM of slab q stores its tiles (the
+// epilogue's TMA stores) straight into rank q's receive slot r, mapped here through CUDA IPC:
+// the partials cross NVLink tile by tile while the next tiles are computed.  The other ranks'
+// slabs go first, this rank's own slab last.  Epoch flags written and waited for by stream
+// memory operations order the calls, so no kernel waits on another GPU:
+//   - rank r writes into rank q's slots only after q has reduced the previous call's;
+//   - after its GEMMs, rank r tells every peer that its partial has landed (the flag write
+//     follows the GEMMs in stream order, behind a memory fence);
+//   - rank r reduces its slots once every peer has said so, summing them in rank order
+//     (deterministic), then tells every peer that its slots are free again.
+struct b2g_rs_plan {
+  ncclComm_t comm = nullptr;
+  int world = 1, rank = 0, dev = 0;
+  int64_t M = 0, N = 0, rows = 0;
+  float* recv = nullptr;         // [world][rows][N]: slot s holds rank s's partial of my rows
+  uint32_t* flags = nullptr;     // [world] partial of rank s landed, [world] rank q's slots free
+  std::vector<float*> peer_recv;       // rank q's receive slots, mapped here (q == rank: recv)
+  std::vector<uint32_t*> peer_flags;   // rank q's flag array, mapped here
+  std::vector<void*> opened;
+  uint32_t epoch = 0;
+};
+
+namespace {
+
+struct RsPeerInfo {
+  cudaIpcMemHandle_t recv_handle;
+  cudaIpcMemHandle_t flag_handle;
+  int64_t M, N;
+};
+
+void rs_plan_free(b2g_rs_plan* p) {
+  if (!p) return;
+  for (void* o : p->opened)
+    if (o) cudaIpcCloseMemHandle(o);
+  if (p->recv) cudaFree(p->recv);
+  if (p->flags) cudaFree(p->flags);
+  delete p;
+}
+
+// C[i][j] = sum over s in rank order of R[s][i][j]: rows x N, slots `rows * N` floats apart.
+__global__ void rs_reduce_kernel(const float* __restrict__ R, float* __restrict__ C, int64_t rows,
+                                 int64_t N, int64_t ldc, int world, int vec) {
+  const int64_t slot = rows * N;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  if (vec) {
+    const int64_t n4 = N / 4;
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < rows * n4; v += stride) {
+      const int64_t i = v / n4, j = (v - i * n4) * 4;
+      const float* src = R + i * N + j;
+      float4 a = __ldcs(reinterpret_cast<const float4*>(src));
+      for (int s = 1; s < world; ++s) {
+        const float4 x = __ldcs(reinterpret_cast<const float4*>(src + s * slot));
+        a.x += x.x;
+        a.y += x.y;
+        a.z += x.z;
+        a.w += x.w;
+      }
+      *reinterpret_cast<float4*>(C + i * ldc + j) = a;
+    }
+  } else {
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < slot; v += stride) {
+      const int64_t i = v / N, j = v - i * N;
+      float a = R[v];
+      for (int s = 1; s < world; ++s) a += R[v + s * slot];
+      C[i * ldc + j] = a;
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int b2g_rs_plan_create(void* comm, int64_t M, int64_t N, void** plan_out) {
+  b2g::set_error("");
+  if (!comm || !plan_out || M < 0 || N < 0) return sfail(B2G_ERR_INVALID_ARG, "bad plan arguments");
+  *plan_out = nullptr;
+  NcclApi* n = nccl();
+  if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
+  if (!drv()) return sfail(B2G_ERR_UNSUPPORTED, "stream memory operations unavailable");
+  auto* p = new b2g_rs_plan();
+  p->comm = static_cast<ncclComm_t>(comm);
+  ncclResult_t r = n->count(p->comm, &p->world);
+  if (r == ncclSuccess) r = n->user_rank(p->comm, &p->rank);
+  if (r != ncclSuccess) {
+    rs_plan_free(p);
+    return nccl_fail(r, "ncclCommCount/UserRank");
+  }
+  // every rank evaluates the same arguments, so an invalid M fails on all of them alike
+  if (M % p->world != 0) {
+    rs_plan_free(p);
+    return sfail(B2G_ERR_INVALID_ARG, "M must be a multiple of the rank count");
+  }
+  p->M = M;
+  p->N = N;
+  p->rows = M / p->world;
+  cudaGetDevice(&p->dev);
+  const size_t rbytes = std::max<size_t>(16, (size_t)p->world * p->rows * N * sizeof(float));
+  cudaError_t e = cudaMalloc(&p->recv, rbytes);
+  if (e == cudaSuccess) e = cudaMalloc(&p->flags, 2 * p->world * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(p->flags, 0, 2 * p->world * sizeof(uint32_t));
+  int rc = e == cudaSuccess ? B2G_OK : cuda_sfail(e, "reduce-scatter plan set-up");
+  p->peer_recv.assign(p->world, nullptr);
+  p->peer_flags.assign(p->world, nullptr);
+  if (rc == B2G_OK) {
+    p->peer_recv[p->rank] = p->recv;
+    p->peer_flags[p->rank] = p->flags;
+  }
+  if (p->world > 1) {
+    // Exchange the IPC handles of every rank's slots and flags.  Every rank takes part in both
+    // collectives below even after a local failure, so that none is left waiting.
+    RsPeerInfo mine = {};
+    if (rc == B2G_OK) {
+      e = cudaIpcGetMemHandle(&mine.recv_handle, p->recv);
+      if (e == cudaSuccess) e = cudaIpcGetMemHandle(&mine.flag_handle, p->flags);
+      if (e != cudaSuccess) rc = cuda_sfail(e, "cudaIpcGetMemHandle");
+    }
+    mine.M = M;
+    mine.N = N;
+    const size_t one = sizeof(RsPeerInfo);
+    void* dbuf = nullptr;
+    e = cudaMalloc(&dbuf, one * (p->world + 1));
+    if (e != cudaSuccess) {
+      rs_plan_free(p);
+      return cuda_sfail(e, "cudaMalloc(handle exchange)");
+    }
+    cudaStream_t xs = nullptr;
+    cudaStreamCreateWithFlags(&xs, cudaStreamNonBlocking);
+    cudaMemcpy(static_cast<char*>(dbuf) + one * p->world, &mine, one, cudaMemcpyHostToDevice);
+    r = n->all_gather(static_cast<char*>(dbuf) + one * p->world, dbuf, one, ncclUint8, p->comm, xs);
+    std::vector<RsPeerInfo> all(p->world);
+    if (r == ncclSuccess) {
+      e = cudaStreamSynchronize(xs);
+      if (e == cudaSuccess) e = cudaMemcpy(all.data(), dbuf, one * p->world, cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess && rc == B2G_OK) rc = cuda_sfail(e, "handle exchange");
+    } else if (rc == B2G_OK) {
+      rc = nccl_fail(r, "ncclAllGather(handles)");
+    }
+    cudaFree(dbuf);
+    if (rc == B2G_OK)
+      for (const RsPeerInfo& q : all)
+        if (q.M != M || q.N != N) rc = sfail(B2G_ERR_INVALID_ARG, "M or N differ across ranks");
+    for (int q = 0; q < p->world && rc == B2G_OK; ++q) {
+      if (q == p->rank) continue;
+      void* a = nullptr;
+      e = cudaIpcOpenMemHandle(&a, all[q].recv_handle, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        rc = cuda_sfail(e, "cudaIpcOpenMemHandle(peer slots)");
+        break;
+      }
+      p->opened.push_back(a);
+      p->peer_recv[q] = static_cast<float*>(a);
+      e = cudaIpcOpenMemHandle(&a, all[q].flag_handle, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        rc = cuda_sfail(e, "cudaIpcOpenMemHandle(peer flags)");
+        break;
+      }
+      p->opened.push_back(a);
+      p->peer_flags[q] = static_cast<uint32_t*>(a);
+    }
+    // every rank learns every rank's outcome: all keep the plan or all free it
+    int32_t* dst = nullptr;
+    e = cudaMalloc(&dst, sizeof(int32_t) * (p->world + 1));
+    if (e == cudaSuccess) {
+      const int32_t mine_rc = rc;
+      cudaMemcpy(dst + p->world, &mine_rc, sizeof(int32_t), cudaMemcpyHostToDevice);
+      r = n->all_gather(dst + p->world, dst, 1, ncclInt32, p->comm, xs);
+      std::vector<int32_t> rcs(p->world, 0);
+      if (r == ncclSuccess && cudaStreamSynchronize(xs) == cudaSuccess &&
+          cudaMemcpy(rcs.data(), dst, sizeof(int32_t) * p->world, cudaMemcpyDeviceToHost) ==
+              cudaSuccess) {
+        for (int q = 0; q < p->world; ++q)
+          if (rcs[q] != B2G_OK && rc == B2G_OK)
+            rc = sfail(rcs[q], "reduce-scatter plan set-up failed on rank " + std::to_string(q));
+      } else if (rc == B2G_OK) {
+        rc = sfail(B2G_ERR_NCCL, "reduce-scatter plan status exchange failed");
+      }
+      cudaFree(dst);
+    } else if (rc == B2G_OK) {
+      rc = cuda_sfail(e, "cudaMalloc(status exchange)");
+    }
+    cudaStreamDestroy(xs);
+  }
+  if (rc != B2G_OK) {
+    rs_plan_free(p);
+    return rc;
+  }
+  *plan_out = p;
+  return B2G_OK;
+}
+
+extern "C" int b2g_rs_plan_destroy(void* plan) {
+  auto* p = static_cast<b2g_rs_plan*>(plan);
+  if (!p) return B2G_OK;
+  // Collective: this rank's queued calls finish, it drops its mappings of the peers' memory,
+  // and only after every rank has done so does anyone free the memory the others had mapped.
+  cudaDeviceSynchronize();
+  for (void*& o : p->opened) {
+    if (o) cudaIpcCloseMemHandle(o);
+    o = nullptr;
+  }
+  int rc = B2G_OK;
+  if (p->world > 1) {
+    NcclApi* n = nccl();
+    int32_t* d = nullptr;
+    cudaStream_t xs = nullptr;
+    if (!n) {
+      rc = sfail(B2G_ERR_NCCL, "NCCL unavailable");
+    } else if (cudaMalloc(&d, sizeof(int32_t) * (p->world + 1)) != cudaSuccess ||
+               cudaStreamCreateWithFlags(&xs, cudaStreamNonBlocking) != cudaSuccess) {
+      rc = sfail(B2G_ERR_CUDA, "reduce-scatter plan barrier set-up");
+    } else {
+      ncclResult_t r = n->all_gather(d + p->world, d, 1, ncclInt32, p->comm, xs);
+      if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather(plan barrier)");
+      else if (cudaStreamSynchronize(xs) != cudaSuccess)
+        rc = sfail(B2G_ERR_CUDA, "reduce-scatter plan barrier");
+    }
+    if (d) cudaFree(d);
+    if (xs) cudaStreamDestroy(xs);
+  }
+  rs_plan_free(p);
+  return rc;
+}
+
+extern "C" int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const void* B_kslab,
+                                      float* C_slab, int64_t M, int64_t N, int64_t K, int64_t lda,
+                                      int64_t ldb, int64_t ldc, void* stream) {
+  b2g::set_error("");
+  auto* p = static_cast<b2g_rs_plan*>(plan);
+  if (!p) return sfail(B2G_ERR_INVALID_ARG, "null plan");
+  const DrvApi* d = drv();
+  if (!d) return sfail(B2G_ERR_UNSUPPORTED, "stream memory operations unavailable");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUstream cs = reinterpret_cast<CUstream>(s);
+  const uint32_t ep = ++p->epoch;
+  const int W = p->world, R = p->rank;
+  const int64_t rows = p->rows;
+  int64_t k0 = 0, kr = 0;
+  b2g_slab_rows(K, W, R, &k0, &kr);
+  // From here on every flag of the protocol is written and waited for even after a local
+  // error (which only skips this rank's GEMMs and reduction), so that no peer's stream is left
+  // waiting for this rank.
+  int rc = B2G_OK;
+  if (M != p->M || N != p->N || K < 0)
+    rc = sfail(B2G_ERR_INVALID_ARG, "M or N differ from the plan's, or K < 0");
+  else if (ldc < std::max<int64_t>(N, 1))
+    rc = sfail(B2G_ERR_INVALID_ARG, "ldc < N");
+  else if (kr > 0 && (lda < kr || ldb < std::max<int64_t>(N, 1)))
+    rc = sfail(B2G_ERR_INVALID_ARG, "lda < the K slab or ldb < N");
+  auto flag = [](uint32_t* base, int i) { return reinterpret_cast<CUdeviceptr>(base + i); };
+  auto cu = [&](CUresult r, const char* what) {
+    if (r != CUDA_SUCCESS && rc == B2G_OK)
+      rc = sfail(B2G_ERR_CUDA, std::string(what) + " failed (CUresult " + std::to_string((int)r) + ")");
+  };
+  // the partial of rows [q*rows, (q+1)*rows) goes to rank q's slot R; the other ranks first
+  for (int t = 1; t <= W; ++t) {
+    const int q = (R + t) % W;
+    if (q != R)  // rank q has reduced the previous call's slots
+      cu(d->wait32(cs, flag(p->flags, W + q), ep - 1, CU_STREAM_WAIT_VALUE_GEQ),
+         "cuStreamWaitValue32(slots free)");
+    if (rc != B2G_OK || rows == 0 || N == 0) continue;
+    rc = b2g_gemm_ex(static_cast<const char*>(A_kslab) + (size_t)(q * rows) * (kr > 0 ? lda : 1) * 2,
+                     B_kslab, p->peer_recv[q] + (size_t)R * rows * N, rows, N, kr,
+                     kr > 0 ? lda : 1, ldb, N, 1.0f, 0.0f, s);
+  }
+  // announce this rank's partials (the default write orders the GEMMs' stores before it), then
+  // wait for every peer's
+  for (int q = 0; q < W; ++q)
+    if (q != R) cu(d->write32(cs, flag(p->peer_flags[q], R), ep, 0), "cuStreamWriteValue32(landed)");
+  for (int q = 0; q < W; ++q)
+    if (q != R)
+      cu(d->wait32(cs, flag(p->flags, q), ep, CU_STREAM_WAIT_VALUE_GEQ), "cuStreamWaitValue32(landed)");
+  if (rc == B2G_OK && rows > 0 && N > 0) {
+    const int vec = (N % 4 == 0 && ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(C_slab) & 15) == 0);
+    const int64_t work = vec ? rows * (N / 4) : rows * N;
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->dev);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)sms * 8));
+    rs_reduce_kernel<<<grid, 256, 0, s>>>(p->recv, C_slab, rows, N, ldc, W, vec);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = cuda_sfail(e, "rs_reduce_kernel");
+  }
+  // this rank's slots may be overwritten by the next call
+  for (int q = 0; q < W; ++q)
+    if (q != R) cu(d->write32(cs, flag(p->peer_flags[q], W + R), ep, 0), "cuStreamWriteValue32(free)");
+  return rc;
+}

@@ -254,6 +254,49 @@ def nccl_tp_rank(mode, rank, world, uid_path, M, N, K, panels, out_q):
         out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))
 
 
+def nccl_p2p_rs_rank(rank, world, uid_path, M, N, K, calls, out_q):
+    """b2g_gemm_sharded_k_p2p on `world` GPUs: `calls` calls in a row with new operands each
+    (another seed), the last one into a padded C (ldc > N); every call checked on sampled rows
+    against the FP64 oracle, the padding left untouched."""
+    try:
+        import torch
+        from oracle import orc
+        b2g = _load_pkg("b2g")
+        torch.cuda.set_device(rank)
+        comm = _nccl_comm(b2g, rank, world, uid_path)
+        plan = b2g.rs_plan_create(comm, M, N)
+        k0, kr = b2g.slab_rows(K, world, rank)
+        rows = M // world
+        outs = []
+        for c in range(calls):
+            dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+            dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+            b2g.fill_uniform(dA, M * K, 1 + 10 * c)
+            b2g.fill_uniform(dB, K * N, 2 + 10 * c)
+            ldc = N + 8 if c == calls - 1 else N
+            dC = torch.full((rows, ldc), float("nan"), dtype=torch.float32, device="cuda")
+            b2g.gemm_sharded_k_p2p(plan, dA[:, k0:k0 + kr].contiguous(),
+                                   dB[k0:k0 + kr].contiguous(), dC, M, N, K, lda=max(kr, 1),
+                                   ldb=N, ldc=ldc)
+            outs.append(dC)
+        torch.cuda.synchronize()
+        bad = 0
+        pad_ok = True
+        for c, dC in enumerate(outs):
+            B = orc.uniform_f16((K, N), 2 + 10 * c)
+            for r in sorted(set([0, rows - 1, rows // 2, rows // 3])):
+                a = orc.uniform_f16((1, K), 1 + 10 * c, (rank * rows + r) * K)
+                bad += orc.check(dC[r:r + 1, :N].cpu().numpy(), orc.gemm_f64(a, B), K, 1.0, 1.0)[0]
+            if dC.shape[1] > N:
+                pad_ok = pad_ok and bool(torch.isnan(dC[:, N:]).all())
+        status = b2g.device_status()
+        b2g.rs_plan_destroy(plan)
+        b2g.comm_destroy(comm)
+        out_q.put((rank, bad, status, pad_ok, None))
+    except Exception:
+        out_q.put((rank, -1, -1, False, traceback.format_exc()))
+
+
 def nccl_chain_rank(rank, world, uid_path, M, N, K, panels, calls, out_q):
     """b2g_gemm_sharded_chain on `world` GPUs: `calls` calls in a row, the root writing a new B
     (another seed) before each; every call checked on sampled rows, and B bit-exact."""

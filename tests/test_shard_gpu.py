@@ -125,6 +125,39 @@ def test_tp_two_ranks(b2g, cuda, mode):
         assert bad == 0 and gbad == 0 and status == 0 and a_ok, (rank, bad, gbad, status, a_ok)
 
 
+def test_p2p_rs_single_rank(b2g, cuda):
+    with tempfile.TemporaryDirectory() as d:
+        q = _ListQueue()
+        shard_worker.nccl_p2p_rs_rank(0, 1, os.path.join(d, "id"), 512, 768, 1024, 3, q)
+    rank, bad, status, pad_ok, tb = q[0]
+    assert tb is None, tb
+    assert bad == 0 and status == 0 and pad_ok
+
+
+@pytest.mark.parametrize("world,M,N,K", [(2, 2048, 1536, 4096), (2, 512, 1001, 777),
+                                         (4, 4096, 2048, 4096), (8, 8192, 4096, 8192)])
+def test_p2p_rs_multi_rank(b2g, cuda, world, M, N, K):
+    """K-split GEMM with the reduce-scatter over peer memory: three calls in a row (slots
+    reused under the epoch flags); N = 1001 stores through the generic kernel (rows not
+    16-byte aligned) and reduces element by element."""
+    if cuda.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=shard_worker.nccl_p2p_rs_rank,
+                             args=(r, world, os.path.join(d, "id"), M, N, K, 3, q))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        res = sorted(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=120)
+    for rank, bad, status, pad_ok, tb in res:
+        assert tb is None, tb
+        assert bad == 0 and status == 0 and pad_ok, (rank, bad, status, pad_ok)
+
+
 def test_chain_single_rank(b2g, cuda):
     with tempfile.TemporaryDirectory() as d:
         q = _ListQueue()
