@@ -238,15 +238,20 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cublas", action="store_true")
     ap.add_argument("--workload", default="gemm8192",
-                    choices=["gemm8192", "sharded32768", "contraction5d"],
+                    choices=["gemm8192", "sharded32768", "contraction5d", "tp_k"],
                     help="gemm8192: BASELINE configs[1] per GPU (the default line); "
                          "contraction5d: BASELINE configs[2] through the contraction entry point "
                          "(C[a,b,i,n] = sum A[a,b,i,j,k] B[j,k,n], a8 b16 i64 j64 k128 n4096); "
                          "sharded32768: BASELINE configs[4], one 32768^3 GEMM as M-row slabs "
-                         "over the N GPUs, B broadcast in K panels inside every step")
+                         "over the N GPUs, B broadcast in K panels inside every step; "
+                         "tp_k: tensor-parallel K-split GEMM (8192^3 or --shape) whose partials "
+                         "are reduce-scattered over the N GPUs inside every step")
     ap.add_argument("--bcast", default="chain", choices=["chain", "nccl"],
                     help="sharded32768: how B reaches the ranks each step (copy-engine chain, "
                          "or ncclBroadcast)")
+    ap.add_argument("--tp", default="p2p", choices=["p2p", "nccl"],
+                    help="tp_k: reduce-scatter fused into the GEMMs over peer memory, or "
+                         "ncclReduceScatter after the GEMM")
     ap.add_argument("--shape", default=None,
                     help="M,N,K: time this row-major GEMM instead of 8192^3 (device-resident "
                          "kernel loop only; used for the other BASELINE shapes and for profiling)")
@@ -277,6 +282,8 @@ def main():
     b2g = load_b2g()
     if args.workload == "sharded32768":
         return run_sharded(args, torch, dist, b2g, ws, rank, local, dev)
+    if args.workload == "tp_k":
+        return run_tp_k(args, torch, dist, b2g, ws, rank, local, dev)
 
     M, N, K = M_PER_GPU, N_DIM, K_DIM
     contraction = args.workload == "contraction5d"
@@ -558,6 +565,110 @@ def run_sharded(args, torch, dist, b2g, ws, rank, local, dev):
                        "rows_per_rank": rows, "k_panels": panels,
                        "broadcast": ("copy-engine chain (peer copies + stream memory ops, no SM)"
                                      if plan is not None else "NCCL broadcast")},
+            "row0_out_of_tolerance": bad, "device_status": status,
+            "gpu_launches": launches}), flush=True)
+    return 0
+
+
+def library_comm(torch, dist, b2g, ws, rank, dev):
+    """The library's own NCCL communicator over the ws ranks (id broadcast from rank 0)."""
+    import numpy as np
+    uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+    if rank == 0:
+        uid.copy_(torch.from_numpy(np.frombuffer(b2g.comm_unique_id(), dtype=np.uint8).copy()))
+    if ws > 1:
+        dist.broadcast(uid, src=0)
+    return b2g.comm_init(ws, rank, bytes(uid.cpu().numpy().tobytes()))
+
+
+def run_tp_k(args, torch, dist, b2g, ws, rank, local, dev):
+    """Tensor-parallel K-split GEMM: rank r holds the K slab of A and B, and every step ends
+    with rows [r*M/ws, (r+1)*M/ws) of C = sum over ranks of A_r.B_r on rank r (the partials
+    reduce-scattered over peer memory inside the GEMMs, or by ncclReduceScatter).  Strong
+    scaling: the total work is fixed."""
+    M, N, K = (int(x) for x in args.shape.split(",")) if args.shape else (8192, 8192, 8192)
+    comm = library_comm(torch, dist, b2g, ws, rank, dev)
+    k0, kr = b2g.slab_rows(K, ws, rank)
+    rows = M // ws
+    stream = torch.cuda.current_stream()
+    # the full seeded A and B on every rank (for the spot check); each rank multiplies its slab
+    A = torch.empty((M, K), dtype=torch.float16, device=dev)
+    B = torch.empty((K, N), dtype=torch.float16, device=dev)
+    b2g.fill_uniform(A, M * K, 1, 0, stream)
+    b2g.fill_uniform(B, K * N, 2, 0, stream)
+    dA = A[:, k0:k0 + kr].contiguous()
+    dB = B[k0:k0 + kr].contiguous()
+    dC = torch.empty((rows, N), dtype=torch.float32, device=dev)
+    plan = b2g.rs_plan_create(comm, M, N) if args.tp == "p2p" else None
+
+    def step():
+        if plan is not None:
+            b2g.gemm_sharded_k_p2p(plan, dA, dB, dC, M, N, K, stream=stream)
+        else:
+            b2g.gemm_sharded_k(dA, dB, dC, M, N, K, comm, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    launches0 = b2g.get_option("launches")
+    t0.record(stream)
+    for _ in range(args.steps):
+        step()
+    t1.record(stream)
+    launches = b2g.get_option("launches") - launches0
+    torch.cuda.synchronize()
+    t = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # spot check: first row of every rank's part against the FP64 product of the full operands
+    bad = row_out_of_tolerance(torch, dC[:1], A[rank * rows:rank * rows + 1], B, K)
+    status = b2g.device_status()
+    if ws > 1:
+        chk = torch.tensor([bad, abs(status)], dtype=torch.int64, device=dev)
+        dist.all_reduce(chk, op=dist.ReduceOp.MAX)
+        bad, status = int(chk[0].item()), int(chk[1].item())
+        dist.barrier()
+    if plan is not None:
+        b2g.rs_plan_destroy(plan)
+    b2g.comm_destroy(comm)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        flops = 2.0 * M * N * K
+        value = flops * args.steps / (ms * 1e-3) / 1e12
+        peaks, src = measured_peaks()
+        # fused compute + collective: the target time per step is the slower of the per-rank
+        # GEMM at the measured sustained peak and the partials this rank sends over NVLink at
+        # the measured 770 GB/s peer bandwidth
+        link = 770.0
+        t_gemm = flops / ws / (peaks["bf16_tflops_sustained"] * 1e12)
+        nv_bytes = (ws - 1) / ws * M * N * 4.0
+        t_link = nv_bytes / (link * 1e9)
+        target = max(t_gemm, t_link)
+        print(json.dumps({
+            "metric": "tp_ksplit_gemm_tflops_%dx%dx%d_fp16_fp32" % (M, N, K), "value": value,
+            "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16 in, f32 accumulate/out",
+            "data": "synthetic: seeded U[-1,1] fp16 generated on the device",
+            "config": {"workload": "tensor-parallel K-split gemm %dx%dx%d, K slabs over N GPUs, "
+                                   "partials reduce-scattered every step" % (M, N, K),
+                       "reduce_scatter": ("fused into the GEMMs over peer memory "
+                                          "(b2g_gemm_sharded_k_p2p)" if plan is not None
+                                          else "ncclReduceScatter after the GEMM (b2g_gemm_sharded_k)"),
+                       "rows_per_rank": rows},
+            "roofline": {"bound": "tensor" if t_gemm >= t_link else "nvlink",
+                         "target_ms": target * 1e3, "frac": target * 1e3 / (ms / args.steps),
+                         "gemm_ms_at_peak": t_gemm * 1e3, "nvlink_ms": t_link * 1e3,
+                         "nvlink_bytes_per_rank": nv_bytes,
+                         "peak_source": "%s bf16_tflops_sustained; peer copy 770 GB/s" % src},
             "row0_out_of_tolerance": bad, "device_status": status,
             "gpu_launches": launches}), flush=True)
     return 0

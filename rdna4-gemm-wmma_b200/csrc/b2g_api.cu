@@ -62,6 +62,7 @@ static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream seri
 // Kernels this library has launched (every GEMM, scale and fill kernel), for callers that
 // count launches (b2g_get_option("launches")).
 static std::atomic<int64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 static std::atomic<int64_t> opt_cluster_fixup{1};  // split-K fix-up through distributed smem
 static std::atomic<int64_t> opt_serial_fixup{0};  // 1 = always the last-arriver fix-up
 

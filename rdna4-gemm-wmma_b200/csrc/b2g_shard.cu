@@ -1027,6 +1027,7 @@ extern "C" int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const voi
     rs_reduce_kernel<<<grid, 256, 0, s>>>(p->recv, C_slab, rows, N, ldc, W, vec);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) rc = cuda_sfail(e, "rs_reduce_kernel");
+    else b2g::count_launch();
   }
   // this rank's slots may be overwritten by the next call
   for (int q = 0; q < W; ++q)
