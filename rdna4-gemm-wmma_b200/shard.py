@@ -91,6 +91,46 @@ def sharded_gemm_k(A_kslab, B_kslab, C_slab, M, N, K, group=None, gemm=None):
     return rank * rows, rows
 
 
+def sharded_gemm_k_p2p(A_kslab, B_kslab, C_slab, M, N, K, group=None, gemm=None):
+    """The schedule of b2g_gemm_sharded_k_p2p.  This rank computes its partial one row slab at a
+    time, the other ranks' slabs first (q = rank+1, ..., rank-1) and its own last; slab q lands
+    in receive slot `rank` of rank q; every rank sums its slots in rank order (slot 0 first).
+    The C library stores each slab into the owner's slot over peer memory from the GEMM's
+    epilogue; here each slab travels as one point-to-point message.  Returns (row0, rows)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if M % world:
+        raise ValueError("M must be a multiple of the rank count")
+    k0, kr = slab_rows(K, world, rank)
+    rows = M // world
+    gemm = gemm or _b2g_gemm
+    peer = (lambda q: dist.get_global_rank(group, q)) if group is not None else (lambda q: q)
+    slots = torch.empty((world, rows, N), dtype=C_slab.dtype, device=C_slab.device)
+    lda = A_kslab.stride(0) if kr else 1
+    reqs, parts = [], []
+    for t in range(1, world + 1):
+        q = (rank + t) % world
+        part = slots[rank] if q == rank else torch.empty((rows, N), dtype=C_slab.dtype,
+                                                          device=C_slab.device)
+        gemm(A_kslab[q * rows:(q + 1) * rows], B_kslab, part, rows, N, kr, 0.0, lda,
+             B_kslab.stride(0), N)
+        if q != rank:
+            parts.append(part)
+            reqs.append(dist.isend(part, peer(q), group=group))
+    for q in range(world):
+        if q != rank:
+            reqs.append(dist.irecv(slots[q], peer(q), group=group))
+    for r in reqs:
+        r.wait()
+    acc = slots[0].clone()
+    for q in range(1, world):
+        acc += slots[q]
+    C_slab.copy_(acc)
+    return rank * rows, rows
+
+
 def sharded_gemm_n(A, B_nslab, C_nslab, M, N, K, group=None, root=0, panels=4, C_full=None,
                    gemm=None):
     """N slabs: A (M x K on every rank, filled from `root`) arrives in row panels (multiples of

@@ -150,9 +150,10 @@ def _cpu_gemm(A_view, B_view, C, r, n, k, beta, lda, ldb, ldc):
 
 
 def gloo_tp_rank(mode, rank, world, port, M, N, K, panels, out_q):
-    """shard.sharded_gemm_k ("k") or shard.sharded_gemm_n ("n") on CPU tensors with the FP64
-    stand-in; reports (rank, max error against the FP64 oracle of the rows/columns this rank
-    owns, max error of the gathered C or 0)."""
+    """shard.sharded_gemm_k ("k"), its peer-memory schedule shard.sharded_gemm_k_p2p ("kp") or
+    shard.sharded_gemm_n ("n") on CPU tensors with the FP64 stand-in; reports (rank, max error
+    against the FP64 oracle of the rows/columns this rank owns, max error of the gathered C or
+    0)."""
     try:
         import torch
         from oracle import orc
@@ -162,11 +163,12 @@ def gloo_tp_rank(mode, rank, world, port, M, N, K, panels, out_q):
         B = orc.uniform_f16((K, N), 2)
         ref = orc.gemm_f64(A, B)
         gerr = 0.0
-        if mode == "k":
+        if mode in ("k", "kp"):
             k0, kr = shard.slab_rows(K, world, rank)
             C_slab = torch.full((M // world, N), float("nan"), dtype=torch.float64)
-            row0, rows = shard.sharded_gemm_k(_f16(A[:, k0:k0 + kr]), _f16(B[k0:k0 + kr]), C_slab,
-                                              M, N, K, gemm=_cpu_gemm)
+            fn = shard.sharded_gemm_k if mode == "k" else shard.sharded_gemm_k_p2p
+            row0, rows = fn(_f16(A[:, k0:k0 + kr]), _f16(B[k0:k0 + kr]), C_slab, M, N, K,
+                            gemm=_cpu_gemm)
             err = float(np.abs(C_slab.numpy() - ref[row0:row0 + rows]).max()) if rows else 0.0
         else:
             n0, nr = shard.slab_rows(N, world, rank)

@@ -115,6 +115,12 @@ def test_gloo_k_split_reduce_scatter(world, M, N, K):
     _run_tp("k", world, M, N, K, 1)
 
 
+@pytest.mark.parametrize("world,M,N,K", [(2, 96, 40, 192), (2, 8, 24, 1), (3, 30, 17, 100)])
+def test_gloo_k_split_peer_schedule(world, M, N, K):
+    """The slab order, slot index and rank-order reduction of b2g_gemm_sharded_k_p2p."""
+    _run_tp("kp", world, M, N, K, 1)
+
+
 @pytest.mark.parametrize("world,M,N,K,panels", [(2, 200, 48, 64, 3), (2, 7, 5, 33, 2),
                                                 (3, 130, 30, 20, 4)])
 def test_gloo_n_slabs_all_gather(world, M, N, K, panels):
