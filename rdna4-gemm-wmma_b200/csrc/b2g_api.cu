@@ -945,9 +945,13 @@ extern "C" int b2g_gemm_f16_f32_noalloc(const void* A, const void* B, float* C, 
   if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
   if (lda < std::max<int64_t>(K, 1) || ldb < std::max<int64_t>(N, 1) || ldc < std::max<int64_t>(N, 1))
     return fail(B2G_ERR_INVALID_ARG, "leading dimension smaller than the row length");
-  FixedScratch fs;
-  int rc = noalloc_scratch(&fs);
-  if (rc != B2G_OK) return rc;
+  // an empty problem needs no device (as in b2g_gemm_f16_f32): the scratch is looked up only
+  // for a non-empty one
+  FixedScratch fs = {nullptr, 0};
+  if (M > 0 && N > 0) {
+    const int rc = noalloc_scratch(&fs);
+    if (rc != B2G_OK) return rc;
+  }
   const int64_t as[5] = {1, 1, M, 1, K}, ast[5] = {0, 0, lda, 0, 1};
   const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
   const int64_t cs[4] = {1, 1, M, N}, cst[4] = {0, 0, ldc, 1};

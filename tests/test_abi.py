@@ -62,6 +62,27 @@ def test_invalid_arguments_rejected_without_gpu(b2g):
     # empty problem: nothing to do, no device needed
     assert L.b2g_gemm_f16_f32(None, None, None, 0, 4, 4, 4, 4, 4, None) == b2g.OK
     assert b2g.last_path() == b2g.PATH_EMPTY
+    assert L.b2g_gemm_f16_f32_noalloc(None, None, None, 4, 0, 4, 4, 4, 4, None) == b2g.OK
+    assert b2g.last_path() == b2g.PATH_EMPTY
+    assert L.b2g_gemm_batched(None, None, None, 0, 4, 4, 4, 4, 4, 4, 16, 16, 16, None) == b2g.OK
+    # epilogue, operand-type and batch arguments
+    assert L.b2g_gemm_epilogue(None, None, None, 4, 4, 4, 4, 4, 4, 0, 1.0, 0.0, None, 7,
+                               None) == b2g.ERR_INVALID_ARG
+    assert b"output type" in L.b2g_last_error_string()
+    assert L.b2g_gemm_epilogue(None, None, None, 4, 4, 4, 4, 4, 4, 0, 1.0, 1.0, None,
+                               b2g.DTYPE_F16, None) == b2g.ERR_INVALID_ARG
+    assert b"beta = 0" in L.b2g_last_error_string()
+    assert L.b2g_gemm_typed(None, None, None, 4, 4, 4, 4, 4, 4, 9, 1.0, 0.0,
+                            None) == b2g.ERR_INVALID_ARG
+    assert L.b2g_gemm_batched(None, None, None, -1, 4, 4, 4, 4, 4, 4, 16, 16, 16,
+                              None) == b2g.ERR_INVALID_ARG
+    # multi-GPU plans: null plan / communicator rejected, destroying a null plan is a no-op
+    assert L.b2g_gemm_sharded_k_p2p(None, None, None, None, 4, 4, 4, 4, 4, 4,
+                                    None) == b2g.ERR_INVALID_ARG
+    plan = ctypes.c_void_p()
+    assert L.b2g_rs_plan_create(None, 4, 4, ctypes.byref(plan)) == b2g.ERR_INVALID_ARG
+    assert L.b2g_rs_plan_destroy(None) == b2g.OK
+    assert L.b2g_chain_plan_destroy(None) == b2g.OK
 
 
 @pytest.mark.parametrize("num_m,num_n,group", [
