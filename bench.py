@@ -186,8 +186,8 @@ def run_reference(args):
     t0 = time.perf_counter()
     orc.gemm_f32_blocked(A, B, rows=(0, 48), threads=thr, Bf=Bf)
     per_row = (time.perf_counter() - t0) / 48
-    budget = 60.0 / max(1, args.steps + args.warmup)
-    rows = int(max(6, min(M_PER_GPU, budget / per_row)) // 6 * 6)
+    step_s = 60.0 / max(1, args.steps + args.warmup)
+    rows = int(max(6, min(M_PER_GPU, step_s / per_row)) // 6 * 6)
     r0 = 0
     for _ in range(args.warmup):
         orc.gemm_f32_blocked(A, B, rows=(r0, r0 + rows), threads=thr, Bf=Bf)

@@ -137,10 +137,10 @@ struct Cfg {
   static constexpr int CHUNKS = BN / 32;  // 32-column epilogue chunks per tile
 };
 
-static_assert(Cfg<1, 256>::SMEM_BYTES <= kSmemLimit && Cfg<1, 256>::STAGES >= 4, "CG=1 budget");
-static_assert(Cfg<2, 256>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256>::STAGES >= 6, "CG=2 budget");
-static_assert(Cfg<2, 512>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512>::STAGES >= 4, "BN=512 budget");
-static_assert(Cfg<1, 128>::SMEM_BYTES <= kSmemLimit && Cfg<1, 128>::STAGES >= 6, "BN=128 budget");
+static_assert(Cfg<1, 256>::SMEM_BYTES <= kSmemLimit && Cfg<1, 256>::STAGES >= 4, "CG=1 shared-memory fit");
+static_assert(Cfg<2, 256>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256>::STAGES >= 6, "CG=2 shared-memory fit");
+static_assert(Cfg<2, 512>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512>::STAGES >= 4, "BN=512 shared-memory fit");
+static_assert(Cfg<1, 128>::SMEM_BYTES <= kSmemLimit && Cfg<1, 128>::STAGES >= 6, "BN=128 shared-memory fit");
 // the cluster fix-up keeps a CTA's 128 x BN fp32 partial in its (then idle) operand stages
 static_assert(Cfg<1, 128>::OFF_C >= 128u * 128u * 4u && Cfg<1, 256>::OFF_C >= 128u * 256u * 4u,
               "partial tile fits in the operand stages");
