@@ -1,0 +1,73 @@
+"""Whole-matrix parity at BASELINE's full sizes, through an order-independent property.
+
+With A and B drawn from {-1, 0, 1}, every product is -1, 0 or 1 and every partial sum an integer
+of magnitude at most K < 2^24.  fp32 accumulation of such terms is exact in any order, so the
+library's C must equal the FP64 product element for element on every path: CTA-pair tiles,
+split-K with either fix-up, the contraction's 5-D tensor maps.  This checks every element of C
+at the sizes BASELINE names, where the FP64 oracle could only afford sampled rows.  The FP64
+product is torch's on the GPU, used here as the checker only.
+"""
+import pytest
+
+from gpu_util import options
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ternary(torch, shape, seed):
+    g = torch.Generator(device=DEV)
+    g.manual_seed(seed)
+    return torch.randint(-1, 2, shape, generator=g, device=DEV).to(torch.float16)
+
+
+def _exact_gemm(b2g, torch, M, N, K, seed):
+    A = _ternary(torch, (M, K), seed)
+    B = _ternary(torch, (K, N), seed + 1)
+    C = torch.full((M, N), float("nan"), dtype=torch.float32, device=DEV)
+    b2g.gemm(A, B, C, M, N, K)
+    torch.cuda.synchronize()
+    assert b2g.device_status() == 0
+    ref = torch.mm(A.to(torch.float64), B.to(torch.float64))
+    return int((C.to(torch.float64) != ref).sum().item())
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (8192, 8192, 8192), (16384, 16384, 4096),
+                                   (8192, 28672, 8192)],
+                         ids=["configs0", "configs1", "configs3_square", "configs3_wide"])
+def test_gemm_full_size_exact(b2g, cuda, M, N, K):
+    """BASELINE configs[0], [1] and the large configs[3] shapes, every element exact."""
+    assert _exact_gemm(b2g, cuda, M, N, K, seed=M + N + K) == 0
+
+
+@pytest.mark.parametrize("cluster_fixup", [1, 0], ids=["cluster_fixup", "global_fixup"])
+def test_gemm_skinny_full_size_exact(b2g, cuda, cluster_fixup):
+    """BASELINE configs[3] 128 x 8192 x 8192: every tile split over K, reduced either through
+    distributed shared memory or through the global workspace; every element exact."""
+    with options(b2g, cluster_fixup=cluster_fixup):
+        assert _exact_gemm(b2g, cuda, 128, 8192, 8192, seed=7) == 0
+
+
+def test_contraction_full_size_exact(b2g, cuda):
+    """C[a,b,i,n] = sum_{j,k} A[a,b,i,j,k] B[j,k,n] with a8 b16 i64 j64
+    k128 n4096 through the contraction entry point; every element exact."""
+    torch = cuda
+    sa, sb, sc = (8, 16, 64, 64, 128), (64, 128, 4096), (8, 16, 64, 4096)
+
+    def rowmajor(sh):
+        st, acc = [], 1
+        for d in reversed(sh):
+            st.append(acc)
+            acc *= d
+        return tuple(reversed(st))
+
+    A = _ternary(torch, sa, 21)
+    B = _ternary(torch, sb, 22)
+    C = torch.full(sc, float("nan"), dtype=torch.float32, device=DEV)
+    b2g.contract5d(A, sa, rowmajor(sa), B, sb, rowmajor(sb), C, sc, rowmajor(sc))
+    torch.cuda.synchronize()
+    assert b2g.device_status() == 0
+    ref = torch.mm(A.reshape(8 * 16 * 64, 64 * 128).to(torch.float64),
+                   B.reshape(64 * 128, 4096).to(torch.float64)).reshape(sc)
+    assert int((C.to(torch.float64) != ref).sum().item()) == 0
