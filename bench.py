@@ -426,6 +426,11 @@ def main():
                     "flops_per_launch": flops, "bytes_per_launch": alg_bytes,
                     "avg_launch_ms": avg_launch_ms}
     roofline["kernel"] = "gemm_tc_kernel"
+    # per-launch spread of the same pass: the minimum is what the reference reports
+    # (getBestTiming, mmm.cpp:1376)
+    roofline["min_launch_ms"] = min(launch_ms)
+    roofline["median_launch_ms"] = statistics.median(launch_ms)
+    roofline["launches_timed"] = len(launch_ms)
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and not args.kernel_only:
         v, rows, secs, thr = cpu_baseline(args.cpu_seconds)
