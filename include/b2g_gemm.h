@@ -100,8 +100,8 @@ int b2g_gemm_typed(const void* A, const void* B, float* C, int64_t M, int64_t N,
  * the library (every GPU that loads the library holds it until the process exits), not from
  * cudaMallocAsync.  A request whose split-K workspace would exceed 32 MiB returns
  * B2G_ERR_INVALID_ARG with a message saying so.  The first call on a device looks up the
- * array's device address (cudaGetSymbolAddress) for that device; make that first call before
- * any stream capture.  All calls share the one array, and it keeps the last call's contents
+ * array's device address (cudaGetSymbolAddress) for that device.  All calls share the one
+ * array, and it keeps the last call's contents
  * (each call clears the split counters it relies on): calls that overlap on the GPU -- on
  * different streams, or from different host threads -- race on it and must be serialized.
  */
@@ -131,20 +131,24 @@ int b2g_contract5d_f16_f32(const void* A, const int64_t a_shape[5], const int64_
                            float* C, const int64_t c_shape[4], const int64_t c_stride[4],
                            void* stream);
 
-/* The contraction with the alpha/beta epilogue of b2g_gemm_ex. */
+/* The contraction with the alpha/beta epilogue of b2g_gemm_ex (the reference's contraction
+ * always overwrites its Output, mmmTensor.cpp:246-252; alpha/beta follow the rocBLAS call at
+ * mmmTensor.cpp:393-420). */
 int b2g_contract5d_ex(const void* A, const int64_t a_shape[5], const int64_t a_stride[5],
                       const void* B, const int64_t b_shape[3], const int64_t b_stride[3],
                       float* C, const int64_t c_shape[4], const int64_t c_stride[4], float alpha,
                       float beta, void* stream);
 
-/* The contraction with an operand type argument (see b2g_gemm_typed). */
+/* The contraction with an operand type argument (see b2g_gemm_typed).  No reference
+ * counterpart: the reference's contraction is fp16 only. */
 int b2g_contract5d_typed(const void* A, const int64_t a_shape[5], const int64_t a_stride[5],
                          const void* B, const int64_t b_shape[3], const int64_t b_stride[3],
                          float* C, const int64_t c_shape[4], const int64_t c_stride[4], int dtype,
                          float alpha, float beta, void* stream);
 
 /* b2g_fill_uniform_f16 for any operand type: the same exact fp32 values, rounded to nearest
- * even into `dtype` (saturating to the largest finite value for the fp8 types). */
+ * even into `dtype` (saturating to the largest finite value for the fp8 types).  Replaces
+ * randomMatrix (mmm.cpp:1409-1414) for the non-fp16 types, which the reference does not have. */
 int b2g_fill_uniform(void* dst, int64_t n, int dtype, uint64_t seed, uint64_t offset, void* stream);
 
 /*
@@ -178,7 +182,8 @@ int b2g_gemm_sharded(const void* A_slab, void* B, float* C_slab, int64_t M, int6
  * (CUDA IPC) and signals the next rank through epoch flags written by stream memory
  * operations, so the broadcast uses no SM and overlaps the slab GEMMs.  b2g_chain_plan_destroy
  * is collective too (every rank calls it); it waits for this rank's queued calls, and frees
- * memory only after every rank has dropped its mappings of it.
+ * memory only after every rank has dropped its mappings of it.  No reference counterpart (the
+ * reference is single-GPU); BASELINE configs[4] asks for B to be broadcast over NVLink.
  */
 int b2g_chain_plan_create(void* comm, void* B, int64_t bytes, int root, void** plan);
 int b2g_chain_plan_destroy(void* plan);
@@ -187,7 +192,8 @@ int b2g_chain_plan_destroy(void* plan);
  * b2g_gemm_sharded over a chain plan: B is the plan's buffer (ldb, K rows); A_slab / C_slab
  * as in b2g_gemm_sharded.  Panel p's GEMM waits only for panel p to arrive.  The call
  * completes on `stream` once this rank's copies are done and the next rank has pulled every
- * panel from this rank's buffer, so the caller may then overwrite B.
+ * panel from this rank's buffer, so the caller may then overwrite B.  No reference
+ * counterpart (the reference is single-GPU).
  */
 int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_slab, int64_t M, int64_t N,
                            int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int k_panels,
@@ -197,7 +203,8 @@ int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_slab, int64_
  * b2g_gemm_sharded_n over a chain plan whose buffer is A (M x K, lda; the root's holds A): A
  * arrives in row panels along the chain, and panel p's GEMM writes rows of this rank's column
  * slab of C (B_nslab: K x n_r, C_nslab: M x n_r with (n0, n_r) = b2g_slab_rows(N, world,
- * rank)) as soon as that panel is here.  No NCCL kernel and no SM are used for A.
+ * rank)) as soon as that panel is here.  No NCCL kernel and no SM are used for A.  No
+ * reference counterpart.
  */
 int b2g_gemm_sharded_n_chain(void* plan, const void* B_nslab, float* C_nslab, int64_t M,
                              int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
@@ -224,7 +231,8 @@ int b2g_gemm_sharded_k(const void* A_kslab, const void* B_kslab, float* C_slab, 
  * slot r over NVLink, and rank r sums its slots in rank order into C_slab.  Epoch flags
  * written and waited for by stream memory operations order the ranks.  Every rank of the
  * plan calls it with the same M, N, K, in the same order.  b2g_rs_plan_destroy is collective.
- * The ranks are processes on one node with CUDA IPC between their GPUs.
+ * The ranks are processes on one node with CUDA IPC between their GPUs.  No reference
+ * counterpart.
  */
 int b2g_rs_plan_create(void* comm, int64_t M, int64_t N, void** plan);
 int b2g_rs_plan_destroy(void* plan);
@@ -237,7 +245,7 @@ int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const void* B_kslab,
  * (K x n_r, ldb) and of C (M x n_r, ldc); A (M x K, lda, every rank) is broadcast from `root`
  * in `m_panels` row panels, each followed by the GEMM of its rows.  With C_full != NULL
  * (N a multiple of the rank count) every rank also receives the whole row-major C (M x N)
- * there (ncclAllGather).
+ * there (ncclAllGather).  No reference counterpart.
  */
 int b2g_gemm_sharded_n(void* A, const void* B_nslab, float* C_nslab, int64_t M, int64_t N,
                        int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* comm, int root,
@@ -286,20 +294,23 @@ int b2g_gemm_batched(const void* A, const void* B, float* C, int64_t L, int64_t 
                      int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int64_t stride_a,
                      int64_t stride_b, int64_t stride_c, void* stream);
 
-/* Balanced contiguous row partition: rank r gets M/world rows, the first M%world ranks one more. */
+/* Balanced contiguous row partition: rank r gets M/world rows, the first M%world ranks one more.
+ * No reference counterpart (the reference is single-GPU). */
 int b2g_slab_rows(int64_t M, int world, int rank, int64_t* row0, int64_t* rows);
 
 /* NCCL communicator helpers for callers without their own NCCL: a 128-byte unique id made on
  * one rank and shared with the others out of band, then one b2g_comm_init per rank (with that
- * rank's device current). */
+ * rank's device current).  No reference counterpart. */
 int b2g_comm_unique_id(void* id_out);
 int b2g_comm_init(void** comm, int world, int rank, const void* id);
 int b2g_comm_destroy(void* comm);
 
-/* Message for the calling thread's last failed call ("" if none). */
+/* Message for the calling thread's last failed call ("" if none).  Replaces the messages the
+ * reference prints before exiting from HIP_CHECK / ROCBLAS_CHECK (mmm.cpp:33-49). */
 const char* b2g_last_error_string(void);
 
-/* Path taken by the calling thread's last successful compute call (B2G_PATH_*). */
+/* Path taken by the calling thread's last successful compute call (B2G_PATH_*).  No reference
+ * counterpart (the reference launches one kernel). */
 int b2g_last_path(void);
 
 /*
@@ -346,7 +357,7 @@ int64_t b2g_get_option(const char* key);
  */
 void b2g_tile_coord(int t, int num_m, int num_n, int group, int* tm, int* tn);
 
-/* Library version string. */
+/* Library version string.  No reference counterpart. */
 const char* b2g_version(void);
 
 #ifdef __cplusplus
