@@ -186,3 +186,33 @@ def test_plan_preview_follows_options(b2g):
         assert b2g.plan_preview(8192, 4096, 8192) == (2, 512, 1, 256)
     with pytest.raises(b2g.B2GError):
         b2g.plan_preview(0, 8, 8)
+
+
+def test_plan_preview_invariants(b2g):
+    """Random shapes, operand types and SM counts: the launch plan is always one the kernel can
+    run.  Legal tile shapes; one-CTA tiles split at most 8 ways (the largest cluster of the
+    cluster fix-up), pairs at most 16; every split keeps at least 16 K blocks; the split units
+    of one launch fit in the resident CTA groups; unsplit plans run every tile whole."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=400, deadline=None)
+    @given(M=st.integers(1, 40000), N=st.integers(1, 40000), K=st.integers(1, 70000),
+           dtype=st.sampled_from([0, 1, 2, 3]), sms=st.sampled_from([148, 132, 74, 16, 2]))
+    def check(M, N, K, dtype, sms):
+        cg, bn, splits, full = b2g.plan_preview(M, N, K, dtype, sms)
+        assert cg in (1, 2) and bn in (128, 256, 512)
+        assert not (cg == 1 and bn == 512) and not (bn == 128 and cg == 2)
+        esz = 2 if dtype < 2 else 1
+        k_iters = -(-K * esz // 128)  # a K block is 128 bytes of K
+        tiles = -(-(-(-M // 128)) // cg) * -(-N // bn)
+        assert 1 <= splits <= (8 if cg == 1 else 16)
+        assert splits <= max(1, k_iters)
+        assert 0 <= full <= tiles
+        if splits == 1:
+            assert full == tiles
+        else:
+            assert -(-k_iters // splits) >= 16
+            groups = sms if cg == 1 else max(1, sms // 2)
+            assert (tiles - full) * splits <= groups
+
+    check()
