@@ -59,6 +59,27 @@ def test_blocked_cpu_baseline_bit_exact_vs_reference_gemm_naive(orc):
             assert np.array_equal(got.view(np.uint32), C.view(np.uint32)), "case %d" % i
 
 
+def test_blocked_cpu_baseline_bit_exact_vs_sequential_random(orc):
+    """Random ragged shapes, row ranges, thread counts and a shared widened B: the blocked
+    baseline keeps GEMM_Naive's arithmetic (fp32, k ascending) bit for bit."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=60, deadline=None)
+    @given(M=st.integers(1, 70), N=st.integers(1, 140), K=st.integers(1, 300),
+           seed=st.integers(0, 2**31), threads=st.integers(1, 5), data=st.data())
+    def check(M, N, K, seed, threads, data):
+        r0 = data.draw(st.integers(0, M - 1))
+        r1 = data.draw(st.integers(r0 + 1, M))
+        A = orc.uniform_f16((M, K), seed)
+        B = orc.uniform_f16((K, N), seed + 1)
+        ref = orc.gemm_f32_seq(A, B, rows=(r0, r1))
+        Bf = orc.widen_b(B, threads=threads) if seed % 2 else None
+        got = orc.gemm_f32_blocked(A, B, rows=(r0, r1), threads=threads, Bf=Bf)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+    check()
+
+
 def test_fp64_oracle_within_tolerance_of_reference(orc):
     for i, A, B, C, _ in _gemm_cases():
         K = A.shape[1]
