@@ -6,8 +6,10 @@ dense FP16 peak, 8192^3 fp16 -> fp32 GEMM, 1/2/4/8 GPU).
 
 One step = one 8192 x 8192 x 8192 GEMM per GPU.  With N > 1 (one
 process per GPU under torchrun) rank r owns rows [8192 r, 8192 (r+1)) of an
-(8192 N) x 8192 x 8192 GEMM: M-row slabs, B broadcast once from rank 0 over NCCL at
-set-up, C written locally with no reduction (weak scaling: per-GPU work fixed).
+(8192 N) x 8192 x 8192 GEMM: M-row slabs, C written locally with no reduction (weak
+scaling: per-GPU work fixed), and every step also sends the whole B (128 MiB) from rank 0
+to every rank along the library's copy-engine chain (b2g_chain_broadcast, peer copies over
+NVLink, no SM).  B is double-buffered: step i+1's B travels while step i's slab GEMM runs.
 
 Prints one JSON line (rank 0).  value = all ranks' FLOPs / max-over-ranks device time of K
 steps with inputs resident in HBM.  e2e = the same metric through the public C ABI with
@@ -313,16 +315,54 @@ def main():
     dC = torch.empty((M, N), device=dev,
                      dtype={"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[args.out])
     dBias = torch.randn(N, device=dev) if args.bias else None
-    # rank r's slab of the (M*ws) x K matrix A; B generated on rank 0 and broadcast once
+    # rank r's slab of the (M*ws) x K matrix A; B generated on rank 0
     b2g.fill_uniform(dA, M * K, 1, rank * M * K, stream, dtype=dt)
     if rank == 0:
         b2g.fill_uniform(dB, K * N, 2, 0, stream, dtype=dt)
-    if ws > 1:
-        dist.broadcast(dB, src=0)
     torch.cuda.synchronize()
+    # N > 1: B travels from rank 0 along the copy-engine chain (peer copies over NVLink, no SM)
+    # inside every step.  Two B buffers with a chain plan each: while step i's slab GEMM reads
+    # buffer i % 2, the broadcast of step i+1's B fills the other one, so every timed step
+    # moves the whole B to every rank and computes one slab GEMM.
+    chain = None
+    if ws > 1 and (contraction or dt or epilogue):
+        dist.broadcast(dB, src=0)  # secondary lines: B replicated once at set-up
+        torch.cuda.synchronize()
+    elif ws > 1:
+        comm = library_comm(torch, dist, b2g, ws, rank, dev)
+        dB2 = torch.empty_like(dB)
+        if rank == 0:
+            dB2.copy_(dB)
+        bufs = [dB, dB2]
+        plans = [b2g.chain_plan_create(comm, b, K * N * dB.element_size(), 0) for b in bufs]
+        sb = torch.cuda.Stream(dev)
+        chain = {"comm": comm, "bufs": bufs, "plans": plans, "sb": sb, "n": 0,
+                 "bdone": [torch.cuda.Event() for _ in range(2)],
+                 "gdone": [torch.cuda.Event() for _ in range(2)],
+                 "bytes": K * N * dB.element_size(), "panels": 8}
+
+        def bcast(i):
+            b = i % 2
+            chain["sb"].wait_event(chain["gdone"][b])  # the GEMM that read this buffer is done
+            b2g.chain_broadcast(chain["plans"][b], chain["bytes"], chain["panels"],
+                                stream=chain["sb"].cuda_stream)
+            chain["bdone"][b].record(chain["sb"])
+
+        bcast(0)  # step 0's B; every step then broadcasts the next step's
+        torch.cuda.synchronize()
+        sys.stderr.write("rank %d/%d: B (%d MiB) along a copy-engine chain of %d ranks every "
+                         "step\n" % (rank, ws, chain["bytes"] >> 20, ws))
 
     def step():
-        if contraction:
+        if chain is not None:
+            i = chain["n"]
+            b = i % 2
+            bcast(i + 1)
+            stream.wait_event(chain["bdone"][b])
+            b2g.gemm(dA, chain["bufs"][b], dC, M, N, K, K, N, N, stream)
+            chain["gdone"][b].record(stream)
+            chain["n"] = i + 1
+        elif contraction:
             b2g.contract5d(dA, a_shape, rowmajor(a_shape), dB, b_shape, rowmajor(b_shape), dC,
                            c_shape, rowmajor(c_shape), stream)
         elif epilogue:
@@ -351,8 +391,12 @@ def main():
         sampler.start()
     launches0 = b2g.get_option("launches")
     t_start.record(stream)
+    if chain is not None:
+        chain["sb"].wait_stream(stream)  # the timed broadcasts start inside the region
     for i in range(args.steps):
         step()
+    if chain is not None:
+        stream.wait_stream(chain["sb"])  # ... and the last one ends inside it
     t_end.record(stream)
     launches = b2g.get_option("launches") - launches0
     torch.cuda.synchronize()
@@ -378,6 +422,27 @@ def main():
     path = b2g.PATH_NAMES.get(b2g.last_path(), "?")
     if b2g.device_status() != 0:
         raise SystemExit("device-side wait timed out during the timed region")
+    chain_info = None
+    if chain is not None:
+        # spot check on every rank: row 0 of the last step's slab against the FP64 product
+        # with the B this rank received, and that B identical on every rank (checksums)
+        last = chain["bufs"][(chain["n"] - 1) % 2]
+        bad = row_out_of_tolerance(torch, dC[:1], dA[:1], last, K)
+        sums = []
+        for b in chain["bufs"]:
+            cs = b.view(torch.int16).to(torch.int64).sum().reshape(1)
+            lo, hi = cs.clone(), cs.clone()
+            dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+            dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+            sums.append(bool(lo.item() == hi.item()))
+        chk = torch.tensor([bad], dtype=torch.int64, device=dev)
+        dist.all_reduce(chk, op=dist.ReduceOp.MAX)
+        for p in chain["plans"]:
+            b2g.chain_plan_destroy(p)
+        b2g.comm_destroy(chain["comm"])
+        chain_info = {"ranks_in_chain": ws, "bytes_per_step": chain["bytes"],
+                      "panels": chain["panels"], "row0_out_of_tolerance_max_over_ranks":
+                      int(chk.item()), "b_identical_on_all_ranks": all(sums)}
     if ws > 1:
         dist.barrier()
 
@@ -474,8 +539,11 @@ def main():
                          "configs[2]; GEMM view %dx%dx%d)" % (M, N, K)) if contraction
                         else ("gemm %dx%dx%d row-major fp16->fp32 (kernel loop)" % (M, N, K)) if args.shape
                         else "gemm 8192x8192x8192 row-major fp16->fp32 per GPU (BASELINE configs[1]);"
-                             " N>1: M-row slabs of a (8192N)x8192x8192 GEMM, B broadcast once",
+                             " N>1: M-row slabs of a (8192N)x8192x8192 GEMM, B (128 MiB) sent from "
+                             "rank 0 along the copy-engine chain every step, double-buffered (step "
+                             "i+1's B travels while step i's slab GEMM runs)",
             "M": M, "N": N, "K": K, "world_size": ws, "path": path,
+            "broadcast": chain_info,
             "l2": "inputs+output %.0f MiB per GPU (%s 126 MB L2)" % (
                 alg_bytes / 2**20, "> : no flush needed" if alg_bytes > 126e6 else
                 "< : steps may hit L2"),

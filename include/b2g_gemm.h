@@ -200,6 +200,18 @@ int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_slab, int64_
                            void* stream);
 
 /*
+ * The chain on its own: the first `bytes` bytes of the plan's buffer travel from the root
+ * along the chain in about `panels` panels (peer copies, no SM), ordered after prior work on
+ * `stream`.  The call completes on `stream` once this rank holds every byte and the next rank
+ * has pulled every panel from this rank's buffer.  A caller that keeps two plans over two
+ * buffers can broadcast the operand of its next step while its current step computes with
+ * the other buffer.  Every rank of the plan makes the same calls in the same order.  No
+ * reference counterpart (the reference is single-GPU); BASELINE configs[4] asks for B to be
+ * broadcast over NVLink.
+ */
+int b2g_chain_broadcast(void* plan, int64_t bytes, int panels, void* stream);
+
+/*
  * b2g_gemm_sharded_n over a chain plan whose buffer is A (M x K, lda; the root's holds A): A
  * arrives in row panels along the chain, and panel p's GEMM writes rows of this rank's column
  * slab of C (B_nslab: K x n_r, C_nslab: M x n_r with (n0, n_r) = b2g_slab_rows(N, world,
@@ -340,11 +352,16 @@ int b2g_device_status(int clear);
  *                  partials go through a global workspace
  *   "pdl"          1 (default) = tensor-core launches use programmatic dependent launch (the
  *                  kernel's set-up overlaps the previous kernel in the stream); 0 = plain launch
+ *   "ring_slots"   split-K arrival counters usable in the per-device ring (default and
+ *                  maximum 1048576, a multiple of 64, at least 512): a small ring makes tests
+ *                  wrap it often
  *   "fault_flags"  test-only fault injection: bit 0 = the TMA producer issues no loads,
  *                  so the MMA wait runs out and the call reports B2G_ERR_TIMEOUT
  * Returns B2G_OK or B2G_ERR_INVALID_ARG for an unknown key or value.  Options are
  * process-wide.  b2g_get_option("launches") (read-only) returns how many kernels the library
- * has launched in this process.
+ * has launched in this process; b2g_get_option("last_split_ws_bytes") (read-only) the bytes of
+ * split-K partial tiles the calling thread's last tensor-core launch kept in global memory (0
+ * when it split nothing or reduced its splits through distributed shared memory).
  */
 int b2g_set_option(const char* key, int64_t value);
 int64_t b2g_get_option(const char* key);

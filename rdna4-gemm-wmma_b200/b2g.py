@@ -107,6 +107,8 @@ def load(path=None):
     L.b2g_chain_plan_destroy.argtypes = [vp]
     L.b2g_gemm_sharded_chain.restype = ctypes.c_int
     L.b2g_gemm_sharded_chain.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, vp]
+    L.b2g_chain_broadcast.restype = ctypes.c_int
+    L.b2g_chain_broadcast.argtypes = [vp, i64, ctypes.c_int, vp]
     L.b2g_plan_preview.restype = ctypes.c_int
     L.b2g_plan_preview.argtypes = [i64, i64, i64, ctypes.c_int, ctypes.c_int] + \
         [ctypes.POINTER(ctypes.c_int)] * 4
@@ -352,6 +354,11 @@ def gemm_sharded_chain(plan, A_slab, C_slab, M, N, K, k_panels=8, lda=None, ldb=
     _check(load().b2g_gemm_sharded_chain(plan, _ptr(A_slab), _ptr(C_slab), M, N, K,
                                          K if lda is None else lda, N if ldb is None else ldb,
                                          N if ldc is None else ldc, k_panels, _stream(stream)))
+
+
+def chain_broadcast(plan, nbytes, panels=8, stream=None):
+    """The plan's buffer (first nbytes) from the root to every rank along the chain."""
+    _check(load().b2g_chain_broadcast(plan, nbytes, panels, _stream(stream)))
 
 
 def plan_preview(M, N, K, dtype=0, sm_count=148):

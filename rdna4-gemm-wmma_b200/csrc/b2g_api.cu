@@ -21,6 +21,8 @@
 #include <mutex>
 #include <string>
 #include <unordered_map>
+#include <utility>
+#include <vector>
 
 #include "../../include/b2g_gemm.h"
 #include "errors.h"
@@ -32,6 +34,9 @@ namespace b2g {
 // ------------------------------------------------------------------ errors / options
 static thread_local std::string t_err;
 static thread_local int t_path = B2G_PATH_NONE;
+// Split-K workspace bytes (partial tiles) of the calling thread's last tensor-core launch: 0
+// when it split nothing or reduced through distributed shared memory.
+static thread_local int64_t t_split_ws = 0;
 
 static int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -331,6 +336,12 @@ static int noalloc_scratch(FixedScratch* out) {
 // device error (b2g_device_status(1)) marks the ring for one full reset before its next use.
 // Calls captured into a CUDA graph do not use the ring (a graph replays fixed addresses long
 // after the ring has moved on); they zero their counters with a memset node instead.
+//
+// Streams: calls on several streams share the ring.  Each call that takes counters records an
+// event on its stream after its launch (under the ring's lock, so no other call can wrap the
+// ring in between).  Before the ring wraps to its start, or is reset, the calling stream waits
+// for the last such event of every other stream that used the ring since the previous wrap, so
+// a range is never handed out again while a kernel on another stream may still use it.
 constexpr size_t kCounterSlots = (size_t)1 << 20;  // 4 MiB of ints per device
 static __device__ int g_split_counters[kCounterSlots];
 
@@ -338,35 +349,97 @@ struct CounterRing {
   int* base = nullptr;
   size_t next = 0;
   bool dirty = false;
+  std::vector<std::pair<cudaStream_t, cudaEvent_t>> users;  // since the last wrap
+  std::vector<cudaEvent_t> spare;
 };
 static std::mutex g_ring_mu;
 static CounterRing g_ring[64];
 
+// Holds the ring of one device locked from the hand-out of a range until the launch that uses
+// it has been recorded (commit), or until it goes out of scope.
+struct RingLease {
+  std::unique_lock<std::mutex> lk;
+  CounterRing* ring = nullptr;
+  RingLease() : lk(g_ring_mu, std::defer_lock) {}
+  // after the launch: record this stream's use of the ring
+  void commit(cudaStream_t stream) {
+    if (!ring) return;
+    cudaEvent_t ev = nullptr;
+    for (auto& u : ring->users)
+      if (u.first == stream) ev = u.second;
+    if (!ev) {
+      if (!ring->spare.empty()) {
+        ev = ring->spare.back();
+        ring->spare.pop_back();
+      } else if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+        ev = nullptr;
+      }
+      if (ev) ring->users.emplace_back(stream, ev);
+    }
+    if (ev) cudaEventRecord(ev, stream);
+    ring = nullptr;
+    lk.unlock();
+  }
+};
+
+// The calling stream waits for every other stream's last use of the ring; the list restarts.
+static int ring_fence(CounterRing& r, cudaStream_t stream) {
+  for (auto& u : r.users) {
+    if (u.first != stream) {
+      cudaError_t e = cudaStreamWaitEvent(stream, u.second, 0);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent(split-K counter ring)");
+    }
+    r.spare.push_back(u.second);
+  }
+  r.users.clear();
+  return B2G_OK;
+}
+
 // `n` zeroed counters on the current device, or nullptr when `n` is too large for the ring.
-static int ring_counters(size_t n, cudaStream_t stream, int** out) {
+// On success with a non-null range the lease holds the ring until lease.commit(stream).
+static std::atomic<int64_t> opt_ring_slots{(int64_t)kCounterSlots};  // test knob: usable slots
+
+static int ring_counters(size_t n, cudaStream_t stream, int** out, RingLease* lease) {
   *out = nullptr;
-  if (n == 0 || n > kCounterSlots / 8) return B2G_OK;
+  const size_t cap = std::min(kCounterSlots, (size_t)opt_ring_slots.load());
+  if (n == 0 || n > cap / 8) return B2G_OK;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= 64) return fail(B2G_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
-  std::lock_guard<std::mutex> lk(g_ring_mu);
+  lease->lk.lock();
   CounterRing& r = g_ring[dev];
   if (!r.base) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_split_counters);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(split-K counters)");
+    if (e != cudaSuccess) {
+      lease->lk.unlock();
+      return cuda_fail(e, "cudaGetSymbolAddress(split-K counters)");
+    }
     r.base = static_cast<int*>(p);
+  }
+  const size_t m = (n + 63) / 64 * 64;  // 256-byte granules
+  const bool wrap = r.next + m > cap;
+  if (r.dirty || wrap) {
+    int rc = ring_fence(r, stream);
+    if (rc != B2G_OK) {
+      lease->lk.unlock();
+      return rc;
+    }
   }
   if (r.dirty) {
     e = cudaMemsetAsync(r.base, 0, kCounterSlots * sizeof(int), stream);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(split-K counter ring)");
+    if (e != cudaSuccess) {
+      lease->lk.unlock();
+      return cuda_fail(e, "cudaMemsetAsync(split-K counter ring)");
+    }
     r.dirty = false;
+    r.next = 0;
   }
-  const size_t m = (n + 63) / 64 * 64;  // 256-byte granules
-  if (r.next + m > kCounterSlots) r.next = 0;
+  if (r.next + m > cap) r.next = 0;
   *out = r.base + r.next;
   r.next += m;
+  lease->ring = &r;
   return B2G_OK;
 }
 
@@ -789,6 +862,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   }
   p.num_full = full;
   p.num_units = full + (p.num_tiles - full) * p.k_splits;
+  t_split_ws = 0;
   p.ws = nullptr;
   p.counters = nullptr;
   // Cluster fix-up: one-CTA tiles, every tile split, at most 8 splits, and one unit per CTA
@@ -826,15 +900,18 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   void* scratch = nullptr;
   const size_t split_tiles = (size_t)(p.num_tiles - p.num_full);
   int* ring = nullptr;  // counters from the ring: no memset
+  RingLease lease;      // holds the ring until the launch is recorded
   if (p.k_splits > 1 && !p.cluster_fixup) {
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaError_t e = cudaStreamIsCapturing(stream, &cap);
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
     if (cap == cudaStreamCaptureStatusNone) {
-      int rrc = ring_counters(split_tiles * cg, stream, &ring);
+      int rrc = ring_counters(split_tiles * cg, stream, &ring, &lease);
       if (rrc != B2G_OK) return rrc;
     }
   }
+  if (p.k_splits > 1 && !p.cluster_fixup)
+    t_split_ws = (int64_t)(split_tiles * p.k_splits * cg * 128 * bn * sizeof(float));
   if (p.cluster_fixup) {
     // partials stay in shared memory: no workspace, no counters
   } else if (p.k_splits > 1 && fixed) {
@@ -907,6 +984,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     ++cfg.numAttrs;
   }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
+  lease.commit(stream);
   if (scratch) cudaFreeAsync(scratch, stream);  // stream-ordered: freed after the kernel
   if (e != cudaSuccess) return cuda_fail(e, "tcgen05 kernel launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -1146,6 +1224,13 @@ extern "C" int b2g_device_status(int clear) {
     fail(B2G_ERR_CUDA, "read device error word: %s", cudaGetErrorString(e));
     return -1;
   }
+  int vs = 0;  // the multi-GPU kernels' word (a peer's failed part of a reduce-scatter)
+  const int se = shard_device_error(clear, &vs);
+  if (se != 0) {
+    fail(B2G_ERR_CUDA, "read shard error word: %s", cudaGetErrorString((cudaError_t)se));
+    return -1;
+  }
+  if (v == 0) v = vs;
   if (clear) {
     if (v != 0) ring_mark_dirty();  // a kernel that gave up may have left counters set
     const int z = 0;
@@ -1186,6 +1271,9 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_split_k = value;
   } else if (!strcmp(key, "store_hint")) {
     opt_store_hint = value ? 1 : 0;
+  } else if (!strcmp(key, "ring_slots")) {
+    if (value < 512 || value > (int64_t)kCounterSlots || value % 64) return B2G_ERR_INVALID_ARG;
+    opt_ring_slots = value;
   } else if (!strcmp(key, "tile_n")) {
     if (value != 0 && value != 128 && value != 256 && value != 512) return B2G_ERR_INVALID_ARG;
     opt_tile_n = value;
@@ -1198,6 +1286,7 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
 extern "C" int64_t b2g_get_option(const char* key) {
   if (!key) return -1;
   if (!strcmp(key, "launches")) return g_launches.load();
+  if (!strcmp(key, "last_split_ws_bytes")) return t_split_ws;
   if (!strcmp(key, "cta_group")) return opt_cta_group;
   if (!strcmp(key, "raster_group")) return opt_raster_group;
   if (!strcmp(key, "timeout_ns")) return opt_timeout_ns;
@@ -1210,6 +1299,7 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "pdl")) return opt_pdl;
   if (!strcmp(key, "cluster_fixup")) return opt_cluster_fixup;
   if (!strcmp(key, "serial_fixup")) return opt_serial_fixup;
+  if (!strcmp(key, "ring_slots")) return opt_ring_slots;
   return -1;
 }
 

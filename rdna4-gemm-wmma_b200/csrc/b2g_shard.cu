@@ -25,6 +25,21 @@
 #include "../../include/b2g_gemm.h"
 #include "errors.h"
 
+using b2g::kErrPeerFailed;
+
+// Device error word of this file's kernels: 0, or kErrPeerFailed once a reduction found that a
+// peer's part of the call had failed.
+__device__ int g_shard_error;
+
+int b2g::shard_device_error(int clear, int* value) {
+  cudaError_t e = cudaMemcpyFromSymbol(value, g_shard_error, sizeof(int));
+  if (e == cudaSuccess && clear) {
+    const int z = 0;
+    e = cudaMemcpyToSymbol(g_shard_error, &z, sizeof(int));
+  }
+  return (int)e;
+}
+
 namespace {
 
 struct NcclApi {
@@ -727,6 +742,24 @@ extern "C" int b2g_gemm_sharded_chain(void* plan, const void* A_slab, float* C_s
                         });
 }
 
+extern "C" int b2g_chain_broadcast(void* plan, int64_t bytes, int panels, void* stream) {
+  b2g::set_error("");
+  auto* p = static_cast<b2g_chain_plan*>(plan);
+  if (!p || bytes < 0) return sfail(B2G_ERR_INVALID_ARG, "bad broadcast arguments");
+  if (bytes > p->bytes) return sfail(B2G_ERR_INVALID_ARG, "bytes exceed the plan's buffer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Panels in 64 KiB units (the chain's panel rule works on 64-row multiples; a row here is
+  // 1 KiB), the last one holding the remainder bytes.
+  const int64_t unit = 1024;
+  const int64_t rows = (bytes + unit - 1) / unit;
+  auto pan = chain_panels(rows, panels, p->world);
+  for (auto& q : pan) {
+    q.first = std::min(bytes, q.first * unit);
+    q.second = std::min(bytes, q.second * unit);
+  }
+  return chain_pipeline(p, pan, 1, s, [](size_t, int64_t, int64_t) { return B2G_OK; });
+}
+
 extern "C" int b2g_gemm_sharded_n_chain(void* plan, const void* B_nslab, float* C_nslab, int64_t M,
                                         int64_t N, int64_t K, int64_t lda, int64_t ldb,
                                         int64_t ldc, int m_panels, void* stream) {
@@ -763,7 +796,9 @@ struct b2g_rs_plan {
   int world = 1, rank = 0, dev = 0;
   int64_t M = 0, N = 0, rows = 0;
   float* recv = nullptr;         // [world][rows][N]: slot s holds rank s's partial of my rows
-  uint32_t* flags = nullptr;     // [world] partial of rank s landed, [world] rank q's slots free
+  uint32_t* flags = nullptr;     // [world] partial of rank s landed, [world] rank q's slots free,
+                                 // [world] call status of rank s (the epoch, or the epoch with
+                                 // bit 31 set when that rank's part failed)
   std::vector<float*> peer_recv;       // rank q's receive slots, mapped here (q == rank: recv)
   std::vector<uint32_t*> peer_flags;   // rank q's flag array, mapped here
   std::vector<void*> opened;
@@ -788,10 +823,26 @@ void rs_plan_free(b2g_rs_plan* p) {
 }
 
 // C[i][j] = sum over s in rank order of R[s][i][j]: rows x N, slots `rows * N` floats apart.
+// status[s] is the call status rank s wrote before announcing its partial: the call's epoch
+// when its part succeeded.  If any peer's part failed, its slot holds a stale partial: C is
+// filled with NaN instead and the library's device error word records ERR_PEER_FAILED.
 __global__ void rs_reduce_kernel(const float* __restrict__ R, float* __restrict__ C, int64_t rows,
-                                 int64_t N, int64_t ldc, int world, int vec) {
+                                 int64_t N, int64_t ldc, int world, int vec,
+                                 const uint32_t* status, uint32_t epoch, int self) {
   const int64_t slot = rows * N;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  bool peer_failed = false;
+  for (int s = 0; s < world; ++s)
+    if (s != self && __ldcv(status + s) != epoch) peer_failed = true;
+  if (peer_failed) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&g_shard_error, 0, kErrPeerFailed);
+    const float nan = __int_as_float(0x7fc00000);
+    for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < slot; v += stride) {
+      const int64_t i = v / N, j = v - i * N;
+      C[i * ldc + j] = nan;
+    }
+    return;
+  }
   if (vec) {
     const int64_t n4 = N / 4;
     for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < rows * n4; v += stride) {
@@ -845,8 +896,8 @@ extern "C" int b2g_rs_plan_create(void* comm, int64_t M, int64_t N, void** plan_
   cudaGetDevice(&p->dev);
   const size_t rbytes = std::max<size_t>(16, (size_t)p->world * p->rows * N * sizeof(float));
   cudaError_t e = cudaMalloc(&p->recv, rbytes);
-  if (e == cudaSuccess) e = cudaMalloc(&p->flags, 2 * p->world * sizeof(uint32_t));
-  if (e == cudaSuccess) e = cudaMemset(p->flags, 0, 2 * p->world * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMalloc(&p->flags, 3 * p->world * sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(p->flags, 0, 3 * p->world * sizeof(uint32_t));
   int rc = e == cudaSuccess ? B2G_OK : cuda_sfail(e, "reduce-scatter plan set-up");
   p->peer_recv.assign(p->world, nullptr);
   p->peer_flags.assign(p->world, nullptr);
@@ -1012,7 +1063,12 @@ extern "C" int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const voi
                      kr > 0 ? lda : 1, ldb, N, 1.0f, 0.0f, s);
   }
   // announce this rank's partials (the default write orders the GEMMs' stores before it), then
-  // wait for every peer's
+  // wait for every peer's.  The status word goes first: the epoch if this rank's part
+  // succeeded, the epoch with bit 31 set if it did not, so that the peers' reductions do not
+  // sum a stale partial as if it were this call's.
+  const uint32_t st = rc == B2G_OK ? ep : (ep | 0x80000000u);
+  for (int q = 0; q < W; ++q)
+    if (q != R) cu(d->write32(cs, flag(p->peer_flags[q], 2 * W + R), st, 0), "cuStreamWriteValue32(status)");
   for (int q = 0; q < W; ++q)
     if (q != R) cu(d->write32(cs, flag(p->peer_flags[q], R), ep, 0), "cuStreamWriteValue32(landed)");
   for (int q = 0; q < W; ++q)
@@ -1024,7 +1080,8 @@ extern "C" int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const voi
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->dev);
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)sms * 8));
-    rs_reduce_kernel<<<grid, 256, 0, s>>>(p->recv, C_slab, rows, N, ldc, W, vec);
+    rs_reduce_kernel<<<grid, 256, 0, s>>>(p->recv, C_slab, rows, N, ldc, W, vec, p->flags + 2 * W,
+                                          ep, R);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) rc = cuda_sfail(e, "rs_reduce_kernel");
     else b2g::count_launch();

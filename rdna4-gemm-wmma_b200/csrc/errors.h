@@ -6,4 +6,9 @@
 namespace b2g {
 void set_error(const char* msg);
 void count_launch();
+// Device error word of the multi-GPU kernels (b2g_shard.cu), merged into b2g_device_status():
+// reads it and, with clear != 0, resets it; returns 0 or a cudaError_t.
+int shard_device_error(int clear, int* value);
+// Device-side error codes beyond the bounded-wait codes of the GEMM kernel (1..6).
+constexpr int kErrPeerFailed = 7;  // a peer's part of a peer-memory reduce-scatter failed
 }  // namespace b2g

@@ -91,12 +91,24 @@ def sharded_gemm_k(A_kslab, B_kslab, C_slab, M, N, K, group=None, gemm=None):
     return rank * rows, rows
 
 
+class PeerFailedError(RuntimeError):
+    """A peer's part of a collective call failed, so this rank's result is invalid (it has been
+    filled with NaN)."""
+
+
 def sharded_gemm_k_p2p(A_kslab, B_kslab, C_slab, M, N, K, group=None, gemm=None):
     """The schedule of b2g_gemm_sharded_k_p2p.  This rank computes its partial one row slab at a
     time, the other ranks' slabs first (q = rank+1, ..., rank-1) and its own last; slab q lands
     in receive slot `rank` of rank q; every rank sums its slots in rank order (slot 0 first).
     The C library stores each slab into the owner's slot over peer memory from the GEMM's
-    epilogue; here each slab travels as one point-to-point message.  Returns (row0, rows)."""
+    epilogue; here each slab travels as one point-to-point message.  Returns (row0, rows).
+
+    Failure: a rank whose own arguments are invalid (here a C_slab narrower than N, the
+    library's ldc < N) still takes every step of the protocol but skips its GEMMs, and tells
+    the others so (the library writes a status word into every peer's flags before its
+    'landed' flag; here the statuses are all-gathered).  It raises ValueError; every other rank
+    fills its C_slab with NaN and raises PeerFailedError (the library reports that through the
+    device error word, b2g_device_status)."""
     import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
@@ -105,25 +117,36 @@ def sharded_gemm_k_p2p(A_kslab, B_kslab, C_slab, M, N, K, group=None, gemm=None)
         raise ValueError("M must be a multiple of the rank count")
     k0, kr = slab_rows(K, world, rank)
     rows = M // world
+    ok = C_slab.dim() == 2 and C_slab.shape[0] >= rows and C_slab.shape[1] >= N
     gemm = gemm or _b2g_gemm
     peer = (lambda q: dist.get_global_rank(group, q)) if group is not None else (lambda q: q)
-    slots = torch.empty((world, rows, N), dtype=C_slab.dtype, device=C_slab.device)
+    slots = torch.zeros((world, rows, N), dtype=C_slab.dtype, device=C_slab.device)
     lda = A_kslab.stride(0) if kr else 1
     reqs, parts = [], []
     for t in range(1, world + 1):
         q = (rank + t) % world
-        part = slots[rank] if q == rank else torch.empty((rows, N), dtype=C_slab.dtype,
+        part = slots[rank] if q == rank else torch.zeros((rows, N), dtype=slots.dtype,
                                                           device=C_slab.device)
-        gemm(A_kslab[q * rows:(q + 1) * rows], B_kslab, part, rows, N, kr, 0.0, lda,
-             B_kslab.stride(0), N)
+        if ok:
+            gemm(A_kslab[q * rows:(q + 1) * rows], B_kslab, part, rows, N, kr, 0.0, lda,
+                 B_kslab.stride(0), N)
         if q != rank:
             parts.append(part)
             reqs.append(dist.isend(part, peer(q), group=group))
     for q in range(world):
         if q != rank:
             reqs.append(dist.irecv(slots[q], peer(q), group=group))
+    status = torch.tensor([0 if ok else 1], dtype=torch.int32)
+    statuses = [torch.zeros(1, dtype=torch.int32) for _ in range(world)]
+    dist.all_gather(statuses, status, group=group)
     for r in reqs:
         r.wait()
+    if not ok:
+        raise ValueError("C_slab must hold M/world rows of N columns")
+    failed = [q for q in range(world) if q != rank and int(statuses[q].item())]
+    if failed:
+        C_slab[:rows, :N] = float("nan")
+        raise PeerFailedError("the part of rank(s) %s failed" % failed)
     acc = slots[0].clone()
     for q in range(1, world):
         acc += slots[q]

@@ -374,3 +374,157 @@ def nccl_n_chain_rank(rank, world, uid_path, M, N, K, panels, calls, out_q):
         out_q.put((rank, nr, worst, status, a_ok, None))
     except Exception:
         out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))
+
+
+def nccl_chain_bcast_rank(rank, world, uid_path, M, N, K, panels, steps, out_q):
+    """Double-buffered broadcast along the copy-engine chain (b2g_chain_broadcast), the pattern
+    of bench.py's multi-GPU line: two B buffers with a chain plan each; while step i's slab
+    GEMM reads buffer i%2, the broadcast of step i+1's B (the root writes a new seed into it
+    first) fills the other.  Every step's slab is checked on sampled rows against the FP64
+    oracle with that step's B, and the last two B buffers must be bit-exact on every rank."""
+    try:
+        import torch
+        from oracle import orc
+        b2g = _load_pkg("b2g")
+        torch.cuda.set_device(rank)
+        comm = _nccl_comm(b2g, rank, world, uid_path)
+        row0, rows = b2g.slab_rows(M, world, rank)
+        dA = torch.empty((max(rows, 1), K), dtype=torch.float16, device="cuda")
+        b2g.fill_uniform(dA, rows * K, 1, row0 * K)
+        nbytes = K * N * 2
+        dB = [torch.full((K, N), float("nan"), dtype=torch.float16, device="cuda")
+              for _ in range(2)]
+        plans = [b2g.chain_plan_create(comm, dB[b], nbytes, 0) for b in range(2)]
+        s = torch.cuda.current_stream()
+        sb = torch.cuda.Stream()
+        bdone = [torch.cuda.Event() for _ in range(2)]
+        gdone = [torch.cuda.Event() for _ in range(2)]
+
+        def bcast(step):
+            b = step % 2
+            sb.wait_event(gdone[b])  # the GEMM that read this buffer two steps ago is done
+            if rank == 0:
+                b2g.fill_uniform(dB[b], K * N, 300 + step, 0, sb.cuda_stream)
+            b2g.chain_broadcast(plans[b], nbytes, panels, stream=sb.cuda_stream)
+            bdone[b].record(sb)
+
+        torch.cuda.synchronize()
+        bcast(0)
+        outs = []
+        for i in range(steps):
+            if i + 1 < steps:
+                bcast(i + 1)
+            s.wait_event(bdone[i % 2])
+            dC = torch.full((max(rows, 1), N), float("nan"), dtype=torch.float32, device="cuda")
+            if rows:
+                b2g.gemm(dA, dB[i % 2], dC, rows, N, K, stream=s.cuda_stream)
+            gdone[i % 2].record(s)
+            outs.append(dC)
+        torch.cuda.synchronize()
+        worst = 0
+        for i, dC in enumerate(outs):
+            B = orc.uniform_f16((K, N), 300 + i)
+            for r in sorted(set([0, rows - 1, rows // 2])) if rows else []:
+                a = orc.uniform_f16((1, K), 1, (row0 + r) * K)
+                worst = max(worst, orc.check(dC[r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K,
+                                             1.0, 1.0)[0])
+        b_ok = True
+        for i in range(max(0, steps - 2), steps):
+            B = orc.uniform_f16((K, N), 300 + i)
+            b_ok = b_ok and bool(torch.equal(dB[i % 2].cpu().view(torch.int16),
+                                             torch.from_numpy(B.view(np.int16))))
+        status = b2g.device_status()
+        for p in plans:
+            b2g.chain_plan_destroy(p)
+        b2g.comm_destroy(comm)
+        out_q.put((rank, rows, worst, status, b_ok, None))
+    except Exception:
+        out_q.put((rank, -1, -1, -1, False, traceback.format_exc()))
+
+
+def gloo_p2p_fail_rank(rank, world, port, M, N, K, bad_rank, out_q):
+    """shard.sharded_gemm_k_p2p with one rank's arguments invalid (a C slab narrower than N, the
+    library's ldc < N) on the second of three calls: every rank must report the failure (the
+    bad rank ValueError, the others PeerFailedError with a NaN C slab), and the calls before
+    and after must be correct.  Reports (rank, [per-call outcome], max error of the good
+    calls)."""
+    try:
+        import torch
+        from oracle import orc
+        shard = _load_pkg("shard")
+        dist = _init_gloo(rank, world, port, 60)
+        A = orc.uniform_f16((M, K), 1)
+        B = orc.uniform_f16((K, N), 2)
+        ref = orc.gemm_f64(A, B)
+        k0, kr = shard.slab_rows(K, world, rank)
+        rows = M // world
+        outcomes, err = [], 0.0
+        for call in range(3):
+            width = N - 1 if (call == 1 and rank == bad_rank) else N
+            C_slab = torch.full((rows, width), float("nan"), dtype=torch.float64)
+            try:
+                row0, _ = shard.sharded_gemm_k_p2p(_f16(A[:, k0:k0 + kr]), _f16(B[k0:k0 + kr]),
+                                                   C_slab, M, N, K, gemm=_cpu_gemm)
+                outcomes.append("ok")
+                err = max(err, float(np.abs(C_slab.numpy() - ref[row0:row0 + rows]).max()))
+            except shard.PeerFailedError:
+                outcomes.append("peer_failed" if bool(torch.isnan(C_slab).all()) else "not_nan")
+            except ValueError:
+                outcomes.append("invalid")
+        dist.barrier()
+        dist.destroy_process_group()
+        out_q.put((rank, outcomes, err, None))
+    except Exception:
+        out_q.put((rank, [], -1.0, traceback.format_exc()))
+
+
+def nccl_p2p_rs_fail_rank(rank, world, uid_path, M, N, K, bad_rank, out_q):
+    """b2g_gemm_sharded_k_p2p on `world` GPUs, three calls; on the second one rank passes an
+    invalid ldc (< N).  That rank's call must return B2G_ERR_INVALID_ARG; every other rank's
+    call is accepted, but its reduction finds the bad rank's status word and must leave NaN in
+    C and the device error word at 7 (a peer's part failed).  The first and third calls must
+    be correct on sampled rows.  Reports (rank, [per-call outcome], failing elements of the
+    good calls, device status after the second call)."""
+    try:
+        import torch
+        from oracle import orc
+        b2g = _load_pkg("b2g")
+        torch.cuda.set_device(rank)
+        comm = _nccl_comm(b2g, rank, world, uid_path)
+        plan = b2g.rs_plan_create(comm, M, N)
+        k0, kr = b2g.slab_rows(K, world, rank)
+        rows = M // world
+        dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+        dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+        b2g.fill_uniform(dA, M * K, 1)
+        b2g.fill_uniform(dB, K * N, 2)
+        Ak, Bk = dA[:, k0:k0 + kr].contiguous(), dB[k0:k0 + kr].contiguous()
+        B = orc.uniform_f16((K, N), 2)
+        outcomes, bad, status1 = [], 0, None
+        for call in range(3):
+            dC = torch.full((rows, N), float("nan"), dtype=torch.float32, device="cuda")
+            ldc = N - 1 if (call == 1 and rank == bad_rank) else N
+            try:
+                b2g.gemm_sharded_k_p2p(plan, Ak, Bk, dC, M, N, K, lda=max(kr, 1), ldb=N, ldc=ldc)
+                rc = b2g.OK
+            except b2g.B2GError as e:
+                rc = e.code
+            torch.cuda.synchronize()
+            st = b2g.device_status()
+            if call == 1:
+                status1 = st
+                if rc != b2g.OK:
+                    outcomes.append("invalid" if rc == b2g.ERR_INVALID_ARG else "rc%d" % rc)
+                else:
+                    outcomes.append("peer_failed" if st == 7 and bool(torch.isnan(dC).all())
+                                    else "status%d" % st)
+            else:
+                outcomes.append("ok" if rc == b2g.OK and st == 0 else "rc%d/status%d" % (rc, st))
+                for r in sorted(set([0, rows - 1, rows // 2])):
+                    a = orc.uniform_f16((1, K), 1, (rank * rows + r) * K)
+                    bad += orc.check(dC[r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, 1.0, 1.0)[0]
+        b2g.rs_plan_destroy(plan)
+        b2g.comm_destroy(comm)
+        out_q.put((rank, outcomes, bad, status1, None))
+    except Exception:
+        out_q.put((rank, [], -1, -1, traceback.format_exc()))

@@ -22,6 +22,18 @@ def _ternary(torch, shape, seed):
     return torch.randint(-1, 2, shape, generator=g, device=DEV).to(torch.float16)
 
 
+def mismatches(torch, C, A, B, block=4096):
+    """Elements of C that differ from the FP64 product A.B, counted over row blocks (so the
+    FP64 reference of a 32768 x 32768 C never exists whole)."""
+    Bd = B.to(torch.float64)
+    bad = 0
+    for r0 in range(0, A.shape[0], block):
+        ref = torch.mm(A[r0:r0 + block].to(torch.float64), Bd)
+        bad += int((C[r0:r0 + block].to(torch.float64) != ref).sum().item())
+        del ref
+    return bad
+
+
 def _exact_gemm(b2g, torch, M, N, K, seed):
     A = _ternary(torch, (M, K), seed)
     B = _ternary(torch, (K, N), seed + 1)
@@ -29,8 +41,7 @@ def _exact_gemm(b2g, torch, M, N, K, seed):
     b2g.gemm(A, B, C, M, N, K)
     torch.cuda.synchronize()
     assert b2g.device_status() == 0
-    ref = torch.mm(A.to(torch.float64), B.to(torch.float64))
-    return int((C.to(torch.float64) != ref).sum().item())
+    return mismatches(torch, C, A, B)
 
 
 @pytest.mark.parametrize("M,N,K", [(1024, 1024, 1024), (8192, 8192, 8192), (16384, 16384, 4096),
@@ -39,6 +50,14 @@ def _exact_gemm(b2g, torch, M, N, K, seed):
 def test_gemm_full_size_exact(b2g, cuda, M, N, K):
     """BASELINE configs[0], [1] and the large configs[3] shapes, every element exact."""
     assert _exact_gemm(b2g, cuda, M, N, K, seed=M + N + K) == 0
+
+
+def test_gemm_32768_cubed_single_gpu_exact(b2g, cuda):
+    """BASELINE configs[4]'s whole problem, 32768^3 (C is 4 GiB: 64-bit offsets in every
+    address), on one GPU; every element exact."""
+    torch = cuda
+    assert _exact_gemm(b2g, torch, 32768, 32768, 32768, seed=11) == 0
+    torch.cuda.empty_cache()
 
 
 @pytest.mark.parametrize("cluster_fixup", [1, 0], ids=["cluster_fixup", "global_fixup"])

@@ -167,10 +167,22 @@ def test_gemm_timeout_reports_error(b2g, cuda, orc):
 
 
 def test_gemm_c_larger_than_4gib(b2g, cuda, orc):
-    """32768 x 32768 x 1024: C is 4 GiB (64-bit offsets everywhere); rows near the end checked."""
+    """32768 x 32768 x 1024: C is 4 GiB (64-bit offsets everywhere).  Ternary operands first,
+    where fp32 accumulation is exact in any order, so every element of C must equal the FP64
+    product; then seeded U[-1,1] operands with rows near the start, middle and end checked
+    against the FP64 oracle."""
     torch = cuda
+    from test_fullsize_exact_gpu import _ternary, mismatches
     M = N = 32768
     K = 1024
+    tA = _ternary(torch, (M, K), 41)
+    tB = _ternary(torch, (K, N), 42)
+    dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    b2g.gemm(tA, tB, dC, M, N, K)
+    torch.cuda.synchronize()
+    assert b2g.device_status() == 0
+    assert mismatches(torch, dC, tA, tB) == 0
+    del tA, tB
     dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
     dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
     dC = torch.empty((M, N), dtype=torch.float32, device="cuda")

@@ -125,3 +125,26 @@ def test_gloo_k_split_peer_schedule(world, M, N, K):
                                                 (3, 130, 30, 20, 4)])
 def test_gloo_n_slabs_all_gather(world, M, N, K, panels):
     _run_tp("n", world, M, N, K, panels)
+
+
+@pytest.mark.parametrize("world,bad_rank", [(2, 1), (3, 0), (3, 2)])
+def test_gloo_k_split_peer_failure_reported_everywhere(world, bad_rank):
+    """One rank's invalid arguments on the second of three peer-memory K-split calls: that rank
+    reports an invalid argument, every other rank a failed peer (C slab NaN), and the calls
+    before and after are correct on every rank."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    M, N, K = 12 * world, 20, 70
+    procs = [ctx.Process(target=shard_worker.gloo_p2p_fail_rank,
+                         args=(r, world, port, M, N, K, bad_rank, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for rank, outcomes, err, tb in res:
+        assert tb is None, tb
+        want = "invalid" if rank == bad_rank else "peer_failed"
+        assert outcomes == ["ok", want, "ok"], (rank, outcomes)
+        assert 0 <= err < 1e-9, (rank, err)

@@ -222,3 +222,64 @@ def test_n_chain_multi_rank(b2g, cuda, world, M, N, K, panels):
         assert tb is None, tb
         assert worst == 0 and status == 0 and a_ok, (rank, nr, worst, status, a_ok)
     assert sum(r[1] for r in res) == N
+
+
+def test_chain_broadcast_single_rank(b2g, cuda):
+    with tempfile.TemporaryDirectory() as d:
+        q = _ListQueue()
+        shard_worker.nccl_chain_bcast_rank(0, 1, os.path.join(d, "id"), 512, 768, 1024, 3, 3, q)
+    rank, rows, worst, status, b_ok, tb = q[0]
+    assert tb is None, tb
+    assert worst == 0 and status == 0 and b_ok
+
+
+@pytest.mark.parametrize("world,M,N,K,panels,steps", [(2, 2048, 1536, 2048, 5, 4),
+                                                      (2, 600, 520, 201, 3, 3),
+                                                      (4, 4096, 1024, 4096, 8, 4),
+                                                      (8, 8192, 2048, 4096, 8, 4)])
+def test_chain_broadcast_multi_rank(b2g, cuda, world, M, N, K, panels, steps):
+    """Double-buffered chain broadcast (bench.py's multi-GPU step): the broadcast of step i+1's
+    B overlaps step i's slab GEMM; every step's rows checked, the B buffers bit-exact.
+    K*N*2 = 209040 bytes in the second case is not a multiple of the 1 KiB panel unit."""
+    if cuda.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=shard_worker.nccl_chain_bcast_rank,
+                             args=(r, world, os.path.join(d, "id"), M, N, K, panels, steps, q))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        res = sorted(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=120)
+    for rank, rows, worst, status, b_ok, tb in res:
+        assert tb is None, tb
+        assert worst == 0 and status == 0 and b_ok, (rank, rows, worst, status, b_ok)
+    assert sum(r[1] for r in res) == M
+
+
+@pytest.mark.parametrize("world,bad_rank", [(2, 1), (4, 2)])
+def test_p2p_rs_peer_failure_reported_everywhere(b2g, cuda, world, bad_rank):
+    """Peer-memory K-split: one rank passes ldc < N on the second of three calls.  That rank
+    gets B2G_ERR_INVALID_ARG; the others' reductions see its status word, fill C with NaN and
+    set the device error word to 7; the first and third calls are correct on every rank."""
+    if cuda.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=shard_worker.nccl_p2p_rs_fail_rank,
+                             args=(r, world, os.path.join(d, "id"), 512 * world, 768, 1024,
+                                   bad_rank, q)) for r in range(world)]
+        for p in procs:
+            p.start()
+        res = sorted(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=120)
+    for rank, outcomes, bad, status1, tb in res:
+        assert tb is None, tb
+        want = "invalid" if rank == bad_rank else "peer_failed"
+        assert outcomes == ["ok", want, "ok"], (rank, outcomes, status1)
+        assert bad == 0, (rank, bad)

@@ -202,3 +202,35 @@ def test_cluster_fixup_matches_global_fixup(b2g, cuda, orc, tn, splits, MNK):
         outs.append(dC[:, :N].clone())
     assert torch.equal(outs[0], outs[1])
     assert_close(orc, outs[0].cpu().numpy(), orc.gemm_f64(A, B), K)
+
+
+def test_split_k_counter_ring_wraps_across_streams(b2g, cuda, orc):
+    """Split calls on two streams share the per-device counter ring.  With the ring cut to 512
+    slots (8 calls per lap) 64 calls alternate between the streams, so the ring wraps eight
+    times while kernels of the other stream may still hold counters; every wrap first waits
+    for the other stream's last user.  Every result must equal the single-stream result bit
+    for bit, and no bounded wait may run out."""
+    torch = cuda
+    b2g.device_status(clear=True)
+    M, N, K = 256, 1024, 4096
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+    dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+    b2g.fill_uniform(dA, M * K, 93)
+    b2g.fill_uniform(dB, K * N, 94)
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    with options(b2g, cta_group=1, tile_n=128, split_k=4, cluster_fixup=0, ring_slots=512):
+        ref = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        b2g.gemm(dA, dB, ref, M, N, K)
+        torch.cuda.synchronize()
+        outs = [torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+                for _ in range(64)]
+        torch.cuda.synchronize()
+        for i, out in enumerate(outs):
+            b2g.gemm(dA, dB, out, M, N, K, stream=streams[i % 2].cuda_stream)
+        torch.cuda.synchronize()
+    assert b2g.device_status() == 0
+    for i, out in enumerate(outs):
+        assert torch.equal(out, ref), i
+    A = orc.uniform_f16((M, K), 93)
+    B = orc.uniform_f16((K, N), 94)
+    assert_close(orc, ref.cpu().numpy(), orc.gemm_f64(A, B), K)
