@@ -147,60 +147,82 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sms)}
 
 
-def cpu_baseline(seconds, threads=None):
-    """The oracle's blocked multithreaded GEMM (GEMM_Naive arithmetic, bit-exact) on a row
-    sample of the 8192^3 problem; returns TFLOP/s, rows done, seconds, threads."""
-    from oracle import orc
-    A = orc.uniform_f16((M_PER_GPU, K_DIM), 1)
-    B = orc.uniform_f16((K_DIM, N_DIM), 2)
-    thr = threads or orc.nthreads()
-    t0 = time.perf_counter()
-    Bf = orc.widen_b(B, threads=thr)
-    t_widen = time.perf_counter() - t0
-    rows_done, t_rows = 0, 0.0
-    chunk = 48
-    while t_rows < seconds and rows_done + chunk <= M_PER_GPU:
+CPU_CHUNK_ROWS = 384  # rows of the 8192^3 problem per timed CPU chunk (both CPU legs)
+
+
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+class CpuGemm:
+    """The oracle's blocked multithreaded port of GEMM_Naive (bit-exact) on the 8192^3 problem,
+    timed in chunks of CPU_CHUNK_ROWS rows that cycle through the matrix.  Both CPU legs of the
+    bench (the cpu_baseline key and --impl reference) use this one sample rule; the one-time
+    widening of B to fp32 is charged pro rata to the rows computed."""
+
+    def __init__(self, threads=None):
+        from oracle import orc
+        self.orc = orc
+        self.A = orc.uniform_f16((M_PER_GPU, K_DIM), 1)
+        self.B = orc.uniform_f16((K_DIM, N_DIM), 2)
+        self.thr = threads or orc.nthreads()
         t0 = time.perf_counter()
-        orc.gemm_f32_blocked(A, B, rows=(rows_done, rows_done + chunk), threads=thr, Bf=Bf)
+        self.Bf = orc.widen_b(self.B, threads=self.thr)
+        self.t_widen = time.perf_counter() - t0
+        self.r0 = 0
+
+    def chunk(self):
+        """One chunk of rows; returns its charged seconds."""
+        r0 = self.r0
+        t0 = time.perf_counter()
+        self.orc.gemm_f32_blocked(self.A, self.B, rows=(r0, r0 + CPU_CHUNK_ROWS), threads=self.thr,
+                                  Bf=self.Bf)
         dt = time.perf_counter() - t0
-        t_rows += dt
-        rows_done += chunk
-        if dt < 0.5:
-            chunk = min(chunk * 2, 768)
-    # the one-time widening of B is charged pro rata to the rows computed
-    t = t_rows + t_widen * rows_done / M_PER_GPU
-    flops = 2.0 * rows_done * N_DIM * K_DIM
-    return flops / t / 1e12, rows_done, t, thr
+        self.r0 = (r0 + CPU_CHUNK_ROWS) % (M_PER_GPU - CPU_CHUNK_ROWS + 1)
+        return dt + self.t_widen * CPU_CHUNK_ROWS / M_PER_GPU
+
+    @staticmethod
+    def tflops(rows, secs):
+        return 2.0 * rows * N_DIM * K_DIM / secs / 1e12
+
+
+def cpu_baseline(seconds, threads=None):
+    """The CPU baseline of the default line: chunks of the 8192^3 problem for about `seconds`
+    (after one untimed chunk); returns TFLOP/s, rows done, seconds, threads."""
+    g = CpuGemm(threads)
+    g.chunk()
+    rows, t = 0, 0.0
+    while t < seconds or rows == 0:
+        t += g.chunk()
+        rows += CPU_CHUNK_ROWS
+    return g.tflops(rows, t), rows, t, g.thr
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    from oracle import orc
-    thr = orc.nthreads()
-    A = orc.uniform_f16((M_PER_GPU, K_DIM), 1)
-    B = orc.uniform_f16((K_DIM, N_DIM), 2)
-    t0 = time.perf_counter()
-    Bf = orc.widen_b(B, threads=thr)
-    t_widen = time.perf_counter() - t0
-    # size each step so the whole run takes about a minute
-    t0 = time.perf_counter()
-    orc.gemm_f32_blocked(A, B, rows=(0, 48), threads=thr, Bf=Bf)
-    per_row = (time.perf_counter() - t0) / 48
+    g = CpuGemm()
+    thr = g.thr
+    # size each step (a whole number of chunks) so the whole run takes about a minute
+    per_chunk = g.chunk()
     step_s = 60.0 / max(1, args.steps + args.warmup)
-    rows = int(max(6, min(M_PER_GPU, step_s / per_row)) // 6 * 6)
-    r0 = 0
+    chunks = max(1, int(round(step_s / per_chunk)))
+    rows = chunks * CPU_CHUNK_ROWS
     for _ in range(args.warmup):
-        orc.gemm_f32_blocked(A, B, rows=(r0, r0 + rows), threads=thr, Bf=Bf)
+        for _ in range(chunks):
+            g.chunk()
     times = []
-    for s in range(args.steps):
-        r0 = (s * rows) % max(1, M_PER_GPU - rows)
-        t0 = time.perf_counter()
-        orc.gemm_f32_blocked(A, B, rows=(r0, r0 + rows), threads=thr, Bf=Bf)
-        times.append(time.perf_counter() - t0 + t_widen * rows / M_PER_GPU)
+    for _ in range(args.steps):
+        times.append(sum(g.chunk() for _ in range(chunks)))
     tot = sum(times)
-    val = 2.0 * rows * N_DIM * K_DIM * args.steps / tot / 1e12
+    val = g.tflops(rows * args.steps, tot)
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     line = {
         "impl": "reference",
@@ -219,14 +241,50 @@ def run_reference(args):
         "config": {"workload": "gemm 8192x8192x8192 row-major fp16->fp32 (BASELINE configs[1])",
                    "sample": "%d rows x 8192 x 8192 per step" % rows, "world_size": ws},
         "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": thr, "kind": "port",
-                         "sample": "%d of 8192 rows per step; blocked AVX2 port of GEMM_Naive "
-                                   "(mmm.cpp:52-62), bit-exact; B widening charged pro rata" % rows},
+                         "cpu_model": cpu_model(),
+                         "sample": "%d rows per step (chunks of %d rows cycling through the "
+                                   "8192) of the 8192^3 GEMM; blocked AVX2 port of GEMM_Naive "
+                                   "(mmm.cpp:52-62), bit-exact; B widening charged pro rata"
+                                   % (rows, CPU_CHUNK_ROWS)},
         "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference is HIP/rocBLAS for AMD gfx12 and cannot run on this box; this "
                 "arm is the CPU port of its arithmetic",
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+ALL_CONFIGS = [
+    ("configs[0]", ["--shape", "1024,1024,1024"]),
+    ("configs[1]", ["--shape", "8192,8192,8192"]),
+    ("configs[2]", ["--workload", "contraction5d"]),
+    ("configs[3]", ["--shape", "16384,16384,4096"]),
+    ("configs[3]", ["--shape", "8192,28672,8192"]),
+    ("configs[3]", ["--shape", "128,8192,8192"]),
+    ("configs[4] on one GPU", ["--shape", "32768,32768,32768"]),
+]
+
+
+def run_all_configs(args):
+    """One kernel-loop line per BASELINE config on one GPU, each from its own process (so every
+    config starts from a fresh memory pool), with clocks and cuBLAS side by side.  32768^3 runs
+    at most 20 steps (61 ms each)."""
+    rc = 0
+    for label, extra in ALL_CONFIGS:
+        steps = args.steps if "32768" not in extra[-1] else min(args.steps, 20)
+        cmd = [sys.executable, os.path.abspath(__file__)] + extra + [
+            "--steps", str(steps), "--warmup", str(args.warmup)]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        lines = [l for l in res.stdout.splitlines() if l.startswith("{")]
+        if res.returncode != 0 or not lines:
+            rc = res.returncode or 1
+            print(json.dumps({"baseline_config": label, "args": extra, "rc": res.returncode,
+                              "stderr_tail": res.stderr[-400:]}), flush=True)
+            continue
+        line = json.loads(lines[-1])
+        line["baseline_config"] = label
+        print(json.dumps(line), flush=True)
+    return rc
 
 
 def main():
@@ -266,10 +324,17 @@ def main():
     ap.add_argument("--kernel-only", action="store_true",
                     help="device-resident GEMM steps only (no e2e, CPU baseline or clock "
                          "sampling): the command profiled with ncu")
+    ap.add_argument("--all-configs", action="store_true",
+                    help="one JSON line per BASELINE config on one GPU (1024^3, 8192^3, the "
+                         "configs[2] contraction, the three configs[3] shapes, 32768^3), each "
+                         "with clocks and cuBLAS side by side")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.all_configs:
+        return run_all_configs(args)
+    args.sample_clocks = not args.kernel_only
 
     import torch
     import torch.distributed as dist
@@ -383,7 +448,7 @@ def main():
     # consecutive launches overlap as they do for a user (programmatic dependent launch).
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local) if not args.kernel_only else None
+    sampler = ClockSampler(local) if args.sample_clocks else None
     if ws > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -455,7 +520,8 @@ def main():
     cublas = None
     if not args.kernel_only:
         e2e = e2e_run(torch, b2g, dev, M, N, K, rank, ws, args.e2e_steps, dist if ws > 1 else None)
-    if rank == 0 and ws == 1 and not args.no_cublas and dt == 0 and not epilogue and (args.shape or not args.kernel_only):
+    if (rank == 0 and ws == 1 and not args.no_cublas and dt == 0 and not epilogue and
+            (args.shape or contraction or not args.kernel_only)):
         cublas = cublas_side_by_side(torch, dA, dB, dC, local, min(args.steps, 1000))
 
     peaks, peaks_src = measured_peaks()
@@ -500,9 +566,10 @@ def main():
     if rank == 0 and ws == 1 and not args.no_cpu_baseline and not args.kernel_only:
         v, rows, secs, thr = cpu_baseline(args.cpu_seconds)
         cpu = {"value": v, "unit": "TFLOP/s", "cores": thr, "kind": "port",
-               "sample": "%d of 8192 rows of the 8192^3 GEMM (%.1f s); blocked AVX2 port of "
-                         "GEMM_Naive (mmm.cpp:52-62), bit-exact; B widening charged pro rata"
-                         % (rows, secs)}
+               "cpu_model": cpu_model(),
+               "sample": "%d rows of the 8192^3 GEMM in chunks of %d rows (%.1f s); blocked "
+                         "AVX2 port of GEMM_Naive (mmm.cpp:52-62), bit-exact; B widening charged "
+                         "pro rata" % (rows, CPU_CHUNK_ROWS, secs)}
     if ws > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -826,6 +893,7 @@ def e2e_run(torch, b2g, dev, M, N, K, rank, ws, steps, dist):
 
     run(2)
     torch.cuda.synchronize()
+    link = pcie_bandwidth(torch, dev, hA, hB, hC[0], bufs[0])
     if dist is not None:
         dist.barrier()
     t0 = torch.cuda.Event(enable_timing=True)
@@ -844,10 +912,55 @@ def e2e_run(torch, b2g, dev, M, N, K, rank, ws, steps, dist):
     # spot-check the result that came back (first row of the last step)
     bad = row_out_of_tolerance(torch, hC[(steps - 1) & 1][:1], gA[:1], gB, K)
     del gA, gB
+    bi, bo = (M * K + K * N) * 2, M * N * 4
+    # the copy bound of a step: its uploads and downloads at the pinned-copy bandwidths measured
+    # above, the two directions overlapping (the GEMM runs under them)
+    target_ms = max(bi / link["h2d_gbs"], bo / link["d2h_gbs"],
+                    (bi + bo) / link["bidir_gbs"]) / 1e6
+    roof = dict(link, bound="pcie", target_ms_per_step=target_ms,
+                frac=target_ms / (ms / steps))
     return {"value": 2.0 * M * N * K * ws * steps / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-            "h2d_bytes_per_step": (M * K + K * N) * 2, "d2h_bytes_per_step": M * N * 4,
+            "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
             "steps": steps, "ms_per_step": ms / steps, "row0_out_of_tolerance": bad,
-            "pipeline": "2 buffer sets, H2D / compute / D2H streams"}
+            "pipeline": "2 buffer sets, H2D / compute / D2H streams", "roofline": roof}
+
+
+def pcie_bandwidth(torch, dev, hA, hB, hC, dbuf):
+    """Pinned host <-> device copy bandwidth of this GPU (GB/s, best of 3): uploads of A and B,
+    a download of C, and both directions at once on two streams."""
+    dA, dB, dC = dbuf
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def timed(fn):
+        best = None
+        for _ in range(3):
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s1)
+            s2.wait_event(e0)
+            fn()
+            s1.wait_stream(s2)
+            e1.record(s1)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            best = ms if best is None else min(best, ms)
+        return best
+
+    def up():
+        with torch.cuda.stream(s1):
+            dA.copy_(hA, non_blocking=True)
+            dB.copy_(hB, non_blocking=True)
+
+    def down():
+        with torch.cuda.stream(s2):
+            hC.copy_(dC, non_blocking=True)
+
+    bi = hA.numel() * hA.element_size() + hB.numel() * hB.element_size()
+    bo = hC.numel() * hC.element_size()
+    t_up, t_down = timed(up), timed(down)
+    t_both = timed(lambda: (up(), down()))
+    return {"h2d_gbs": bi / (t_up * 1e6), "d2h_gbs": bo / (t_down * 1e6),
+            "bidir_gbs": (bi + bo) / (t_both * 1e6)}
 
 
 if __name__ == "__main__":

@@ -21,7 +21,8 @@
  *     (b2g_last_path() tells which).
  *   - Numerics: fp32 accumulation of exact fp16 products.  Results agree with an FP64
  *     reference within |err| <= 1e-3*sqrt(K)*max|a|*max|b| + 1e-3*|ref|.
- *   - Thread-safe; calls from several host threads may run concurrently.
+ *   - Thread-safe; calls from several host threads may run concurrently (except the
+ *     no-alloc entry point, whose calls share one scratch array).
  */
 #ifndef B2G_GEMM_H
 #define B2G_GEMM_H
@@ -312,10 +313,29 @@ int b2g_slab_rows(int64_t M, int world, int rank, int64_t* row0, int64_t* rows);
 
 /* NCCL communicator helpers for callers without their own NCCL: a 128-byte unique id made on
  * one rank and shared with the others out of band, then one b2g_comm_init per rank (with that
- * rank's device current).  No reference counterpart. */
+ * rank's device current).  The communicator is non-blocking (option "comm_nonblocking"): its
+ * set-up and every NCCL call the library makes on it are polled for at most the option
+ * "comm_timeout_ms" (default 60000), after which the communicator is aborted
+ * (ncclCommAbort) and the call returns B2G_ERR_TIMEOUT.  b2g_comm_destroy flushes this rank's
+ * operations (bounded the same way) and frees the communicator.  No reference counterpart
+ * (the reference is single-GPU; its HIP_CHECK exits the process, mmm.cpp:33-39). */
 int b2g_comm_unique_id(void* id_out);
 int b2g_comm_init(void** comm, int world, int rank, const void* id);
 int b2g_comm_destroy(void* comm);
+
+/*
+ * Liveness check between steps: a one-word all-reduce over `comm` on `stream` (NULL: an
+ * internal stream), waited for on the host for at most timeout_ms.  Returns B2G_OK when every
+ * rank answered.  If a rank has gone (its process exited or stopped calling), the wait runs
+ * out, the communicator is aborted (its kernels return) and the call returns B2G_ERR_TIMEOUT.
+ * From then on every entry point given that communicator, or a chain or reduce-scatter plan
+ * built on it, returns B2G_ERR_NCCL without queueing any work, and b2g_chain_plan_destroy /
+ * b2g_rs_plan_destroy only free this rank's memory.  Every rank calls it at the same point of
+ * its step sequence.  The library's stream-memory-operation waits (chain and peer-memory
+ * plans) have no bound of their own: a caller that may lose a rank checks between steps, so
+ * that no work is queued that waits for the lost rank.  No reference counterpart.
+ */
+int b2g_comm_check(void* comm, int64_t timeout_ms, void* stream);
 
 /* Message for the calling thread's last failed call ("" if none).  Replaces the messages the
  * reference prints before exiting from HIP_CHECK / ROCBLAS_CHECK (mmm.cpp:33-49). */
@@ -352,6 +372,8 @@ int b2g_device_status(int clear);
  *                  partials go through a global workspace
  *   "pdl"          1 (default) = tensor-core launches use programmatic dependent launch (the
  *                  kernel's set-up overlaps the previous kernel in the stream); 0 = plain launch
+ *   "comm_timeout_ms" bound of every NCCL wait of the multi-GPU entry points (default 60000)
+ *   "comm_nonblocking" 1 (default) = b2g_comm_init makes a non-blocking NCCL communicator
  *   "ring_slots"   split-K arrival counters usable in the per-device ring (default and
  *                  maximum 1048576, a multiple of 64, at least 512): a small ring makes tests
  *                  wrap it often

@@ -19,7 +19,10 @@ wrappers below run GEMM_Naive over its documented launch grid (16x16 blocks,
 README.md:103).  The translation unit is fed to g++ on stdin: no reference source is
 written anywhere; only the shared object lands in oracle/_ref/.
 
-    python oracle/build_ref.py
+    python oracle/build_ref.py [--reference DIR] [--force]
+
+The reference checkout is the directory given by --reference, else B2G_REFERENCE_DIR, else a
+directory named `reference` beside this repository.
 """
 import os
 import shutil
@@ -27,7 +30,6 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("B2G_REFERENCE_DIR", "/root/reference")
 OUT_DIR = os.path.join(HERE, "_ref")
 LIB = os.path.join(OUT_DIR, "libref.so")
 
@@ -82,13 +84,25 @@ extern "C" void ref_pack_g(const uint16_t* G_, uint16_t* hA_, int rt_, int nt_, 
 """
 
 
-def reference_available():
-    return all(os.path.exists(os.path.join(REF, f)) for f in ("mmm.cpp", "mmmTensor.cpp"))
+def reference_dir(given=None):
+    """The reference checkout: `given`, else B2G_REFERENCE_DIR, else `reference` beside the
+    repository."""
+    if given:
+        return given
+    env = os.environ.get("B2G_REFERENCE_DIR")
+    if env:
+        return env
+    return os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 
 
-def _piece(name):
+def reference_available(ref=None):
+    ref = reference_dir(ref)
+    return all(os.path.exists(os.path.join(ref, f)) for f in ("mmm.cpp", "mmmTensor.cpp"))
+
+
+def _piece(name, ref):
     fname, lo, hi, head = PIECES[name]
-    with open(os.path.join(REF, fname)) as f:
+    with open(os.path.join(ref, fname)) as f:
         lines = f.read().splitlines()
     text = lines[lo - 1:hi]
     if not text or not text[0].strip().startswith(head):
@@ -100,20 +114,23 @@ def _piece(name):
     return "#line %d \"%s\"\n%s\n" % (lo, fname, body)
 
 
-def translation_unit():
-    return (PRELUDE + _piece("gemm_naive") + _piece("validate_gemm") + _piece("validate_tensor")
-            + WRAPPERS + PACK_HEAD + _piece("pack_g") + "}\n")
+def translation_unit(ref=None):
+    ref = reference_dir(ref)
+    return (PRELUDE + _piece("gemm_naive", ref) + _piece("validate_gemm", ref)
+            + _piece("validate_tensor", ref) + WRAPPERS + PACK_HEAD + _piece("pack_g", ref)
+            + "}\n")
 
 
-def build(force=False):
-    if not reference_available():
-        raise RuntimeError("reference sources not found under %s" % REF)
+def build(force=False, ref=None):
+    ref = reference_dir(ref)
+    if not reference_available(ref):
+        raise RuntimeError("reference sources not found under %s" % ref)
     if not force and os.path.exists(LIB):
         return LIB
     os.makedirs(OUT_DIR, exist_ok=True)
     cxx = os.environ.get("CXX") or shutil.which("g++") or "c++"
     cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-x", "c++", "-", "-o", LIB + ".tmp"]
-    res = subprocess.run(cmd, input=translation_unit(), capture_output=True, text=True)
+    res = subprocess.run(cmd, input=translation_unit(ref), capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
         raise RuntimeError("compiling the reference pieces failed")
@@ -122,4 +139,9 @@ def build(force=False):
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv))
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=None, help="the reference checkout")
+    ap.add_argument("--force", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force, ref=a.reference))

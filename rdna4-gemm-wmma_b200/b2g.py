@@ -135,6 +135,8 @@ def load(path=None):
     L.b2g_comm_init.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int, vp]
     L.b2g_comm_destroy.restype = ctypes.c_int
     L.b2g_comm_destroy.argtypes = [vp]
+    L.b2g_comm_check.restype = ctypes.c_int
+    L.b2g_comm_check.argtypes = [vp, i64, vp]
     if path is None:
         _lib = L
     return L
@@ -279,6 +281,12 @@ def comm_init(world, rank, uid):
 
 def comm_destroy(comm):
     _check(load().b2g_comm_destroy(comm))
+
+
+def comm_check(comm, timeout_ms=5000, stream=None):
+    """Liveness check between steps: B2G_OK if every rank answered within timeout_ms, else the
+    communicator is aborted and B2GError (ERR_TIMEOUT) is raised."""
+    _check(load().b2g_comm_check(comm, int(timeout_ms), None if stream is None else _stream(stream)))
 
 
 def gemm_sharded(A_slab, B, C_slab, M, N, K, comm, root=0, k_panels=4, lda=None, ldb=None,

@@ -68,6 +68,10 @@ static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream seri
 // count launches (b2g_get_option("launches")).
 static std::atomic<int64_t> g_launches{0};
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+static std::atomic<int64_t> opt_comm_timeout_ms{60000};  // bound of the library's NCCL waits
+static std::atomic<int64_t> opt_comm_nonblocking{1};    // b2g_comm_init: non-blocking NCCL
+int64_t comm_timeout_ms() { return opt_comm_timeout_ms.load(); }
+bool comm_nonblocking() { return opt_comm_nonblocking.load() != 0; }
 static std::atomic<int64_t> opt_cluster_fixup{1};  // split-K fix-up through distributed smem
 static std::atomic<int64_t> opt_serial_fixup{0};  // 1 = always the last-arriver fix-up
 
@@ -1271,6 +1275,11 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_split_k = value;
   } else if (!strcmp(key, "store_hint")) {
     opt_store_hint = value ? 1 : 0;
+  } else if (!strcmp(key, "comm_timeout_ms")) {
+    if (value <= 0) return B2G_ERR_INVALID_ARG;
+    opt_comm_timeout_ms = value;
+  } else if (!strcmp(key, "comm_nonblocking")) {
+    opt_comm_nonblocking = value ? 1 : 0;
   } else if (!strcmp(key, "ring_slots")) {
     if (value < 512 || value > (int64_t)kCounterSlots || value % 64) return B2G_ERR_INVALID_ARG;
     opt_ring_slots = value;
@@ -1300,6 +1309,8 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "cluster_fixup")) return opt_cluster_fixup;
   if (!strcmp(key, "serial_fixup")) return opt_serial_fixup;
   if (!strcmp(key, "ring_slots")) return opt_ring_slots;
+  if (!strcmp(key, "comm_timeout_ms")) return opt_comm_timeout_ms;
+  if (!strcmp(key, "comm_nonblocking")) return opt_comm_nonblocking;
   return -1;
 }
 

@@ -16,10 +16,13 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <set>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/b2g_gemm.h"
@@ -54,6 +57,11 @@ struct NcclApi {
   decltype(&ncclCommDestroy) destroy = nullptr;
   decltype(&ncclCommCount) count = nullptr;
   decltype(&ncclCommUserRank) user_rank = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclCommInitRankConfig) init_rank_config = nullptr;
+  decltype(&ncclCommGetAsyncError) async_error = nullptr;
+  decltype(&ncclCommAbort) abort = nullptr;
+  decltype(&ncclCommFinalize) finalize = nullptr;
   std::string error;
 };
 
@@ -83,9 +91,16 @@ NcclApi* nccl() {
     api.destroy = reinterpret_cast<decltype(api.destroy)>(dlsym(h, "ncclCommDestroy"));
     api.count = reinterpret_cast<decltype(api.count)>(dlsym(h, "ncclCommCount"));
     api.user_rank = reinterpret_cast<decltype(api.user_rank)>(dlsym(h, "ncclCommUserRank"));
+    api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+    api.init_rank_config =
+        reinterpret_cast<decltype(api.init_rank_config)>(dlsym(h, "ncclCommInitRankConfig"));
+    api.async_error = reinterpret_cast<decltype(api.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
+    api.abort = reinterpret_cast<decltype(api.abort)>(dlsym(h, "ncclCommAbort"));
+    api.finalize = reinterpret_cast<decltype(api.finalize)>(dlsym(h, "ncclCommFinalize"));
     if (!api.bcast || !api.errstr || !api.unique_id || !api.init_rank || !api.destroy ||
         !api.count || !api.user_rank || !api.reduce_scatter || !api.all_gather ||
-        !api.group_start || !api.group_end)
+        !api.group_start || !api.group_end || !api.all_reduce || !api.init_rank_config ||
+        !api.async_error || !api.abort || !api.finalize)
       api.error = "libnccl.so.2 lacks an expected symbol";
   });
   return api.error.empty() ? &api : nullptr;
@@ -95,6 +110,83 @@ int nccl_fail(ncclResult_t r, const char* what) {
   NcclApi* n = nccl();
   return sfail(B2G_ERR_NCCL,
                std::string(what) + ": " + (n ? n->errstr(r) : "NCCL unavailable"));
+}
+
+// Communicators this library aborted (after a bounded wait ran out).  Their handles are freed
+// by NCCL; every entry point given one, or a plan built on one, refuses with B2G_ERR_NCCL
+// instead of queueing work that could wait for a peer forever.
+std::mutex g_abort_mu;
+std::set<void*> g_aborted;
+
+bool comm_aborted(void* comm) {
+  std::lock_guard<std::mutex> lk(g_abort_mu);
+  return g_aborted.count(comm) != 0;
+}
+
+int refuse_aborted() {
+  return sfail(B2G_ERR_NCCL, "the communicator was aborted after a peer stopped answering");
+}
+
+// Abort `c` (its kernels in flight return) and remember that it is gone.
+void abort_comm(ncclComm_t c) {
+  NcclApi* n = nccl();
+  if (n) n->abort(c);
+  std::lock_guard<std::mutex> lk(g_abort_mu);
+  g_aborted.insert(c);
+}
+
+double now_ms() {
+  return std::chrono::duration<double, std::milli>(
+             std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+// Result of an NCCL call on `c`.  A non-blocking communicator returns ncclInProgress while the
+// call (or the communicator's set-up) completes in the background: poll its state, for at
+// most the library's communicator timeout; if that runs out the communicator is aborted and
+// the call reports B2G_ERR_TIMEOUT.
+int nccl_settle(ncclComm_t c, ncclResult_t r, const char* what) {
+  NcclApi* n = nccl();
+  if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
+  if (r == ncclInProgress) {
+    const double deadline = now_ms() + (double)b2g::comm_timeout_ms();
+    ncclResult_t st = ncclInProgress;
+    while (true) {
+      if (n->async_error(c, &st) != ncclSuccess) st = ncclSystemError;
+      if (st != ncclInProgress) break;
+      if (now_ms() > deadline) {
+        abort_comm(c);
+        return sfail(B2G_ERR_TIMEOUT, std::string(what) +
+                                          ": did not complete within the communicator timeout; "
+                                          "the communicator was aborted");
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    r = st;
+  }
+  if (r != ncclSuccess) return nccl_fail(r, what);
+  return B2G_OK;
+}
+
+// Wait (bounded by the communicator timeout) for `s`, whose last work is an NCCL collective on
+// `c`.  If the limit runs out the communicator is aborted (its kernels return) and the wait
+// reports B2G_ERR_TIMEOUT.
+int nccl_sync(ncclComm_t c, cudaStream_t s, const char* what) {
+  const double deadline = now_ms() + (double)b2g::comm_timeout_ms();
+  while (true) {
+    const cudaError_t q = cudaStreamQuery(s);
+    if (q == cudaSuccess) return B2G_OK;
+    if (q != cudaErrorNotReady)
+      return sfail(B2G_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(q));
+    if (now_ms() > deadline) break;
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+  abort_comm(c);
+  const double drain = now_ms() + 10000.0;
+  while (cudaStreamQuery(s) == cudaErrorNotReady && now_ms() < drain)
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  return sfail(B2G_ERR_TIMEOUT, std::string(what) + ": a peer did not answer within the "
+                                                    "communicator timeout; the communicator was "
+                                                    "aborted");
 }
 
 // One non-blocking stream per device for the broadcasts.
@@ -137,19 +229,90 @@ extern "C" int b2g_comm_init(void** comm, int world, int rank, const void* id) {
   ncclUniqueId uid;
   std::memcpy(&uid, id, sizeof(uid));
   ncclComm_t c = nullptr;
-  ncclResult_t r = n->init_rank(&c, world, uid, rank);
-  if (r != ncclSuccess) return nccl_fail(r, "ncclCommInitRank");
+  // Non-blocking (the default): the set-up runs in the background and is polled here for at
+  // most the communicator timeout, so a rank that never joins ends in an error, not a hang.
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = b2g::comm_nonblocking() ? 0 : 1;
+  ncclResult_t r = n->init_rank_config(&c, world, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclCommInitRankConfig");
+  {
+    std::lock_guard<std::mutex> lk(g_abort_mu);
+    g_aborted.erase(c);  // a new communicator may reuse a freed handle's address
+  }
+  const int rc = nccl_settle(c, r, "ncclCommInitRankConfig");
+  if (rc != B2G_OK) return rc;
   *comm = c;
   return B2G_OK;
 }
 
 extern "C" int b2g_comm_destroy(void* comm) {
   if (!comm) return B2G_OK;
+  {
+    std::lock_guard<std::mutex> lk(g_abort_mu);
+    if (g_aborted.erase(comm)) return B2G_OK;  // already freed by ncclCommAbort
+  }
   NcclApi* n = nccl();
   if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
-  ncclResult_t r = n->destroy(static_cast<ncclComm_t>(comm));
-  if (r != ncclSuccess) return nccl_fail(r, "ncclCommDestroy");
-  return B2G_OK;
+  ncclComm_t c = static_cast<ncclComm_t>(comm);
+  // flush this rank's operations (bounded), then free the communicator
+  int rc = nccl_settle(c, n->finalize(c), "ncclCommFinalize");
+  if (rc == B2G_ERR_TIMEOUT) {
+    std::lock_guard<std::mutex> lk(g_abort_mu);
+    g_aborted.erase(comm);  // aborted (freed) by the settle
+    return rc;
+  }
+  ncclResult_t r = n->destroy(c);
+  if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(r, "ncclCommDestroy");
+  return rc;
+}
+
+extern "C" int b2g_comm_check(void* comm, int64_t timeout_ms, void* stream) {
+  b2g::set_error("");
+  if (!comm || timeout_ms <= 0) return sfail(B2G_ERR_INVALID_ARG, "bad check arguments");
+  if (comm_aborted(comm)) return refuse_aborted();
+  NcclApi* n = nccl();
+  if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
+  ncclComm_t c = static_cast<ncclComm_t>(comm);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return sfail(B2G_ERR_UNSUPPORTED, "device ordinal out of range");
+  // one int per device for the liveness all-reduce (allocated at the first check)
+  static std::mutex mu;
+  static int32_t* word[64] = {};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (!word[dev] && cudaMalloc(&word[dev], 256) != cudaSuccess)
+      return sfail(B2G_ERR_CUDA, "cudaMalloc(liveness word)");
+  }
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : comm_stream(dev);
+  if (!s) return sfail(B2G_ERR_CUDA, "no communication stream");
+  const double deadline = now_ms() + (double)timeout_ms;
+  int rc = nccl_settle(c, n->all_reduce(word[dev], word[dev], 1, ncclInt32, ncclSum, c, s),
+                       "ncclAllReduce(liveness)");
+  if (rc != B2G_OK) return rc;
+  // The all-reduce completes only when every rank has joined it.  Poll; if the limit runs
+  // out, abort the communicator (its kernels in flight return) and report the peer as gone.
+  while (true) {
+    const cudaError_t q = cudaStreamQuery(s);
+    if (q == cudaSuccess) return B2G_OK;
+    if (q != cudaErrorNotReady) return sfail(B2G_ERR_CUDA, std::string("liveness check: ") +
+                                                               cudaGetErrorString(q));
+    ncclResult_t st = ncclSuccess;
+    if (n->async_error(c, &st) == ncclSuccess && st != ncclSuccess && st != ncclInProgress) {
+      abort_comm(c);
+      return nccl_fail(st, "liveness check (communicator aborted)");
+    }
+    if (now_ms() > deadline) break;
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+  abort_comm(c);
+  // the aborted all-reduce leaves the stream; wait for that (bounded) so it is usable again
+  const double drain = now_ms() + 10000.0;
+  while (cudaStreamQuery(s) == cudaErrorNotReady && now_ms() < drain)
+    std::this_thread::sleep_for(std::chrono::microseconds(200));
+  return sfail(B2G_ERR_TIMEOUT, "liveness check: a peer did not answer within " +
+                                    std::to_string(timeout_ms) +
+                                    " ms; the communicator was aborted");
 }
 
 extern "C" int b2g_gemm_sharded(const void* A_slab, void* B, float* C_slab, int64_t M, int64_t N,
@@ -158,6 +321,7 @@ extern "C" int b2g_gemm_sharded(const void* A_slab, void* B, float* C_slab, int6
   b2g::set_error("");
   if (M < 0 || N < 0 || K < 0 || !comm) return sfail(B2G_ERR_INVALID_ARG, "bad sharded arguments");
   if (ldb < std::max<int64_t>(N, 1)) return sfail(B2G_ERR_INVALID_ARG, "ldb < N");
+  if (comm_aborted(comm)) return refuse_aborted();
   NcclApi* n = nccl();
   if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
   ncclComm_t c = static_cast<ncclComm_t>(comm);
@@ -196,11 +360,9 @@ extern "C" int b2g_gemm_sharded(const void* A_slab, void* B, float* C_slab, int6
     const int64_t k0 = (int64_t)p * kp, k1 = std::min<int64_t>(K, k0 + kp);
     if (k1 > k0) {
       char* bp = static_cast<char*>(B) + k0 * ldb * 2;
-      r = n->bcast(bp, bp, (size_t)((k1 - k0) * ldb * 2), ncclUint8, root, c, cs);
-      if (r != ncclSuccess) {
-        rc = nccl_fail(r, "ncclBroadcast");
-        break;
-      }
+      rc = nccl_settle(c, n->bcast(bp, bp, (size_t)((k1 - k0) * ldb * 2), ncclUint8, root, c, cs),
+                       "ncclBroadcast");
+      if (rc != B2G_OK) break;
     }
     cudaEventRecord(done[p], cs);
     cudaStreamWaitEvent(s, done[p], 0);
@@ -239,6 +401,7 @@ cudaMemPool_t shard_pool(int dev) {
 }
 
 int comm_info(void* comm, int* world, int* rank) {
+  if (comm_aborted(comm)) return refuse_aborted();
   NcclApi* n = nccl();
   if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
   ncclResult_t r = n->count(static_cast<ncclComm_t>(comm), world);
@@ -280,9 +443,10 @@ extern "C" int b2g_gemm_sharded_k(const void* A_kslab, const void* B_kslab, floa
   // this rank's partial product over its K slab (kr == 0: zeros)
   rc = b2g_gemm_ex(A_kslab, B_kslab, P, M, N, kr, kr > 0 ? lda : 1, ldb, N, 1.0f, 0.0f, s);
   if (rc == B2G_OK) {
-    ncclResult_t r = n->reduce_scatter(P, recv, (size_t)rows * N, ncclFloat32, ncclSum,
-                                       static_cast<ncclComm_t>(comm), s);
-    if (r != ncclSuccess) rc = nccl_fail(r, "ncclReduceScatter");
+    rc = nccl_settle(static_cast<ncclComm_t>(comm),
+                     n->reduce_scatter(P, recv, (size_t)rows * N, ncclFloat32, ncclSum,
+                                       static_cast<ncclComm_t>(comm), s),
+                     "ncclReduceScatter");
   }
   if (rc == B2G_OK && !direct && rows > 0) {
     e = cudaMemcpy2DAsync(C_slab, ldc * sizeof(float), recv, N * sizeof(float), N * sizeof(float),
@@ -327,12 +491,11 @@ extern "C" int b2g_gemm_sharded_n(void* A, const void* B_nslab, float* C_nslab, 
     const int64_t m0 = (int64_t)p * mp, m1 = std::min<int64_t>(M, m0 + mp);
     if (m1 > m0) {
       char* ap = static_cast<char*>(A) + m0 * lda * 2;
-      ncclResult_t r = n->bcast(ap, ap, (size_t)((m1 - m0) * lda * 2), ncclUint8, root,
-                                static_cast<ncclComm_t>(comm), cs);
-      if (r != ncclSuccess) {
-        rc = nccl_fail(r, "ncclBroadcast");
-        break;
-      }
+      rc = nccl_settle(static_cast<ncclComm_t>(comm),
+                       n->bcast(ap, ap, (size_t)((m1 - m0) * lda * 2), ncclUint8, root,
+                                static_cast<ncclComm_t>(comm), cs),
+                       "ncclBroadcast");
+      if (rc != B2G_OK) break;
     }
     cudaEventRecord(done[p], cs);
     cudaStreamWaitEvent(s, done[p], 0);
@@ -363,9 +526,10 @@ extern "C" int b2g_gemm_sharded_n(void* A, const void* B_nslab, float* C_nslab, 
     send = packed;
   }
   if (rc == B2G_OK) {
-    ncclResult_t r = n->all_gather(send, G, (size_t)M * nw, ncclFloat32,
-                                   static_cast<ncclComm_t>(comm), s);
-    if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather");
+    rc = nccl_settle(static_cast<ncclComm_t>(comm),
+                     n->all_gather(send, G, (size_t)M * nw, ncclFloat32,
+                                   static_cast<ncclComm_t>(comm), s),
+                     "ncclAllGather");
   }
   for (int q = 0; q < world && rc == B2G_OK; ++q) {
     e = cudaMemcpy2DAsync(C_full + q * nw, N * sizeof(float), G + (size_t)q * M * nw,
@@ -471,6 +635,7 @@ extern "C" int b2g_chain_plan_create(void* comm, void* B, int64_t bytes, int roo
   if (!comm || !plan_out || bytes < 0 || (bytes > 0 && !B))
     return sfail(B2G_ERR_INVALID_ARG, "bad chain-plan arguments");
   *plan_out = nullptr;
+  if (comm_aborted(comm)) return refuse_aborted();
   NcclApi* n = nccl();
   if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
   const DrvApi* d = drv();
@@ -534,16 +699,18 @@ extern "C" int b2g_chain_plan_create(void* comm, void* B, int64_t bytes, int roo
       return cuda_sfail(e, "cudaMalloc(handle exchange)");
     }
     cudaMemcpy(static_cast<char*>(dbuf) + one * p->world, &mine, one, cudaMemcpyHostToDevice);
-    r = n->all_gather(static_cast<char*>(dbuf) + one * p->world, dbuf, one, ncclUint8, p->comm,
-                      p->cs);
+    int xrc = nccl_settle(p->comm, n->all_gather(static_cast<char*>(dbuf) + one * p->world, dbuf,
+                                                 one, ncclUint8, p->comm, p->cs),
+                          "ncclAllGather(handles)");
+    if (xrc == B2G_OK) xrc = nccl_sync(p->comm, p->cs, "handle exchange");
     std::vector<PeerInfo> all(p->world);
-    if (r == ncclSuccess) {
-      e = cudaStreamSynchronize(p->cs);
-      if (e == cudaSuccess)
-        e = cudaMemcpy(all.data(), dbuf, one * p->world, cudaMemcpyDeviceToHost);
+    if (xrc == B2G_OK) {
+      e = cudaMemcpy(all.data(), dbuf, one * p->world, cudaMemcpyDeviceToHost);
       if (e != cudaSuccess && rc == B2G_OK) rc = cuda_sfail(e, "handle exchange");
-    } else if (rc == B2G_OK) {
-      rc = nccl_fail(r, "ncclAllGather(handles)");
+    } else {
+      cudaFree(dbuf);
+      plan_free(p);
+      return xrc;  // the communicator is unusable: no status exchange can follow
     }
     cudaFree(dbuf);
     if (rc == B2G_OK) {
@@ -580,16 +747,19 @@ extern "C" int b2g_chain_plan_create(void* comm, void* B, int64_t bytes, int roo
     if (e == cudaSuccess) {
       const int32_t mine_rc = rc;
       cudaMemcpy(dst + p->world, &mine_rc, sizeof(int32_t), cudaMemcpyHostToDevice);
-      r = n->all_gather(dst + p->world, dst, 1, ncclInt32, p->comm, p->cs);
+      int xrc = nccl_settle(p->comm, n->all_gather(dst + p->world, dst, 1, ncclInt32, p->comm,
+                                                   p->cs),
+                            "ncclAllGather(status)");
+      if (xrc == B2G_OK) xrc = nccl_sync(p->comm, p->cs, "chain plan status exchange");
       std::vector<int32_t> rcs(p->world, 0);
-      if (r == ncclSuccess && cudaStreamSynchronize(p->cs) == cudaSuccess &&
+      if (xrc == B2G_OK &&
           cudaMemcpy(rcs.data(), dst, sizeof(int32_t) * p->world, cudaMemcpyDeviceToHost) ==
               cudaSuccess) {
         for (int q = 0; q < p->world; ++q)
           if (rcs[q] != B2G_OK && rc == B2G_OK)
             rc = sfail(rcs[q], "chain plan set-up failed on rank " + std::to_string(q));
       } else if (rc == B2G_OK) {
-        rc = sfail(B2G_ERR_NCCL, "chain plan status exchange failed");
+        rc = xrc != B2G_OK ? xrc : sfail(B2G_ERR_NCCL, "chain plan status exchange failed");
       }
       cudaFree(dst);
     } else if (rc == B2G_OK) {
@@ -617,7 +787,9 @@ extern "C" int b2g_chain_plan_destroy(void* plan) {
     o = nullptr;
   }
   int rc = B2G_OK;
-  if (p->world > 1) {
+  // With an aborted communicator (a peer is gone) there is no barrier to take: the mappings
+  // are dropped and this rank's memory is freed.
+  if (p->world > 1 && !comm_aborted(p->comm)) {
     NcclApi* n = nccl();
     int32_t* d = nullptr;
     if (!n) {
@@ -625,10 +797,9 @@ extern "C" int b2g_chain_plan_destroy(void* plan) {
     } else if (cudaMalloc(&d, sizeof(int32_t) * (p->world + 1)) != cudaSuccess) {
       rc = sfail(B2G_ERR_CUDA, "cudaMalloc(chain plan barrier)");
     } else {
-      ncclResult_t r = n->all_gather(d + p->world, d, 1, ncclInt32, p->comm, p->cs);
-      if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather(chain plan barrier)");
-      else if (cudaStreamSynchronize(p->cs) != cudaSuccess)
-        rc = sfail(B2G_ERR_CUDA, "chain plan barrier");
+      rc = nccl_settle(p->comm, n->all_gather(d + p->world, d, 1, ncclInt32, p->comm, p->cs),
+                       "ncclAllGather(chain plan barrier)");
+      if (rc == B2G_OK) rc = nccl_sync(p->comm, p->cs, "chain plan barrier");
       cudaFree(d);
     }
   }
@@ -664,6 +835,7 @@ int chain_pipeline(b2g_chain_plan* p, const std::vector<std::pair<int64_t, int64
                    int64_t row_bytes, cudaStream_t s, F&& on_panel) {
   const DrvApi* d = drv();
   if (!d) return sfail(B2G_ERR_UNSUPPORTED, "stream memory operations unavailable");
+  if (p->world > 1 && comm_aborted(p->comm)) return refuse_aborted();
   if ((int)panels.size() > kMaxPanels) return sfail(B2G_ERR_INVALID_ARG, "too many panels");
   if (!panels.empty() && panels.back().second * row_bytes > p->bytes)
     return sfail(B2G_ERR_INVALID_ARG, "the broadcast operand exceeds the plan's buffer");
@@ -874,6 +1046,7 @@ extern "C" int b2g_rs_plan_create(void* comm, int64_t M, int64_t N, void** plan_
   b2g::set_error("");
   if (!comm || !plan_out || M < 0 || N < 0) return sfail(B2G_ERR_INVALID_ARG, "bad plan arguments");
   *plan_out = nullptr;
+  if (comm_aborted(comm)) return refuse_aborted();
   NcclApi* n = nccl();
   if (!n) return sfail(B2G_ERR_NCCL, "NCCL unavailable");
   if (!drv()) return sfail(B2G_ERR_UNSUPPORTED, "stream memory operations unavailable");
@@ -926,14 +1099,19 @@ extern "C" int b2g_rs_plan_create(void* comm, int64_t M, int64_t N, void** plan_
     cudaStream_t xs = nullptr;
     cudaStreamCreateWithFlags(&xs, cudaStreamNonBlocking);
     cudaMemcpy(static_cast<char*>(dbuf) + one * p->world, &mine, one, cudaMemcpyHostToDevice);
-    r = n->all_gather(static_cast<char*>(dbuf) + one * p->world, dbuf, one, ncclUint8, p->comm, xs);
+    int xrc = nccl_settle(p->comm, n->all_gather(static_cast<char*>(dbuf) + one * p->world, dbuf,
+                                                 one, ncclUint8, p->comm, xs),
+                          "ncclAllGather(handles)");
+    if (xrc == B2G_OK) xrc = nccl_sync(p->comm, xs, "handle exchange");
     std::vector<RsPeerInfo> all(p->world);
-    if (r == ncclSuccess) {
-      e = cudaStreamSynchronize(xs);
-      if (e == cudaSuccess) e = cudaMemcpy(all.data(), dbuf, one * p->world, cudaMemcpyDeviceToHost);
+    if (xrc == B2G_OK) {
+      e = cudaMemcpy(all.data(), dbuf, one * p->world, cudaMemcpyDeviceToHost);
       if (e != cudaSuccess && rc == B2G_OK) rc = cuda_sfail(e, "handle exchange");
-    } else if (rc == B2G_OK) {
-      rc = nccl_fail(r, "ncclAllGather(handles)");
+    } else {
+      cudaFree(dbuf);
+      cudaStreamDestroy(xs);
+      rs_plan_free(p);
+      return xrc;  // the communicator is unusable: no status exchange can follow
     }
     cudaFree(dbuf);
     if (rc == B2G_OK)
@@ -963,16 +1141,19 @@ extern "C" int b2g_rs_plan_create(void* comm, int64_t M, int64_t N, void** plan_
     if (e == cudaSuccess) {
       const int32_t mine_rc = rc;
       cudaMemcpy(dst + p->world, &mine_rc, sizeof(int32_t), cudaMemcpyHostToDevice);
-      r = n->all_gather(dst + p->world, dst, 1, ncclInt32, p->comm, xs);
+      int xrc2 = nccl_settle(p->comm, n->all_gather(dst + p->world, dst, 1, ncclInt32, p->comm, xs),
+                             "ncclAllGather(status)");
+      if (xrc2 == B2G_OK) xrc2 = nccl_sync(p->comm, xs, "reduce-scatter plan status exchange");
       std::vector<int32_t> rcs(p->world, 0);
-      if (r == ncclSuccess && cudaStreamSynchronize(xs) == cudaSuccess &&
+      if (xrc2 == B2G_OK &&
           cudaMemcpy(rcs.data(), dst, sizeof(int32_t) * p->world, cudaMemcpyDeviceToHost) ==
               cudaSuccess) {
         for (int q = 0; q < p->world; ++q)
           if (rcs[q] != B2G_OK && rc == B2G_OK)
             rc = sfail(rcs[q], "reduce-scatter plan set-up failed on rank " + std::to_string(q));
       } else if (rc == B2G_OK) {
-        rc = sfail(B2G_ERR_NCCL, "reduce-scatter plan status exchange failed");
+        rc = xrc2 != B2G_OK ? xrc2
+                            : sfail(B2G_ERR_NCCL, "reduce-scatter plan status exchange failed");
       }
       cudaFree(dst);
     } else if (rc == B2G_OK) {
@@ -999,7 +1180,7 @@ extern "C" int b2g_rs_plan_destroy(void* plan) {
     o = nullptr;
   }
   int rc = B2G_OK;
-  if (p->world > 1) {
+  if (p->world > 1 && !comm_aborted(p->comm)) {
     NcclApi* n = nccl();
     int32_t* d = nullptr;
     cudaStream_t xs = nullptr;
@@ -1009,10 +1190,9 @@ extern "C" int b2g_rs_plan_destroy(void* plan) {
                cudaStreamCreateWithFlags(&xs, cudaStreamNonBlocking) != cudaSuccess) {
       rc = sfail(B2G_ERR_CUDA, "reduce-scatter plan barrier set-up");
     } else {
-      ncclResult_t r = n->all_gather(d + p->world, d, 1, ncclInt32, p->comm, xs);
-      if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather(plan barrier)");
-      else if (cudaStreamSynchronize(xs) != cudaSuccess)
-        rc = sfail(B2G_ERR_CUDA, "reduce-scatter plan barrier");
+      rc = nccl_settle(p->comm, n->all_gather(d + p->world, d, 1, ncclInt32, p->comm, xs),
+                       "ncclAllGather(plan barrier)");
+      if (rc == B2G_OK) rc = nccl_sync(p->comm, xs, "reduce-scatter plan barrier");
     }
     if (d) cudaFree(d);
     if (xs) cudaStreamDestroy(xs);
@@ -1027,6 +1207,7 @@ extern "C" int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const voi
   b2g::set_error("");
   auto* p = static_cast<b2g_rs_plan*>(plan);
   if (!p) return sfail(B2G_ERR_INVALID_ARG, "null plan");
+  if (p->world > 1 && comm_aborted(p->comm)) return refuse_aborted();
   const DrvApi* d = drv();
   if (!d) return sfail(B2G_ERR_UNSUPPORTED, "stream memory operations unavailable");
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -2,7 +2,8 @@
 
     python tests/golden/gen_golden.py
 
-Needs the reference checkout (its directory in B2G_REFERENCE_DIR, else oracle/build_ref.py's default):
+Needs the reference checkout (B2G_REFERENCE_DIR, or a `reference` directory beside the
+repository; see oracle/build_ref.py):
 oracle/build_ref.py compiles the reference's GEMM_Naive (mmm.cpp:52-62), its two
 validateResults (mmm.cpp:1387-1407, mmmTensor.cpp:278-306) and its G pack loop
 (mmmTensor.cpp:329-340) for the CPU.  Inputs come from the seeded generator of the oracle,

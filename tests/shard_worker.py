@@ -528,3 +528,79 @@ def nccl_p2p_rs_fail_rank(rank, world, uid_path, M, N, K, bad_rank, out_q):
         out_q.put((rank, outcomes, bad, status1, None))
     except Exception:
         out_q.put((rank, [], -1, -1, traceback.format_exc()))
+
+
+def nccl_peer_leaves_rank(rank, world, uid_path, out_q):
+    """Rank 1 leaves between steps: after one chain GEMM and one liveness check that every rank
+    passes, it stops taking part (it stays alive, idle, until rank 0 is done, so no peer memory
+    goes away under rank 0).  Rank 0's next liveness check must end within its limit with
+    B2G_ERR_TIMEOUT (the communicator aborted, its all-reduce kernel returned); its next chain
+    call must be refused without queueing work; plan and communicator teardown must return;
+    and the GPU must still compute a correct GEMM.  NVLS is off (NCCL_NVLS_ENABLE=0).
+    Reports (rank, first check ok, check code after the leave, seconds it took, code of the
+    refused call, GEMM correct afterwards)."""
+    import time
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        import torch
+        from oracle import orc
+        b2g = _load_pkg("b2g")
+        torch.cuda.set_device(rank)
+        b2g.set_option("comm_timeout_ms", 20000)
+        comm = _nccl_comm(b2g, rank, world, uid_path)
+        M, N, K = 512 * world, 512, 1024
+        row0, rows = b2g.slab_rows(M, world, rank)
+        dA = torch.empty((rows, K), dtype=torch.float16, device="cuda")
+        b2g.fill_uniform(dA, rows * K, 1, row0 * K)
+        dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+        if rank == 0:
+            b2g.fill_uniform(dB, K * N, 2)
+        plan = b2g.chain_plan_create(comm, dB, K * N * 2, 0)
+        dC = torch.empty((rows, N), dtype=torch.float32, device="cuda")
+        b2g.gemm_sharded_chain(plan, dA, dC, M, N, K, k_panels=2)
+        torch.cuda.synchronize()
+        b2g.comm_check(comm, 10000)
+        first_ok = True
+        done_flag = uid_path + ".rank0_done"
+        if rank != 0:
+            out_q.put((rank, first_ok, 0, 0.0, 0, True, None))
+            out_q.close()
+            out_q.join_thread()
+            t0 = time.time()
+            while not os.path.exists(done_flag) and time.time() - t0 < 120:
+                time.sleep(0.05)
+            os._exit(0)  # leaves without tearing anything down
+        time.sleep(0.5)
+        t0 = time.time()
+        code = 0
+        try:
+            b2g.comm_check(comm, 3000)
+        except b2g.B2GError as e:
+            code = e.code
+        took = time.time() - t0
+        refused = 0
+        try:
+            b2g.gemm_sharded_chain(plan, dA, dC, M, N, K, k_panels=2)
+        except b2g.B2GError as e:
+            refused = e.code
+        b2g.chain_plan_destroy(plan)
+        b2g.comm_destroy(comm)
+        # the GPU still works
+        A = orc.uniform_f16((256, 512), 5)
+        B = orc.uniform_f16((512, 384), 6)
+        gA = torch.from_numpy(A.view(np.int16)).view(torch.float16).cuda()
+        gB = torch.from_numpy(B.view(np.int16)).view(torch.float16).cuda()
+        gC = torch.empty((256, 384), dtype=torch.float32, device="cuda")
+        b2g.gemm(gA, gB, gC, 256, 384, 512)
+        torch.cuda.synchronize()
+        ok_after = orc.check(gC.cpu().numpy(), orc.gemm_f64(A, B), 512, 1.0, 1.0)[0] == 0
+        with open(done_flag, "w") as f:
+            f.write("done")
+        out_q.put((rank, first_ok, code, took, refused, bool(ok_after), None))
+    except Exception:
+        try:
+            with open(uid_path + ".rank0_done", "w") as f:
+                f.write("failed")
+        except OSError:
+            pass
+        out_q.put((rank, False, -1, -1.0, -1, False, traceback.format_exc()))

@@ -283,3 +283,30 @@ def test_p2p_rs_peer_failure_reported_everywhere(b2g, cuda, world, bad_rank):
         want = "invalid" if rank == bad_rank else "peer_failed"
         assert outcomes == ["ok", want, "ok"], (rank, outcomes, status1)
         assert bad == 0, (rank, bad)
+
+
+def test_peer_leaves_between_steps_is_reported_within_the_limit(b2g, cuda):
+    """Failure detection on 2 GPUs without a GPU fault: rank 1 stops taking part between steps.
+    Rank 0's liveness check (b2g_comm_check, 3 s limit) returns B2G_ERR_TIMEOUT, with the
+    communicator aborted, in a few seconds; its next chain call is refused (B2G_ERR_NCCL)
+    without queueing work; teardown returns; the GPU still computes correctly."""
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=shard_worker.nccl_peer_leaves_rank,
+                             args=(r, 2, os.path.join(d, "id"), q)) for r in range(2)]
+        for p in procs:
+            p.start()
+        res = sorted(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=120)
+    for rank, first_ok, code, took, refused, ok_after, tb in res:
+        assert tb is None, tb
+        assert first_ok, rank
+    r0 = res[0]
+    assert r0[2] == b2g.ERR_TIMEOUT, r0
+    assert r0[3] < 3.0 + 12.0, r0  # the limit plus the bounded drain of the aborted stream
+    assert r0[4] == b2g.ERR_NCCL, r0
+    assert r0[5], r0
