@@ -267,11 +267,13 @@ int b2g_gemm_sharded_n(void* A, const void* B_nslab, float* C_nslab, int64_t M, 
 /*
  * Launch plan the library would choose for a row-major M x N x K GEMM of operand type `dtype`
  * on a GPU with `sm_count` SMs (full cluster occupancy assumed), under the current options:
- * CTAs per tile, tile width, K splits per split tile, and how many tiles run unsplit.  No GPU
- * needed (no reference counterpart; for tests and tuning).
+ * CTAs per tile, tile width, K splits per split tile, how many tiles run unsplit, and (if
+ * cta_rows is not NULL) the A rows each CTA holds: 128, or 64 for the half-height pair tile
+ * (128 x 256 over a CTA pair).  No GPU needed (no reference counterpart; for tests and
+ * tuning).
  */
 int b2g_plan_preview(int64_t M, int64_t N, int64_t K, int dtype, int sm_count, int* cta_group,
-                     int* tile_n, int* k_splits, int* num_full);
+                     int* tile_n, int* k_splits, int* num_full, int* cta_rows);
 
 /*
  * Fused epilogue variants: C = alpha*A.B + beta*C + bias, with C stored as fp32
@@ -362,6 +364,11 @@ int b2g_device_status(int clear);
  *   "force_generic" 1 = run the generic kernel for every call (testing)
  *   "tile_n"       0 = choose by shape (default); 128 (one CTA, 128x128 tiles), 256 or 512
  *                  columns per tile (512 needs CTA pairs)
+ *   "pair_rows"    0 = choose by shape (default); 64 = half-height pair tiles (128 x 256 over a
+ *                  CTA pair, UMMA M = 128 with cta_group::2, 64 A rows per CTA) whenever the
+ *                  call allows them; 128 = never.  The planner takes them for skinny shapes
+ *                  whose one-CTA tiles would split K: each CTA's partial tile is half as
+ *                  large and fewer splits are needed
  *   "split_k"      0 = choose by shape (default), else split every tile's K this many ways
  *   "tail_split"   1 (default) = split only the tiles of a partial last wave; 0 = never
  *   "serial_fixup" 1 = split-K partials are always summed by the last unit to arrive

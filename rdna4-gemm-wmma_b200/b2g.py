@@ -111,7 +111,7 @@ def load(path=None):
     L.b2g_chain_broadcast.argtypes = [vp, i64, ctypes.c_int, vp]
     L.b2g_plan_preview.restype = ctypes.c_int
     L.b2g_plan_preview.argtypes = [i64, i64, i64, ctypes.c_int, ctypes.c_int] + \
-        [ctypes.POINTER(ctypes.c_int)] * 4
+        [ctypes.POINTER(ctypes.c_int)] * 5
     L.b2g_gemm_sharded_n_chain.restype = ctypes.c_int
     L.b2g_gemm_sharded_n_chain.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, ctypes.c_int, vp]
     L.b2g_gemm_epilogue.restype = ctypes.c_int
@@ -369,11 +369,13 @@ def chain_broadcast(plan, nbytes, panels=8, stream=None):
     _check(load().b2g_chain_broadcast(plan, nbytes, panels, _stream(stream)))
 
 
-def plan_preview(M, N, K, dtype=0, sm_count=148):
-    """(cta_group, tile_n, k_splits, num_full) the library would choose (no GPU needed)."""
-    out = [ctypes.c_int() for _ in range(4)]
+def plan_preview(M, N, K, dtype=0, sm_count=148, rows=False):
+    """(cta_group, tile_n, k_splits, num_full) the library would choose (no GPU needed); with
+    rows=True also the A rows per CTA (128, or 64 for half-height pair tiles)."""
+    out = [ctypes.c_int() for _ in range(5)]
     _check(load().b2g_plan_preview(M, N, K, dtype, sm_count, *[ctypes.byref(x) for x in out]))
-    return tuple(x.value for x in out)
+    vals = tuple(x.value for x in out)
+    return vals if rows else vals[:4]
 
 
 def gemm_sharded_n_chain(plan, B_nslab, C_nslab, M, N, K, m_panels=4, lda=None, ldb=None,

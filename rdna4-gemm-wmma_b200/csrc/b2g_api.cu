@@ -37,6 +37,8 @@ static thread_local int t_path = B2G_PATH_NONE;
 // Split-K workspace bytes (partial tiles) of the calling thread's last tensor-core launch: 0
 // when it split nothing or reduced through distributed shared memory.
 static thread_local int64_t t_split_ws = 0;
+// Set while run() plans a call again without half-height pair tiles (see there).
+static thread_local bool t_no_half = false;
 
 static int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -64,6 +66,7 @@ static std::atomic<int64_t> opt_store_hint{0};
 static std::atomic<int64_t> opt_split_k{0};  // 0 = choose by shape, else the split count
 static std::atomic<int64_t> opt_tail_split{1};  // split the tail wave's tiles (auto mode)
 static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream serialization
+static std::atomic<int64_t> opt_pair_rows{0};  // 0 = choose, 64 = half-height pair tiles, 128 = never
 // Kernels this library has launched (every GEMM, scale and fill kernel), for callers that
 // count launches (b2g_get_option("launches")).
 static std::atomic<int64_t> g_launches{0};
@@ -146,9 +149,11 @@ static CUresult encode_cached(CUtensorMap* out, CUtensorMapDataType dt, cuuint32
 struct DevState {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
-  bool attr_set[2][4][2][2] = {};  // [fp8][variant][b_kmajor][c_mcontig]
-  int max_clusters[2][4][2][2] = {};
-  int max_clusters_cg1[2][4][2][2][9] = {};  // one-CTA tiles launched in clusters of s (cluster fix-up)
+  bool attr_set[2][5][2][2] = {};  // [fp8][variant][b_kmajor][c_mcontig]
+  int max_clusters[2][5][2][2] = {};
+  // clusters of s split units resident at once (cluster fix-up): one-CTA tiles, or s CTA pairs
+  // of half-height pair tiles
+  int max_clusters_cg1[2][5][2][2][9] = {};
 };
 static std::mutex g_dev_mu;
 static DevState g_dev[64];
@@ -634,26 +639,28 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
       jsz > INT32_MAX / 2 || ksz > INT32_MAX / 2)
     return launch_generic(B2G_PATH_GENERIC);
   int bi, bb, ba;
-  if (batched) {
-    // a tile never spans two batch entries: the 128-row box covers (i, b) only, rows past
-    // b's extent are zero-filled on load and clipped on store
-    bi = (isz >= 128 || (128 % isz) != 0) ? 128 : (int)isz;
-    bb = 128 / bi;
-    ba = 1;
-  } else if (isz >= 128 || (128 % isz) != 0 || bsz * asz == 1) {
-    bi = 128; bb = 1; ba = 1;
-  } else {
-    bi = (int)isz;
-    const int rem = 128 / bi;
-    if (bsz >= rem || (rem % bsz) != 0) {
-      bb = rem; ba = 1;
+  // the load box of one CTA's `rows` rows (128, or 64 for half-height pair tiles) over (i, b, a)
+  auto decompose = [&](int rows) {
+    if (batched) {
+      // a tile never spans two batch entries: the box covers (i, b) only, rows past b's
+      // extent are zero-filled on load and clipped on store
+      bi = (isz >= rows || (rows % isz) != 0) ? rows : (int)isz;
+      bb = rows / bi;
+      ba = 1;
+    } else if (isz >= rows || (rows % isz) != 0 || bsz * asz == 1) {
+      bi = rows; bb = 1; ba = 1;
     } else {
-      bb = (int)bsz; ba = rem / bb;
+      bi = (int)isz;
+      const int rem = rows / bi;
+      if (bsz >= rem || (rem % bsz) != 0) {
+        bb = rem; ba = 1;
+      } else {
+        bb = (int)bsz; ba = rem / bb;
+      }
     }
-  }
-  const int si = std::min(bi, 32);
-  const int sb = std::min(bb, 32 / si);
-  const int sa = 32 / (si * sb);
+  };
+  decompose(128);
+  int si = std::min(bi, 32);
   if (c_m && si < 4) return launch_generic(B2G_PATH_GENERIC);  // TMA inner box >= 16 bytes
 
   // ---- TMA legality: 16-byte aligned bases and strides (size-1 modes do not matter)
@@ -682,6 +689,41 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   };
 
   CUtensorMap tmA, tmB, tmC;
+  // choose CTA grouping (on 128-row tiles)
+  int num_m_tiles_i = (int)((isz + bi - 1) / bi);
+  int num_m_tiles_b = (int)((bsz + bb - 1) / bb);
+  int num_m_tiles_a = (int)((asz + ba - 1) / ba);
+  int64_t nmt64 = (int64_t)num_m_tiles_i * num_m_tiles_b * num_m_tiles_a;
+  // batched: a CTA pair holds M tiles 2p and 2p+1, whose rows must be of one batch entry (the
+  // pair's MMA shares both halves of B); with an odd number of M tiles per batch entry, tiles
+  // are one-CTA
+  const bool pair_ok = !batched || ((int64_t)num_m_tiles_i * num_m_tiles_b) % 2 == 0;
+  const int64_t kit = ((ksz + kb_elems - 1) / kb_elems) * jsz;
+  // half-height pair tiles need the cluster fix-up whenever they split K
+  int half_opt = (batched || t_no_half) ? 128 : (int)opt_pair_rows.load();
+  if (half_opt == 0 && (!opt_cluster_fixup.load() || opt_serial_fixup.load() || opt_split_k.load() > 4))
+    half_opt = 128;
+  TileChoice tc = choose_tiles(nmt64, N, kit, ds->sm_count, pair_ok ? (int)opt_cta_group.load() : 1,
+                               (int)opt_tile_n.load(), half_opt);
+  if (tc.half) {
+    // half-height pair tiles: each CTA loads 64 rows; the M tiles are 64-row tiles, a pair
+    // holds tiles 2p and 2p+1
+    decompose(64);
+    si = std::min(bi, 32);
+    if (c_m && si < 4) {  // the 32-row store box of a warp would be too narrow: plain tiles
+      decompose(128);
+      si = std::min(bi, 32);
+      tc = choose_tiles(nmt64, N, kit, ds->sm_count, pair_ok ? (int)opt_cta_group.load() : 1,
+                        (int)opt_tile_n.load(), 128);
+    } else {
+      num_m_tiles_i = (int)((isz + bi - 1) / bi);
+      num_m_tiles_b = (int)((bsz + bb - 1) / bb);
+      num_m_tiles_a = (int)((asz + ba - 1) / ba);
+      nmt64 = (int64_t)num_m_tiles_i * num_m_tiles_b * num_m_tiles_a;
+    }
+  }
+  const int sb = std::min(bb, 32 / si);
+  const int sa = 32 / (si * sb);
   // A: dims (k, j, i, b, a)
   {
     cuuint64_t dims[5] = {(cuuint64_t)ksz, (cuuint64_t)jsz, (cuuint64_t)isz, (cuuint64_t)bsz,
@@ -695,17 +737,6 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     CUresult r = encode_cached(&tmA, map_type, 5, const_cast<void*>(A), dims, st, box, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
     if (r != CUDA_SUCCESS) return launch_generic(B2G_PATH_GENERIC);  // tensor map A not encodable
   }
-  // choose CTA grouping
-  const int num_m_tiles_i = (int)((isz + bi - 1) / bi);
-  const int num_m_tiles_b = (int)((bsz + bb - 1) / bb);
-  const int num_m_tiles_a = (int)((asz + ba - 1) / ba);
-  const int64_t nmt64 = (int64_t)num_m_tiles_i * num_m_tiles_b * num_m_tiles_a;
-  // batched: a CTA pair holds M tiles 2p and 2p+1, whose rows must be of one batch entry (the
-  // pair's MMA shares both halves of B); with an odd number of M tiles per batch entry, tiles
-  // are one-CTA
-  const bool pair_ok = !batched || ((int64_t)num_m_tiles_i * num_m_tiles_b) % 2 == 0;
-  const TileChoice tc = choose_tiles(nmt64, N, ((ksz + kb_elems - 1) / kb_elems) * jsz, ds->sm_count,
-                                     pair_ok ? (int)opt_cta_group.load() : 1, (int)opt_tile_n.load());
   const int cg = tc.cg, bn = tc.bn;
   const int64_t nnt64 = (N + bn - 1) / bn;
   if (nmt64 * nnt64 > INT32_MAX / 4) return launch_generic(B2G_PATH_GENERIC);
@@ -784,20 +815,14 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.b_batched = batched ? 1 : 0;
   p.alpha = alpha;
   p.accumulate = beta != 0.0f ? 1 : 0;
-  if (beta != 0.0f && beta != 1.0f) {  // C = beta*C first; the kernel then adds alpha*A.B
-    scale_c_kernel<<<eblocks, eth, 0, stream>>>(Cp, make_geo(), beta);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return cuda_fail(e, "scale kernel launch");
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-  }
   p.timeout_ns = (unsigned long long)opt_timeout_ns.load();
   p.fault_flags = (int)opt_fault_flags.load();
 
   // ---- launch
   using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
   const int bk = b_k ? 1 : 0, cm = c_m ? 1 : 0;
-  const int variant = cg == 1 ? (bn == 128 ? 3 : 0) : (bn == 256 ? 1 : 2);
-  static const KernFn table[2][4][2][2] = {
+  const int variant = tc.half ? 4 : cg == 1 ? (bn == 128 ? 3 : 0) : (bn == 256 ? 1 : 2);
+  static const KernFn table[2][5][2][2] = {
       {{{gemm_tc_kernel<1, 256, false, false, 2>, gemm_tc_kernel<1, 256, false, true, 2>},
         {gemm_tc_kernel<1, 256, true, false, 2>, gemm_tc_kernel<1, 256, true, true, 2>}},
        {{gemm_tc_kernel<2, 256, false, false, 2>, gemm_tc_kernel<2, 256, false, true, 2>},
@@ -805,7 +830,9 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
        {{gemm_tc_kernel<2, 512, false, false, 2>, gemm_tc_kernel<2, 512, false, true, 2>},
         {gemm_tc_kernel<2, 512, true, false, 2>, gemm_tc_kernel<2, 512, true, true, 2>}},
        {{gemm_tc_kernel<1, 128, false, false, 2>, gemm_tc_kernel<1, 128, false, true, 2>},
-        {gemm_tc_kernel<1, 128, true, false, 2>, gemm_tc_kernel<1, 128, true, true, 2>}}},
+        {gemm_tc_kernel<1, 128, true, false, 2>, gemm_tc_kernel<1, 128, true, true, 2>}},
+       {{gemm_tc_kernel<2, 256, false, false, 2, 64>, gemm_tc_kernel<2, 256, false, true, 2, 64>},
+        {gemm_tc_kernel<2, 256, true, false, 2, 64>, gemm_tc_kernel<2, 256, true, true, 2, 64>}}},
       {{{gemm_tc_kernel<1, 256, false, false, 1>, gemm_tc_kernel<1, 256, false, true, 1>},
         {gemm_tc_kernel<1, 256, true, false, 1>, gemm_tc_kernel<1, 256, true, true, 1>}},
        {{gemm_tc_kernel<2, 256, false, false, 1>, gemm_tc_kernel<2, 256, false, true, 1>},
@@ -813,9 +840,12 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
        {{gemm_tc_kernel<2, 512, false, false, 1>, gemm_tc_kernel<2, 512, false, true, 1>},
         {gemm_tc_kernel<2, 512, true, false, 1>, gemm_tc_kernel<2, 512, true, true, 1>}},
        {{gemm_tc_kernel<1, 128, false, false, 1>, gemm_tc_kernel<1, 128, false, true, 1>},
-        {gemm_tc_kernel<1, 128, true, false, 1>, gemm_tc_kernel<1, 128, true, true, 1>}}}};
-  static const uint32_t smem_of[4] = {Cfg<1, 256>::SMEM_BYTES, Cfg<2, 256>::SMEM_BYTES,
-                                      Cfg<2, 512>::SMEM_BYTES, Cfg<1, 128>::SMEM_BYTES};
+        {gemm_tc_kernel<1, 128, true, false, 1>, gemm_tc_kernel<1, 128, true, true, 1>}},
+       {{gemm_tc_kernel<2, 256, false, false, 1, 64>, gemm_tc_kernel<2, 256, false, true, 1, 64>},
+        {gemm_tc_kernel<2, 256, true, false, 1, 64>, gemm_tc_kernel<2, 256, true, true, 1, 64>}}}};
+  static const uint32_t smem_of[5] = {Cfg<1, 256>::SMEM_BYTES, Cfg<2, 256>::SMEM_BYTES,
+                                      Cfg<2, 512>::SMEM_BYTES, Cfg<1, 128>::SMEM_BYTES,
+                                      Cfg<2, 256, 64>::SMEM_BYTES};
   const int e8 = esz == 1 ? 1 : 0;
   KernFn kern = table[e8][variant][bk][cm];
   const uint32_t smem = smem_of[variant];
@@ -850,7 +880,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   // Tail split: when the tiles fill whole waves plus a partial one, split only the tiles of
   // the partial wave so that its units fill the CTA groups.
   const SplitChoice sc = choose_splits(p.num_tiles, p.k_iters, group_cap, cg, (int)opt_split_k.load(),
-                                       opt_tail_split.load() != 0);
+                                       opt_tail_split.load() != 0, tc.half);
   p.k_per_split = sc.k_per_split;
   p.k_splits = sc.k_splits;
   int full = sc.num_full;
@@ -869,11 +899,12 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   t_split_ws = 0;
   p.ws = nullptr;
   p.counters = nullptr;
-  // Cluster fix-up: one-CTA tiles, every tile split, at most 8 splits, and one unit per CTA
-  // with every cluster resident at once (checked against the cluster occupancy).
+  // Cluster fix-up: one-CTA tiles (at most 8 splits) or half-height pair tiles (at most 4
+  // splits: 2 CTAs each), every tile split, one unit per CTA group, and every cluster resident
+  // at once (checked against the cluster occupancy).
   p.cluster_fixup = 0;
-  if (cg == 1 && p.k_splits > 1 && p.k_splits <= 8 && p.num_full == 0 && opt_cluster_fixup.load() &&
-      !opt_serial_fixup.load()) {
+  if ((cg == 1 || tc.half) && p.k_splits > 1 && p.k_splits * cg <= 8 && p.num_full == 0 &&
+      opt_cluster_fixup.load() && !opt_serial_fixup.load()) {
     const int S = p.k_splits;
     int nclu = 0;
     {
@@ -883,10 +914,10 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
         cudaLaunchConfig_t qc = {};
         cudaLaunchAttribute qa[1];
         qa[0].id = cudaLaunchAttributeClusterDimension;
-        qa[0].val.clusterDim.x = (unsigned)S;
+        qa[0].val.clusterDim.x = (unsigned)(cg * S);
         qa[0].val.clusterDim.y = 1;
         qa[0].val.clusterDim.z = 1;
-        qc.gridDim = dim3((unsigned)(S * (ds->sm_count / S)), 1, 1);
+        qc.gridDim = dim3((unsigned)(cg * S * (ds->sm_count / (cg * S))), 1, 1);
         qc.blockDim = dim3(kThreads, 1, 1);
         qc.dynamicSmemBytes = smem;
         qc.attrs = qa;
@@ -900,6 +931,19 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
       }
     }
     if (nclu > 0 && p.num_units <= nclu * S) p.cluster_fixup = 1;
+  }
+  if (tc.half && p.k_splits > 1 && !p.cluster_fixup) {
+    // Half-height pair tiles reduce split partials only through distributed shared memory.
+    // Forced by the caller: refuse; chosen by the planner: plan again without them.
+    if (opt_pair_rows.load() == 64)
+      return fail(B2G_ERR_UNSUPPORTED,
+                  "half-height pair tiles split K only with the cluster fix-up (at most 4 "
+                  "splits, every cluster resident)");
+    t_no_half = true;
+    const int rc2 = run(A, as, ast, B, bs, bst, Cv, cs, cst, dtype, alpha, beta, stream, fixed, bias,
+                        c_type, b_batch);
+    t_no_half = false;
+    return rc2;
   }
   void* scratch = nullptr;
   const size_t split_tiles = (size_t)(p.num_tiles - p.num_full);
@@ -975,7 +1019,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   cfg.numAttrs = 0;
   if (cg == 2 || p.cluster_fixup) {
     attr[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
-    attr[cfg.numAttrs].val.clusterDim.x = cg == 2 ? 2u : (unsigned)p.k_splits;
+    attr[cfg.numAttrs].val.clusterDim.x = p.cluster_fixup ? (unsigned)(cg * p.k_splits) : 2u;
     attr[cfg.numAttrs].val.clusterDim.y = 1;
     attr[cfg.numAttrs].val.clusterDim.z = 1;
     ++cfg.numAttrs;
@@ -986,6 +1030,15 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
     ++cfg.numAttrs;
+  }
+  if (beta != 0.0f && beta != 1.0f) {  // C = beta*C first; the kernel then adds alpha*A.B
+    scale_c_kernel<<<eblocks, eth, 0, stream>>>(Cp, make_geo(), beta);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      if (scratch) cudaFreeAsync(scratch, stream);
+      return cuda_fail(e, "scale kernel launch");
+    }
+    g_launches.fetch_add(1, std::memory_order_relaxed);
   }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tmA, tmB, tmC, p);
   lease.commit(stream);
@@ -1280,6 +1333,9 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_comm_timeout_ms = value;
   } else if (!strcmp(key, "comm_nonblocking")) {
     opt_comm_nonblocking = value ? 1 : 0;
+  } else if (!strcmp(key, "pair_rows")) {
+    if (value != 0 && value != 64 && value != 128) return B2G_ERR_INVALID_ARG;
+    opt_pair_rows = value;
   } else if (!strcmp(key, "ring_slots")) {
     if (value < 512 || value > (int64_t)kCounterSlots || value % 64) return B2G_ERR_INVALID_ARG;
     opt_ring_slots = value;
@@ -1309,6 +1365,7 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "cluster_fixup")) return opt_cluster_fixup;
   if (!strcmp(key, "serial_fixup")) return opt_serial_fixup;
   if (!strcmp(key, "ring_slots")) return opt_ring_slots;
+  if (!strcmp(key, "pair_rows")) return opt_pair_rows;
   if (!strcmp(key, "comm_timeout_ms")) return opt_comm_timeout_ms;
   if (!strcmp(key, "comm_nonblocking")) return opt_comm_nonblocking;
   return -1;
@@ -1321,23 +1378,28 @@ extern "C" void b2g_tile_coord(int t, int num_m, int num_n, int group, int* tm, 
 extern "C" const char* b2g_version(void) { return "b2g_gemm 0.1 (sm_100a tcgen05)"; }
 
 extern "C" int b2g_plan_preview(int64_t M, int64_t N, int64_t K, int dtype, int sm_count, int* cg,
-                                int* bn, int* k_splits, int* num_full) {
+                                int* bn, int* k_splits, int* num_full, int* cta_rows) {
   if (M < 1 || N < 1 || K < 1 || sm_count < 2 || !cg || !bn || !k_splits || !num_full)
     return fail(B2G_ERR_INVALID_ARG, "bad plan-preview arguments");
   if (dtype < B2G_DTYPE_F16 || dtype > B2G_DTYPE_E5M2)
     return fail(B2G_ERR_INVALID_ARG, "unknown operand type code %d", dtype);
   const int64_t kb = dtype >= B2G_DTYPE_E4M3 ? 128 : 64;  // K elements per 128-byte stage row
   const int64_t nmt = (M + 127) / 128;
+  int half_opt = (int)opt_pair_rows.load();
+  if (half_opt == 0 && (!opt_cluster_fixup.load() || opt_serial_fixup.load() || opt_split_k.load() > 4))
+    half_opt = 128;
   const TileChoice t = choose_tiles(nmt, N, (K + kb - 1) / kb, sm_count, (int)opt_cta_group.load(),
-                                    (int)opt_tile_n.load());
-  const int64_t tiles = ((nmt + t.cg - 1) / t.cg) * ((N + t.bn - 1) / t.bn);
+                                    (int)opt_tile_n.load(), half_opt);
+  const int64_t rows = t.half ? 64 : 128;
+  const int64_t tiles = ((((M + rows - 1) / rows) + t.cg - 1) / t.cg) * ((N + t.bn - 1) / t.bn);
   if (tiles > INT32_MAX / 4) return fail(B2G_ERR_UNSUPPORTED, "too many tiles");
   const int group_cap = t.cg == 1 ? sm_count : sm_count / 2;  // CTA pairs: full occupancy assumed
   const SplitChoice s = choose_splits((int)tiles, (int)((K + kb - 1) / kb), group_cap, t.cg,
-                                      (int)opt_split_k.load(), opt_tail_split.load() != 0);
+                                      (int)opt_split_k.load(), opt_tail_split.load() != 0, t.half);
   *cg = t.cg;
   *bn = t.bn;
   *k_splits = s.k_splits;
   *num_full = s.num_full;
+  if (cta_rows) *cta_rows = (int)rows;
   return B2G_OK;
 }

@@ -105,20 +105,29 @@ constexpr uint32_t kCBuf = 32 * 32 * 4;  // one 32x32 fp32 staging buffer
 constexpr uint32_t kSmemLimit = 232448;  // max dynamic shared memory per CTA on sm_100
 
 // CG: CTAs per tile (1, or 2 = cta_group::2 pair).  BN: tile width in columns (128, 256 or
-// 512); a tile is (128*CG) x BN.  BN <= 256 keeps two accumulators in TMEM (the epilogue of
+// 512); a tile is (BMC*CG) x BN.  BN <= 256 keeps two accumulators in TMEM (the epilogue of
 // tile t overlaps the main loop of tile t+1); BN = 512 fills TMEM with one accumulator and cuts
 // the operand bytes each CTA pulls from L2 per FLOP by a quarter; BN = 128 (one CTA only)
 // gives small problems four times as many tiles as the 256x512 pair tile.
-template <int CG, int BN>
+// BMC: A rows per CTA.  128, or 64 for the half-height pair tile (CG = 2, BN = 256: a 128 x 256
+// tile, UMMA M = 128 over the pair).  That accumulator is folded into the TMEM of each CTA:
+// its 64 rows x 256 columns sit in 128 lanes x 128 columns, columns [0, 128) of the tile in
+// lanes 0-63 and columns [128, 256) in lanes 64-127 (the "2x2" data-path layout of M = 128
+// with cta_group::2).  It halves the partial tile a CTA holds when K is split, which is what
+// bounds the split-K reduction of skinny problems.
+template <int CG, int BN, int BMC = kBM>
 struct Cfg {
   static_assert(CG == 1 || CG == 2, "CTA group");
   static_assert(BN == 256 || BN == 512 || (BN == 128 && CG == 1), "tile width");
+  static_assert(BMC == kBM || (BMC == 64 && CG == 2 && BN == 256), "half-height pair tile");
   static constexpr int UN = BN < kUN ? BN : kUN;      // N of one UMMA instruction
   static constexpr int NH = BN / UN;                  // UMMA N-halves per k step
-  static constexpr int ACC_BUFS = BN <= 256 ? 2 : 1;  // accumulators held in TMEM
+  static constexpr int ACC_COLS = BMC == kBM ? BN : BN / 2;  // TMEM columns of one accumulator
+  static constexpr int UN_COLS = BMC == kBM ? UN : UN / 2;   // TMEM columns written by one UMMA
+  static constexpr int ACC_BUFS = ACC_COLS <= 256 ? 2 : 1;   // accumulators held in TMEM
   static constexpr int BPH = UN / CG;                 // B columns per N-half held by one CTA
   static constexpr int BN_CTA = BN / CG;              // B columns loaded per CTA
-  static constexpr uint32_t A_BYTES = kBM * kRowBytes;  // 16 KiB
+  static constexpr uint32_t A_BYTES = BMC * kRowBytes;  // 16 KiB (8 KiB for BMC = 64)
   static constexpr uint32_t B_BYTES = BN_CTA * kRowBytes;
   static constexpr uint32_t HALF_BYTES = BPH * kRowBytes;  // one N-half of B in shared memory
   static constexpr uint32_t EPI_BYTES = kEpiWarps * 2 * kCBuf;
@@ -134,15 +143,18 @@ struct Cfg {
   static constexpr uint32_t OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr uint32_t SMEM_BYTES = OFF_MISC + 16 + 1024;  // + alignment slack
   static constexpr uint32_t TX_BYTES = CG * (A_BYTES + B_BYTES);  // bytes per stage per group
-  static constexpr int CHUNKS = BN / 32;  // 32-column epilogue chunks per tile
+  static constexpr int CHUNKS = ACC_COLS / 32;  // 32-column epilogue chunks per warp and tile
+  static constexpr int WARP_COLS = ACC_COLS;     // tile columns one epilogue warp stores
 };
 
 static_assert(Cfg<1, 256>::SMEM_BYTES <= kSmemLimit && Cfg<1, 256>::STAGES >= 4, "CG=1 shared-memory fit");
 static_assert(Cfg<2, 256>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256>::STAGES >= 6, "CG=2 shared-memory fit");
 static_assert(Cfg<2, 512>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512>::STAGES >= 4, "BN=512 shared-memory fit");
 static_assert(Cfg<1, 128>::SMEM_BYTES <= kSmemLimit && Cfg<1, 128>::STAGES >= 6, "BN=128 shared-memory fit");
+static_assert(Cfg<2, 256, 64>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256, 64>::STAGES >= 8, "half-pair shared-memory fit");
 // the cluster fix-up keeps a CTA's 128 x BN fp32 partial in its (then idle) operand stages
-static_assert(Cfg<1, 128>::OFF_C >= 128u * 128u * 4u && Cfg<1, 256>::OFF_C >= 128u * 256u * 4u,
+static_assert(Cfg<1, 128>::OFF_C >= 128u * 128u * 4u && Cfg<1, 256>::OFF_C >= 128u * 256u * 4u &&
+                  Cfg<2, 256, 64>::OFF_C >= 64u * 256u * 4u,
               "partial tile fits in the operand stages");
 
 // Instruction descriptor (kind::f16 and kind::f8f6f4 share the layout): D fp32 (bit 4), A and
@@ -186,11 +198,11 @@ __device__ __forceinline__ void m_tile_origin(const GemmParams& p, int mt, int& 
 
 // ESZ: operand element size in bytes (2 = fp16/bf16 via kind::f16, 1 = fp8 via kind::f8f6f4).
 // A K block is 128 bytes of K (64 or 128 elements), consumed by 4 UMMAs of 32 bytes of K each.
-template <int CG, int BN, bool B_KMAJOR, bool C_MCONTIG, int ESZ>
+template <int CG, int BN, bool B_KMAJOR, bool C_MCONTIG, int ESZ, int BMC = kBM>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using C = Cfg<CG, BN>;
+  using C = Cfg<CG, BN, BMC>;
   constexpr int KB = kRowBytes / ESZ;                 // K elements per stage
   constexpr int ATOM = kRowBytes / ESZ;               // MN-major swizzle atom width (elements)
   constexpr uint32_t ATOM_BYTES = (uint32_t)kRowBytes * KB;  // one atom: ATOM x KB elements
@@ -203,7 +215,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t cta_rank = (CG == 2) ? ptx::cluster_ctarank() : 0u;
+  // CTA pairs are cluster ranks (2i, 2i+1); a cluster may hold several pairs (the cluster
+  // fix-up of half-height pair tiles).  pair0 is the cluster rank of this CTA's pair leader.
+  const uint32_t crank = (CG == 2 || p.cluster_fixup) ? ptx::cluster_ctarank() : 0u;
+  const uint32_t cta_rank = (CG == 2) ? (crank & 1u) : 0u;
+  const uint32_t pair0 = (CG == 2) ? (crank & ~1u) : 0u;
+  const uint16_t pair_mask = (uint16_t)(0x3u << pair0);
   const bool leader = (cta_rank == 0);
 
   auto full_bar = [&](int s) { return base + C::OFF_BAR + 8u * s; };
@@ -301,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          const uint32_t fb = (CG == 1) ? full_bar(s) : ptx::mapa(full_bar(s), 0);
+          const uint32_t fb = (CG == 1) ? full_bar(s) : ptx::mapa(full_bar(s), pair0);
           if (leader) ptx::mbar_arrive_expect_tx(full_bar(s), C::TX_BYTES);
           if (p.fault_flags & 1) continue;
           const int jj = kb / p.k_blocks_per_j;
@@ -327,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (leader && lane == 0) {
-      const uint32_t idesc = make_idesc(kBM * CG, C::UN, !B_KMAJOR, (uint32_t)p.ab_format);
+      const uint32_t idesc = make_idesc(BMC * CG, C::UN, !B_KMAJOR, (uint32_t)p.ab_format);
       int it = 0, tc = 0;
       bool ok = true;
       // Issue the MMAs of K block kb from stage s into N-halves [h_lo, h_hi).
@@ -343,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t bh = sb + (uint32_t)h * C::HALF_BYTES;
             const uint64_t bd = B_KMAJOR ? ptx::smem_desc_sw128(bh + 32u * k16, 16u, 1024u)
                                          : ptx::smem_desc_sw128(bh + MN_STEP * k16, ATOM_BYTES, 1024u);
-            ptx::umma<CG, ESZ>(d + (uint32_t)h * C::UN, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
+            ptx::umma<CG, ESZ>(d + (uint32_t)h * C::UN_COLS, ad, bd, idesc, (kb | k16) != 0 ? 1u : 0u);
           }
         }
       };
@@ -361,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)acc * C::UN;
+        const uint32_t d = tmem_base + (uint32_t)acc * C::ACC_COLS;
         int kb = 0;  // K block of this unit, relative to kb_lo
         if constexpr (C::NH == 2) {
           // Half 0 of every K block already in shared memory first, then wait for half 1 of
@@ -386,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k2 = 0; k2 < pro; ++k2) {
             const int s = (it + k2) % C::STAGES;
             issue_mma(d, s, k2, 1, 2);
-            ptx::umma_commit<CG>(empty_bar(s), (uint16_t)0x3);
+            ptx::umma_commit<CG>(empty_bar(s), pair_mask);
           }
           it += pro;
         }
@@ -399,21 +416,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           ptx::tc_fence_after();
           issue_mma(d, s, kb, 0, C::NH);
-          ptx::umma_commit<CG>(empty_bar(s), (uint16_t)0x3);
+          ptx::umma_commit<CG>(empty_bar(s), pair_mask);
         }
         if (!ok) break;
-        ptx::umma_commit<CG>(tfull_bar(acc), (uint16_t)0x3);
+        ptx::umma_commit<CG>(tfull_bar(acc), pair_mask);
       }
       // Teardown: all MMAs issued by this thread must finish before TMEM/shared memory go away.
-      ptx::umma_commit<CG>(mma_done_bar, (uint16_t)0x1);
+      ptx::umma_commit<CG>(mma_done_bar, (uint16_t)(0x1u << pair0));
       ptx::mbar_wait_drain(mma_done_bar, 0u, err, ERR_WAIT_DRAIN, lim);
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter
     const uint32_t cbuf = base + C::OFF_C + (uint32_t)(warp - 2) * 2u * kCBuf;
-    // This warp's 32-row sub-box inside the 128-row tile (flattened (a, b, i) order).
-    const int r0 = 32 * q;
+    // This warp's 32-row sub-box inside the CTA's BMC-row tile (flattened (a, b, i) order) and
+    // its columns: BMC = 128, all BN columns of rows 32q..32q+31; BMC = 64 (folded
+    // accumulator), columns [(q/2)*BN/2, (q/2+1)*BN/2) of rows 32(q%2)..32(q%2)+31.
+    const int r0 = BMC == kBM ? 32 * q : 32 * (q & 1);
+    const int col_off = BMC == kBM ? 0 : (q >> 1) * C::WARP_COLS;
     const int a_l = r0 / (p.bi * p.bb);
     const int b_l = (r0 / p.bi) % p.bb;
     const int i_l = r0 % p.bi;
@@ -433,8 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool got = ptx::mbar_wait(tfull_bar(acc), aph, abort_flag, err, ERR_WAIT_TFULL, lim);
       if (!__all_sync(0xffffffffu, got)) break;
       ptx::tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)acc * C::UN;
-      const int n0 = tn * BN;
+      const uint32_t tbase = tmem_base + ((uint32_t)(32 * q) << 16) + (uint32_t)acc * C::ACC_COLS;
+      const int n0 = tn * BN + col_off;
 
       // Stage chunk `ch` (32 columns of this warp's 32 rows) and TMA-store it.
       auto store_chunk = [&](const uint32_t (&v)[32], int ch) {
@@ -524,15 +544,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (CG == 1)
             ptx::mbar_arrive(tempty_bar(rel));
           else
-            ptx::mbar_arrive_cluster(tempty_bar(rel), 0);
+            ptx::mbar_arrive_cluster(tempty_bar(rel), pair0);
         }
       };
 
-      if (CG == 1 && ns > 1 && p.cluster_fixup) {
+      if ((CG == 1 || BMC != kBM) && ns > 1 && p.cluster_fixup) {
         // ---- cluster fix-up: partial tile -> this CTA's shared memory (the operand stages,
         // idle after its only unit's main loop) as float4 [chunk][warp][j][lane]; then split sp
-        // sums chunks sp, sp + ns, ... over the ns CTAs of the cluster (distributed shared
-        // memory, in split order) and stores them.  The split index is the CTA's cluster rank.
+        // sums chunks sp, sp + ns, ... over the ns CTAs of the cluster that hold the same rows
+        // (distributed shared memory, in split order) and stores them.  One-CTA tiles: split r
+        // is cluster rank r.  Half-height pairs: split r is the pair at cluster ranks 2r, 2r+1,
+        // and this CTA's counterpart in it is rank 2r + cta_rank.
+        auto split_cta = [&](int r) -> uint32_t {
+          return CG == 1 ? (uint32_t)r : (uint32_t)(2 * r) + cta_rank;
+        };
         const uint32_t part = base + (uint32_t)(q * 8 * 32 + lane) * 16u;
         ptx::fence_proxy_async_smem();
         uint32_t w0[32], w1[32];
@@ -559,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::named_barrier_sync(1, kEpiWarps * 32);
         volatile int* ready_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
         if (threadIdx.x == 64) {
-          for (int r = 0; r < ns; ++r) ptx::mbar_arrive_cluster(ready_bar, (uint32_t)r);
+          for (int r = 0; r < ns; ++r) ptx::mbar_arrive_cluster(ready_bar, split_cta(r));
           *ready_flag = ptx::mbar_wait_cluster(ready_bar, 0u, abort_flag, err, ERR_WAIT_FIXUP, lim)
                             ? 1 : 0;
         }
@@ -576,11 +601,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             float4 x[8], y[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              x[j] = ptx::ld_shared_cluster_v4(ptx::mapa(off, 0u) + (uint32_t)(j * 32) * 16u);
+              x[j] = ptx::ld_shared_cluster_v4(ptx::mapa(off, split_cta(0)) + (uint32_t)(j * 32) * 16u);
 #pragma unroll 1
             for (int r = 0; r < ns; ++r) {
               if (r + 1 < ns) {
-                const uint32_t src = ptx::mapa(off, (uint32_t)(r + 1));
+                const uint32_t src = ptx::mapa(off, split_cta(r + 1));
 #pragma unroll
                 for (int j = 0; j < 8; ++j) y[j] = ptx::ld_shared_cluster_v4(src + (uint32_t)(j * 32) * 16u);
               }
@@ -600,6 +625,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_chunk(vv, ch);
           }
         }
+        continue;
+      }
+      if (BMC != kBM && ns > 1) {
+        // half-height pair tiles split K only with the cluster fix-up (the launcher never
+        // plans otherwise); record the inconsistency and leave C untouched
+        if (lane == 0) atomicCAS(err, 0, ERR_WAIT_FIXUP);
+        release(acc);
         continue;
       }
       if (ns > 1) {

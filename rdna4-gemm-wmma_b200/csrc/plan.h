@@ -8,32 +8,60 @@
 namespace b2g {
 
 struct TileChoice {
-  int cg;  // CTAs per tile (1 or 2)
-  int bn;  // tile width in columns (128, 256 or 512)
+  int cg;    // CTAs per tile (1 or 2)
+  int bn;    // tile width in columns (128, 256 or 512)
+  bool half; // CG = 2 half-height pair tile: 128 x 256 over the pair, 64 A rows per CTA
 };
 
+// Split count of one-CTA (cg = 1) or half-height pair (half) tiles of a small problem: what
+// choose_splits gives when every tile is split (at least 16 K blocks per split, at most 8
+// one-CTA splits or 4 pair splits: the largest cluster of the cluster fix-up is 8 CTAs).
+inline int64_t small_splits(int64_t tiles, int64_t kit, int64_t groups, bool half) {
+  int64_t sp = std::min<int64_t>({groups / std::max<int64_t>(1, tiles), kit / 16, half ? 4 : 8});
+  if (2 * tiles > groups || kit < 32) sp = 1;
+  return std::max<int64_t>(1, sp);
+}
+
 // nmt: 128-row M tiles; kit: K blocks of one tile; sms: SMs; opt_cg / opt_bn: forced values
-// (0 = choose).
+// (0 = choose); opt_rows: 0 = choose, 64 = half-height pair tiles whenever the shape allows,
+// 128 = never.
 inline TileChoice choose_tiles(int64_t nmt, int64_t N, int64_t kit, int sms, int opt_cg,
-                               int opt_bn) {
+                               int opt_bn, int opt_rows = 0) {
   int cg = opt_cg, bn = opt_bn;
   if (bn == 128) cg = 1;  // the 128-column tile exists for one CTA only
+  const bool half_ok = opt_rows != 128 && (bn == 0 || bn == 256) && cg != 1;
+  if (opt_rows == 64 && half_ok) return {2, 256, true};
   if (cg != 1 && cg != 2) {
     // Small problems (fewer 128x256 tiles than SMs) take one-CTA tiles.  The width is the one
     // whose work units (tiles times the split count choose_splits would give) fill the SMs
     // best; on a tie the 128x256 tile, which moves a quarter fewer bytes per FLOP.
     if (bn == 0 && nmt * ((N + 255) / 256) < sms) {
       cg = 1;
-      auto fill = [&](int w) {
+      auto fill = [&](int w, int64_t* splits) {
         const int64_t tiles = nmt * ((N + w - 1) / w);
-        int64_t sp = std::min<int64_t>({(int64_t)sms / std::max<int64_t>(1, tiles), kit / 16, 8});
-        if (2 * tiles > sms || kit < 32) sp = 1;
-        sp = std::max<int64_t>(1, sp);
+        const int64_t sp = small_splits(tiles, kit, sms, false);
         const int64_t units = tiles * sp;
         const int64_t waves = (units + sms - 1) / sms;
+        *splits = sp;
         return (double)units / (double)(waves * sms);
       };
-      bn = fill(128) > fill(256) + 1e-9 ? 128 : 256;
+      int64_t sp128 = 1, sp256 = 1;
+      const double f128 = fill(128, &sp128), f256 = fill(256, &sp256);
+      bn = f128 > f256 + 1e-9 ? 128 : 256;
+      const int64_t sp1 = bn == 128 ? sp128 : sp256;
+      // When those one-CTA tiles split K, half-height pair tiles (128 x 256 over a CTA pair)
+      // that fill the SMs as well are taken instead: each CTA's partial tile is half as large
+      // and they need fewer splits (often none), so the split-K reduction moves far fewer
+      // bytes.
+      if (half_ok && sp1 > 1) {
+        const int64_t pairs = std::max(1, sms / 2);
+        const int64_t tiles = nmt * ((N + 255) / 256);
+        const int64_t sp = small_splits(tiles, kit, pairs, true);
+        const int64_t units = tiles * sp;
+        const int64_t waves = (units + pairs - 1) / pairs;
+        const double fh = (double)units / (double)(waves * pairs);
+        if (waves == 1 && fh + 1e-9 >= std::max(f128, f256)) return {2, 256, true};
+      }
     } else {
       cg = (nmt >= 2) ? 2 : 1;
     }
@@ -47,7 +75,7 @@ inline TileChoice choose_tiles(int64_t nmt, int64_t N, int64_t kit, int sms, int
   }
   if (cg == 1 && bn == 512) bn = 256;  // one CTA: at most 256 columns (two accumulators)
   if (cg == 2 && bn == 128) bn = 256;
-  return {cg, bn};
+  return {cg, bn, false};
 }
 
 struct SplitChoice {
@@ -57,9 +85,10 @@ struct SplitChoice {
 };
 
 // Split-K for under-filled grids and for the tail wave.  group_cap: CTA groups resident at
-// once (SMs, or CTA pairs); opt_split: forced split count (0 = choose).
+// once (SMs, or CTA pairs); opt_split: forced split count (0 = choose); half: half-height pair
+// tiles (at most 4 splits, and never a tail split: they split only with the cluster fix-up).
 inline SplitChoice choose_splits(int num_tiles, int k_iters, int group_cap, int cg, int opt_split,
-                                 bool tail_split) {
+                                 bool tail_split, bool half = false) {
   int splits = opt_split;
   int full = 0;
   if (splits <= 0) {
@@ -71,9 +100,11 @@ inline SplitChoice choose_splits(int num_tiles, int k_iters, int group_cap, int 
     // partial write, fix-up) outweighs the shorter main loop.  One-CTA tiles split at most 8
     // ways, the largest cluster of the cluster fix-up.
     if (2 * num_tiles <= group_cap && k_iters >= 32) {
-      splits = std::min({group_cap / std::max(1, num_tiles), k_iters / 16, cg == 1 ? 8 : 16});
+      splits = std::min({group_cap / std::max(1, num_tiles), k_iters / 16,
+                         half ? 4 : (cg == 1 ? 8 : 16)});
       full = 0;
-    } else if (tail_split && waves >= 1 && rem > 0 && group_cap / rem >= 2 && k_iters >= 32) {
+    } else if (!half && tail_split && waves >= 1 && rem > 0 && group_cap / rem >= 2 &&
+               k_iters >= 32) {
       // whole waves plus a partial one: split only the partial wave's tiles
       splits = std::min({group_cap / rem, 4, k_iters / 16});
       full = waves * group_cap;

@@ -31,10 +31,17 @@ def assert_close(orc, got, ref, K, max_a=1.0, max_b=1.0, what=""):
 # kernel variants of the tensor-core path: (CTAs per tile, tile width)
 VARIANTS = [(1, 128), (1, 256), (2, 256), (2, 512)]
 VARIANT_IDS = ["cta1_n128", "cta1_n256", "cta2_n256", "cta2_n512"]
+# ... plus the half-height pair tile (128 x 256 over a CTA pair, 64 A rows per CTA), which
+# options() below selects from the tile width "256h"
+VARIANTS_H = VARIANTS + [(2, "256h")]
+VARIANT_H_IDS = VARIANT_IDS + ["cta2_n256_half"]
 
 
 @contextlib.contextmanager
 def options(b2g, **kw):
+    if kw.get("tile_n") == "256h":
+        kw["tile_n"] = 256
+        kw["pair_rows"] = 64
     old = {k: b2g.get_option(k) for k in kw}
     try:
         for k, v in kw.items():

@@ -166,9 +166,9 @@ int main() {
     ((8192, 4096, 8192), (2, 512, 2, 222)),         # configs[2] GEMM view: tail wave split 2 ways
     ((8192, 28672, 8192), (2, 512, 4, 1776)),       # configs[3]: 16 tail tiles split 4 ways
     ((16384, 16384, 4096), (2, 512, 1, 2048)),      # configs[3]: whole waves
-    ((128, 8192, 8192), (1, 256, 4, 0)),            # configs[3] skinny: 32 tiles x 4 splits
+    ((128, 8192, 8192), (2, 256, 2, 0)),            # configs[3] skinny: 32 half-height pair tiles x 2 splits
     ((1024, 1024, 1024), (1, 128, 1, 64)),          # configs[0]: 64 tiles, K too short to split
-    ((256, 8192, 8192), (1, 256, 2, 0)),
+    ((256, 8192, 8192), (2, 256, 1, 64)),           # 64 half-height pair tiles, no split
     ((128, 2048, 8192), (1, 128, 8, 0)),
     ((2048, 2048, 2048), (1, 256, 1, 128)),
 ])
@@ -176,6 +176,23 @@ def test_plan_preview_choices(b2g, shape, plan):
     """The launch plan for the BASELINE shapes and the small shapes whose choice was measured
     (the width whose split units fill the SMs best; ties to 128x256)."""
     assert b2g.plan_preview(*shape) == plan
+
+
+@pytest.mark.parametrize("shape,rows", [((128, 8192, 8192), 64), ((256, 8192, 8192), 64),
+                                        ((8192, 8192, 8192), 128), ((128, 2048, 8192), 128),
+                                        ((1024, 1024, 1024), 128)])
+def test_plan_preview_half_height_pairs(b2g, shape, rows):
+    """Skinny shapes whose one-CTA tiles would split K take half-height pair tiles (64 A rows
+    per CTA); the option pair_rows=128 turns them off, and options that rule out the cluster
+    fix-up (which they need to split K) keep the planner from choosing them."""
+    from gpu_util import options
+    assert b2g.plan_preview(*shape, rows=True)[4] == rows
+    with options(b2g, pair_rows=128):
+        assert b2g.plan_preview(*shape, rows=True)[4] == 128
+    with options(b2g, cluster_fixup=0):
+        assert b2g.plan_preview(*shape, rows=True)[4] == 128
+    with options(b2g, pair_rows=64):
+        assert b2g.plan_preview(*shape, rows=True)[:2] + (b2g.plan_preview(*shape, rows=True)[4],) == (2, 256, 64)
 
 
 def test_plan_preview_follows_options(b2g):
@@ -199,13 +216,16 @@ def test_plan_preview_invariants(b2g):
     @given(M=st.integers(1, 40000), N=st.integers(1, 40000), K=st.integers(1, 70000),
            dtype=st.sampled_from([0, 1, 2, 3]), sms=st.sampled_from([148, 132, 74, 16, 2]))
     def check(M, N, K, dtype, sms):
-        cg, bn, splits, full = b2g.plan_preview(M, N, K, dtype, sms)
-        assert cg in (1, 2) and bn in (128, 256, 512)
+        cg, bn, splits, full, rows = b2g.plan_preview(M, N, K, dtype, sms, rows=True)
+        assert cg in (1, 2) and bn in (128, 256, 512) and rows in (64, 128)
         assert not (cg == 1 and bn == 512) and not (bn == 128 and cg == 2)
+        assert rows == 128 or (cg == 2 and bn == 256)
         esz = 2 if dtype < 2 else 1
         k_iters = -(-K * esz // 128)  # a K block is 128 bytes of K
-        tiles = -(-(-(-M // 128)) // cg) * -(-N // bn)
-        assert 1 <= splits <= (8 if cg == 1 else 16)
+        tiles = -(-(-(-M // rows)) // cg) * -(-N // bn)
+        # half-height pairs split only through the cluster fix-up: at most 4 splits, no tail
+        assert 1 <= splits <= (4 if rows == 64 else 8 if cg == 1 else 16)
+        assert rows == 128 or splits == 1 or full == 0
         assert splits <= max(1, k_iters)
         assert 0 <= full <= tiles
         if splits == 1:

@@ -12,7 +12,7 @@ Tolerance: |C - R| <= 1e-3*sqrt(K)*max|a|*max|b| + 1e-3*|R| against the FP64 ora
 import numpy as np
 import pytest
 
-from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, to_dev
+from gpu_util import VARIANT_H_IDS, VARIANTS_H, assert_close, options, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -47,7 +47,7 @@ def _contract(b2g, torch, orc, a_shape, a_order, n, c_order, b_kmajor=False, see
     return path
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 def test_contract_baseline_form_small(b2g, cuda, orc, cg, tn):
     """BASELINE configs[2] layout at reduced size: coalesces to a plain 2-D GEMM view."""
     with options(b2g, cta_group=cg, tile_n=tn):
@@ -55,7 +55,7 @@ def test_contract_baseline_form_small(b2g, cuda, orc, cg, tn):
     assert path in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 def test_contract_permuted_memory_not_coalescible(b2g, cuda, orc, cg, tn):
     """A stored as [b][a][i][j][k] and C as [b][a][i][n]: the M modes cannot be merged, so the
     load box spans (i, b, a) of a rank-5 tensor map and the store box spans three modes."""
@@ -64,7 +64,7 @@ def test_contract_permuted_memory_not_coalescible(b2g, cuda, orc, cg, tn):
     assert path in (b2g.PATH_TC_1CTA, b2g.PATH_TC_2CTA)
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 def test_contract_ragged_k_mode(b2g, cuda, orc, cg, tn):
     """A stored [b][a][j][i][k], so neither the K modes (j, k) nor the M modes (b, i) merge;
     k = 96 is not a multiple of the 64-wide K block: each j visits two K blocks, the second
@@ -97,7 +97,7 @@ def _reference_form(b2g, torch, orc, mt, rt, nt, rt_l, bt, seed=9):
     return path
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 def test_contract_reference_form_small(b2g, cuda, orc, cg, tn):
     """rt=8, mt=16, nt=4, rt_l=64, bt=256: K-major B and an M-contiguous output (8-row
     store boxes)."""

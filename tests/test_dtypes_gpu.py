@@ -9,7 +9,7 @@ the exact operand values.
 import numpy as np
 import pytest
 
-from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, to_dev
+from gpu_util import VARIANT_H_IDS, VARIANTS_H, assert_close, options, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -45,7 +45,7 @@ def test_fill_uniform_typed_matches_oracle(b2g, cuda, orc, dt):
     assert np.array_equal(d.cpu().numpy().view(host.dtype), host)
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 @pytest.mark.parametrize("dt", DTYPES, ids=DT_IDS)
 @pytest.mark.parametrize("MNK", [(256, 512, 512), (384, 1024, 1152), (200, 272, 208)])
 def test_gemm_typed(b2g, cuda, orc, cg, tn, dt, MNK):

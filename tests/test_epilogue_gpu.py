@@ -8,7 +8,7 @@ beta*C term, far below it) against an FP64 reference R.
 import numpy as np
 import pytest
 
-from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, to_dev
+from gpu_util import VARIANT_H_IDS, VARIANTS_H, assert_close, options, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -18,7 +18,7 @@ def _inputs(orc, M, N, K, seed=31):
         orc.uniform_f16((M, N), seed + 2).astype(np.float32)
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 @pytest.mark.parametrize("alpha,beta", [(2.0, 0.0), (1.0, 1.0), (-0.5, 1.0), (1.5, 0.25)])
 def test_gemm_alpha_beta(b2g, cuda, orc, cg, tn, alpha, beta):
     torch = cuda

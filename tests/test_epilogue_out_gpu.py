@@ -10,7 +10,7 @@ nearest even, so its tolerance adds the output type's unit roundoff u to the rel
 import numpy as np
 import pytest
 
-from gpu_util import VARIANT_IDS, VARIANTS, options, to_dev
+from gpu_util import VARIANT_H_IDS, VARIANTS_H, options, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -46,7 +46,7 @@ def _check(orc, got, ref, K, alpha, c_dtype, what):
         what, int(bad.sum()), float(np.nanmax(err)), np.argwhere(bad)[0].tolist())
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 @pytest.mark.parametrize("c_dtype", [F32, F16, BF16], ids=["f32", "f16", "bf16"])
 def test_bias_and_output_type(b2g, cuda, orc, cg, tn, c_dtype):
     torch = cuda

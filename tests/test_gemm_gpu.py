@@ -8,7 +8,7 @@ Inputs: seeded U[-1,1] fp16 (max|a| = max|b| = 1).
 import numpy as np
 import pytest
 
-from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, padded_f16, to_dev
+from gpu_util import VARIANT_H_IDS, VARIANTS_H, assert_close, options, padded_f16, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -37,7 +37,7 @@ def test_fill_uniform_matches_oracle(b2g, cuda, orc):
     assert np.array_equal(d.cpu().numpy().view(np.uint16), host.view(np.uint16))
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 @pytest.mark.parametrize("MNK", [(128, 256, 64), (256, 256, 128), (512, 768, 320), (1024, 1024, 1024)])
 def test_gemm_tile_multiples(b2g, cuda, orc, cg, tn, MNK):
     M, N, K = MNK
@@ -47,7 +47,7 @@ def test_gemm_tile_multiples(b2g, cuda, orc, cg, tn, MNK):
     assert_close(orc, C, orc.gemm_f64(A, B), K, what="%s cg=%d" % (MNK, cg))
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 @pytest.mark.parametrize("MNK", [(1, 8, 8), (127, 129, 136), (129, 127, 1000), (1000, 1000, 8),
                                  (300, 40, 72), (8, 520, 64), (385, 264, 4104)])
 def test_gemm_ragged_aligned_pitch(b2g, cuda, orc, cg, tn, MNK):
@@ -71,7 +71,7 @@ def test_gemm_unaligned_runs_generic_bit_exact(b2g, cuda, orc, MNK):
     assert np.array_equal(C.view(np.uint32), ref.view(np.uint32))
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 def test_gemm_single_element(b2g, cuda, orc, cg, tn):
     """M = N = K = 1: every mode has extent 1, so the TMA path takes it (boxes larger than
     the tensor, zero-filled loads, clipped store)."""

@@ -12,7 +12,7 @@ import os
 import numpy as np
 import pytest
 
-from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, to_dev
+from gpu_util import VARIANT_H_IDS, VARIANTS_H, assert_close, options, to_dev
 
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
@@ -30,7 +30,7 @@ def _padded(torch, X, ld):
     return to_dev(torch, P)
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 def test_golden_gemm_tensor_core_path(b2g, cuda, orc, cg, tn):
     torch = cuda
     r8 = lambda x: (x + 7) // 8 * 8
@@ -77,7 +77,7 @@ def _ref_contraction(b2g, torch, force_generic):
     return z, dOut.cpu().numpy(), b2g.last_path(), nt * rt_l
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_H, ids=VARIANT_H_IDS)
 def test_golden_reference_contraction_tensor_core(b2g, cuda, orc, cg, tn):
     with options(b2g, cta_group=cg, tile_n=tn):
         z, out, path, K = _ref_contraction(b2g, cuda, 0)

@@ -234,3 +234,77 @@ def test_split_k_counter_ring_wraps_across_streams(b2g, cuda, orc):
     A = orc.uniform_f16((M, K), 93)
     B = orc.uniform_f16((K, N), 94)
     assert_close(orc, ref.cpu().numpy(), orc.gemm_f64(A, B), K)
+
+
+@pytest.mark.parametrize("splits", [2, 3, 4])
+@pytest.mark.parametrize("MNK", [(128, 1024, 4096), (100, 520, 3000), (256, 768, 2240),
+                                 (64, 256, 8192)])
+def test_half_pair_split_cluster_fixup(b2g, cuda, orc, splits, MNK):
+    """Half-height pair tiles (128 x 256 over a CTA pair, 64 A rows per CTA) with K split 2-4
+    ways: the splits of a tile are consecutive CTA pairs of one cluster, and each CTA sums its
+    counterparts' partials (same rows, other splits) through distributed shared memory in
+    split order.  Correct, and identical bits on a second call.  64 x 256 x 8192 leaves the
+    second CTA of every pair without rows."""
+    torch = cuda
+    M, N, K = MNK
+    r8 = lambda x: (x + 7) // 8 * 8
+    A = orc.uniform_f16((M, K), 81)
+    B = orc.uniform_f16((K, N), 82)
+    Ap = np.zeros((M, r8(K)), np.float16)
+    Ap[:, :K] = A
+    Bp = np.zeros((K, r8(N)), np.float16)
+    Bp[:, :N] = B
+    dA, dB = to_dev(torch, Ap), to_dev(torch, Bp)
+    outs = []
+    with options(b2g, pair_rows=64, split_k=splits):
+        for _ in range(2):
+            dC = torch.full((M, r8(N)), float("nan"), dtype=torch.float32, device="cuda")
+            b2g.gemm(dA, dB, dC, M, N, K, lda=r8(K), ldb=r8(N), ldc=r8(N))
+            torch.cuda.synchronize()
+            assert b2g.device_status() == 0
+            assert b2g.last_path() == b2g.PATH_TC_2CTA
+            assert b2g.get_option("last_split_ws_bytes") == 0  # no global workspace
+            outs.append(dC[:, :N].clone())
+    assert torch.equal(outs[0], outs[1])
+    assert_close(orc, outs[0].cpu().numpy(), orc.gemm_f64(A, B), K, what="split %d" % splits)
+
+
+def test_half_pair_refuses_a_split_it_cannot_reduce(b2g, cuda):
+    """Forced half-height pair tiles split K only through the cluster fix-up (at most 4
+    splits): a forced 5-way split, or the cluster fix-up turned off, is refused."""
+    torch = cuda
+    M, N, K = 128, 1024, 8192
+    dA = torch.zeros((M, K), dtype=torch.float16, device="cuda")
+    dB = torch.zeros((K, N), dtype=torch.float16, device="cuda")
+    dC = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    for kw in (dict(split_k=5), dict(split_k=2, cluster_fixup=0)):
+        with options(b2g, pair_rows=64, **kw):
+            with pytest.raises(b2g.B2GError) as e:
+                b2g.gemm(dA, dB, dC, M, N, K)
+        assert e.value.code == b2g.ERR_UNSUPPORTED
+
+
+def test_skinny_auto_plan_uses_half_pairs_and_agrees(b2g, cuda, orc):
+    """BASELINE configs[3] 128 x 8192 x 8192: the default plan takes half-height pair tiles
+    split 2 ways; it agrees with the one-CTA plan (pair_rows=128, K split 4) within tolerance,
+    and both with the oracle on sampled rows."""
+    torch = cuda
+    M, N, K = 128, 8192, 8192
+    assert b2g.plan_preview(M, N, K, rows=True) == (2, 256, 2, 0, 64)
+    dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+    dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+    b2g.fill_uniform(dA, M * K, 83)
+    b2g.fill_uniform(dB, K * N, 84)
+    res = {}
+    for rows in (0, 128):
+        with options(b2g, pair_rows=rows):
+            dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+            b2g.gemm(dA, dB, dC, M, N, K)
+            torch.cuda.synchronize()
+            assert b2g.device_status() == 0
+            res[rows] = dC
+    assert_close(orc, res[0].cpu().numpy(), res[128].cpu().numpy().astype(np.float64), K)
+    B = orc.uniform_f16((K, N), 84)
+    for r in (0, 31, 32, 63, 64, 100, 127):
+        a = orc.uniform_f16((1, K), 83, r * K)
+        assert_close(orc, res[0][r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, what="row %d" % r)
