@@ -364,11 +364,10 @@ int b2g_device_status(int clear);
  *   "force_generic" 1 = run the generic kernel for every call (testing)
  *   "tile_n"       0 = choose by shape (default); 128 (one CTA, 128x128 tiles), 256 or 512
  *                  columns per tile (512 needs CTA pairs)
- *   "pair_rows"    0 = choose by shape (default); 64 = half-height pair tiles (128 x 256 over a
- *                  CTA pair, UMMA M = 128 with cta_group::2, 64 A rows per CTA) whenever the
- *                  call allows them; 128 = never.  The planner takes them for skinny shapes
- *                  whose one-CTA tiles would split K: each CTA's partial tile is half as
- *                  large and fewer splits are needed
+ *   "pair_rows"    64 = half-height pair tiles (128 x 256 over a CTA pair, UMMA M = 128 with
+ *                  cta_group::2, 64 A rows per CTA) whenever the call allows them; 0 (default)
+ *                  or 128 = the planner's tiles, which never include them (measured slower on
+ *                  the skinny shapes they were built for)
  *   "split_k"      0 = choose by shape (default), else split every tile's K this many ways
  *   "tail_split"   1 (default) = split only the tiles of a partial last wave; 0 = never
  *   "serial_fixup" 1 = split-K partials are always summed by the last unit to arrive

@@ -23,13 +23,14 @@ inline int64_t small_splits(int64_t tiles, int64_t kit, int64_t groups, bool hal
 }
 
 // nmt: 128-row M tiles; kit: K blocks of one tile; sms: SMs; opt_cg / opt_bn: forced values
-// (0 = choose); opt_rows: 0 = choose, 64 = half-height pair tiles whenever the shape allows,
-// 128 = never.
+// (0 = choose); opt_rows: 64 = half-height pair tiles whenever the shape allows, 0 or 128 =
+// never (the planner does not choose them: measured on B200 they stream B more slowly than
+// one-CTA tiles on every skinny shape tried, although their split-K reduction is smaller).
 inline TileChoice choose_tiles(int64_t nmt, int64_t N, int64_t kit, int sms, int opt_cg,
                                int opt_bn, int opt_rows = 0) {
   int cg = opt_cg, bn = opt_bn;
   if (bn == 128) cg = 1;  // the 128-column tile exists for one CTA only
-  const bool half_ok = opt_rows != 128 && (bn == 0 || bn == 256) && cg != 1;
+  const bool half_ok = (bn == 0 || bn == 256) && cg != 1;
   if (opt_rows == 64 && half_ok) return {2, 256, true};
   if (cg != 1 && cg != 2) {
     // Small problems (fewer 128x256 tiles than SMs) take one-CTA tiles.  The width is the one
@@ -48,20 +49,6 @@ inline TileChoice choose_tiles(int64_t nmt, int64_t N, int64_t kit, int sms, int
       int64_t sp128 = 1, sp256 = 1;
       const double f128 = fill(128, &sp128), f256 = fill(256, &sp256);
       bn = f128 > f256 + 1e-9 ? 128 : 256;
-      const int64_t sp1 = bn == 128 ? sp128 : sp256;
-      // When those one-CTA tiles split K, half-height pair tiles (128 x 256 over a CTA pair)
-      // that fill the SMs as well are taken instead: each CTA's partial tile is half as large
-      // and they need fewer splits (often none), so the split-K reduction moves far fewer
-      // bytes.
-      if (half_ok && sp1 > 1) {
-        const int64_t pairs = std::max(1, sms / 2);
-        const int64_t tiles = nmt * ((N + 255) / 256);
-        const int64_t sp = small_splits(tiles, kit, pairs, true);
-        const int64_t units = tiles * sp;
-        const int64_t waves = (units + pairs - 1) / pairs;
-        const double fh = (double)units / (double)(waves * pairs);
-        if (waves == 1 && fh + 1e-9 >= std::max(f128, f256)) return {2, 256, true};
-      }
     } else {
       cg = (nmt >= 2) ? 2 : 1;
     }

@@ -166,9 +166,9 @@ int main() {
     ((8192, 4096, 8192), (2, 512, 2, 222)),         # configs[2] GEMM view: tail wave split 2 ways
     ((8192, 28672, 8192), (2, 512, 4, 1776)),       # configs[3]: 16 tail tiles split 4 ways
     ((16384, 16384, 4096), (2, 512, 1, 2048)),      # configs[3]: whole waves
-    ((128, 8192, 8192), (2, 256, 2, 0)),            # configs[3] skinny: 32 half-height pair tiles x 2 splits
+    ((128, 8192, 8192), (1, 256, 4, 0)),            # configs[3] skinny: 32 tiles x 4 splits
     ((1024, 1024, 1024), (1, 128, 1, 64)),          # configs[0]: 64 tiles, K too short to split
-    ((256, 8192, 8192), (2, 256, 1, 64)),           # 64 half-height pair tiles, no split
+    ((256, 8192, 8192), (1, 256, 2, 0)),
     ((128, 2048, 8192), (1, 128, 8, 0)),
     ((2048, 2048, 2048), (1, 256, 1, 128)),
 ])
@@ -178,21 +178,18 @@ def test_plan_preview_choices(b2g, shape, plan):
     assert b2g.plan_preview(*shape) == plan
 
 
-@pytest.mark.parametrize("shape,rows", [((128, 8192, 8192), 64), ((256, 8192, 8192), 64),
-                                        ((8192, 8192, 8192), 128), ((128, 2048, 8192), 128),
-                                        ((1024, 1024, 1024), 128)])
-def test_plan_preview_half_height_pairs(b2g, shape, rows):
-    """Skinny shapes whose one-CTA tiles would split K take half-height pair tiles (64 A rows
-    per CTA); the option pair_rows=128 turns them off, and options that rule out the cluster
-    fix-up (which they need to split K) keep the planner from choosing them."""
+@pytest.mark.parametrize("shape", [(128, 8192, 8192), (256, 8192, 8192), (8192, 8192, 8192),
+                                   (128, 2048, 8192), (1024, 1024, 1024)])
+def test_plan_preview_half_height_pairs_only_when_forced(b2g, shape):
+    """The planner never chooses half-height pair tiles (64 A rows per CTA); pair_rows=64
+    forces them (CTA pairs, 256-wide tiles) unless the caller also forces one-CTA tiles."""
     from gpu_util import options
-    assert b2g.plan_preview(*shape, rows=True)[4] == rows
-    with options(b2g, pair_rows=128):
-        assert b2g.plan_preview(*shape, rows=True)[4] == 128
-    with options(b2g, cluster_fixup=0):
-        assert b2g.plan_preview(*shape, rows=True)[4] == 128
+    assert b2g.plan_preview(*shape, rows=True)[4] == 128
     with options(b2g, pair_rows=64):
-        assert b2g.plan_preview(*shape, rows=True)[:2] + (b2g.plan_preview(*shape, rows=True)[4],) == (2, 256, 64)
+        cg, bn, _, _, rows = b2g.plan_preview(*shape, rows=True)
+        assert (cg, bn, rows) == (2, 256, 64)
+    with options(b2g, pair_rows=64, cta_group=1):
+        assert b2g.plan_preview(*shape, rows=True)[4] == 128
 
 
 def test_plan_preview_follows_options(b2g):

@@ -284,27 +284,29 @@ def test_half_pair_refuses_a_split_it_cannot_reduce(b2g, cuda):
         assert e.value.code == b2g.ERR_UNSUPPORTED
 
 
-def test_skinny_auto_plan_uses_half_pairs_and_agrees(b2g, cuda, orc):
-    """BASELINE configs[3] 128 x 8192 x 8192: the default plan takes half-height pair tiles
-    split 2 ways; it agrees with the one-CTA plan (pair_rows=128, K split 4) within tolerance,
-    and both with the oracle on sampled rows."""
+def test_skinny_half_pairs_agree_with_the_default_plan(b2g, cuda, orc):
+    """BASELINE configs[3] 128 x 8192 x 8192: forced half-height pair tiles (K split 2 ways)
+    agree with the default plan (one-CTA tiles, K split 4 ways) within tolerance, and both
+    with the oracle on sampled rows."""
     torch = cuda
     M, N, K = 128, 8192, 8192
-    assert b2g.plan_preview(M, N, K, rows=True) == (2, 256, 2, 0, 64)
+    assert b2g.plan_preview(M, N, K, rows=True) == (1, 256, 4, 0, 128)
     dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
     dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
     b2g.fill_uniform(dA, M * K, 83)
     b2g.fill_uniform(dB, K * N, 84)
     res = {}
-    for rows in (0, 128):
+    for rows in (0, 64):
         with options(b2g, pair_rows=rows):
             dC = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
             b2g.gemm(dA, dB, dC, M, N, K)
             torch.cuda.synchronize()
             assert b2g.device_status() == 0
             res[rows] = dC
-    assert_close(orc, res[0].cpu().numpy(), res[128].cpu().numpy().astype(np.float64), K)
+    assert_close(orc, res[64].cpu().numpy(), res[0].cpu().numpy().astype(np.float64), K)
     B = orc.uniform_f16((K, N), 84)
     for r in (0, 31, 32, 63, 64, 100, 127):
         a = orc.uniform_f16((1, K), 83, r * K)
-        assert_close(orc, res[0][r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, what="row %d" % r)
+        for rows in (0, 64):
+            assert_close(orc, res[rows][r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K,
+                         what="row %d pair_rows %d" % (r, rows))
