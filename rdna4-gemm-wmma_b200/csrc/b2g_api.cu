@@ -67,6 +67,7 @@ static std::atomic<int64_t> opt_split_k{0};  // 0 = choose by shape, else the sp
 static std::atomic<int64_t> opt_tail_split{1};  // split the tail wave's tiles (auto mode)
 static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream serialization
 static std::atomic<int64_t> opt_pair_rows{0};  // 0 = choose, 64 = half-height pair tiles, 128 = never
+static std::atomic<int64_t> opt_epi_warps{4};  // epilogue warps of the 256 x 512 pair tile (4 or 8)
 // Kernels this library has launched (every GEMM, scale and fill kernel), for callers that
 // count launches (b2g_get_option("launches")).
 static std::atomic<int64_t> g_launches{0};
@@ -149,11 +150,11 @@ static CUresult encode_cached(CUtensorMap* out, CUtensorMapDataType dt, cuuint32
 struct DevState {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
-  bool attr_set[2][5][2][2] = {};  // [fp8][variant][b_kmajor][c_mcontig]
-  int max_clusters[2][5][2][2] = {};
+  bool attr_set[2][6][2][2] = {};  // [fp8][variant][b_kmajor][c_mcontig]
+  int max_clusters[2][6][2][2] = {};
   // clusters of s split units resident at once (cluster fix-up): one-CTA tiles, or s CTA pairs
   // of half-height pair tiles
-  int max_clusters_cg1[2][5][2][2][9] = {};
+  int max_clusters_cg1[2][6][2][2][9] = {};
 };
 static std::mutex g_dev_mu;
 static DevState g_dev[64];
@@ -821,8 +822,11 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   // ---- launch
   using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
   const int bk = b_k ? 1 : 0, cm = c_m ? 1 : 0;
-  const int variant = tc.half ? 4 : cg == 1 ? (bn == 128 ? 3 : 0) : (bn == 256 ? 1 : 2);
-  static const KernFn table[2][5][2][2] = {
+  const int variant = tc.half ? 4
+                      : cg == 1 ? (bn == 128 ? 3 : 0)
+                      : bn == 256 ? 1
+                      : (opt_epi_warps.load() == 8 ? 5 : 2);
+  static const KernFn table[2][6][2][2] = {
       {{{gemm_tc_kernel<1, 256, false, false, 2>, gemm_tc_kernel<1, 256, false, true, 2>},
         {gemm_tc_kernel<1, 256, true, false, 2>, gemm_tc_kernel<1, 256, true, true, 2>}},
        {{gemm_tc_kernel<2, 256, false, false, 2>, gemm_tc_kernel<2, 256, false, true, 2>},
@@ -832,7 +836,9 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
        {{gemm_tc_kernel<1, 128, false, false, 2>, gemm_tc_kernel<1, 128, false, true, 2>},
         {gemm_tc_kernel<1, 128, true, false, 2>, gemm_tc_kernel<1, 128, true, true, 2>}},
        {{gemm_tc_kernel<2, 256, false, false, 2, 64>, gemm_tc_kernel<2, 256, false, true, 2, 64>},
-        {gemm_tc_kernel<2, 256, true, false, 2, 64>, gemm_tc_kernel<2, 256, true, true, 2, 64>}}},
+        {gemm_tc_kernel<2, 256, true, false, 2, 64>, gemm_tc_kernel<2, 256, true, true, 2, 64>}},
+       {{gemm_tc_kernel<2, 512, false, false, 2, 128, 8>, gemm_tc_kernel<2, 512, false, true, 2, 128, 8>},
+        {gemm_tc_kernel<2, 512, true, false, 2, 128, 8>, gemm_tc_kernel<2, 512, true, true, 2, 128, 8>}}},
       {{{gemm_tc_kernel<1, 256, false, false, 1>, gemm_tc_kernel<1, 256, false, true, 1>},
         {gemm_tc_kernel<1, 256, true, false, 1>, gemm_tc_kernel<1, 256, true, true, 1>}},
        {{gemm_tc_kernel<2, 256, false, false, 1>, gemm_tc_kernel<2, 256, false, true, 1>},
@@ -842,10 +848,16 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
        {{gemm_tc_kernel<1, 128, false, false, 1>, gemm_tc_kernel<1, 128, false, true, 1>},
         {gemm_tc_kernel<1, 128, true, false, 1>, gemm_tc_kernel<1, 128, true, true, 1>}},
        {{gemm_tc_kernel<2, 256, false, false, 1, 64>, gemm_tc_kernel<2, 256, false, true, 1, 64>},
-        {gemm_tc_kernel<2, 256, true, false, 1, 64>, gemm_tc_kernel<2, 256, true, true, 1, 64>}}}};
-  static const uint32_t smem_of[5] = {Cfg<1, 256>::SMEM_BYTES, Cfg<2, 256>::SMEM_BYTES,
+        {gemm_tc_kernel<2, 256, true, false, 1, 64>, gemm_tc_kernel<2, 256, true, true, 1, 64>}},
+       {{gemm_tc_kernel<2, 512, false, false, 1, 128, 8>, gemm_tc_kernel<2, 512, false, true, 1, 128, 8>},
+        {gemm_tc_kernel<2, 512, true, false, 1, 128, 8>, gemm_tc_kernel<2, 512, true, true, 1, 128, 8>}}}};
+  static const uint32_t smem_of[6] = {Cfg<1, 256>::SMEM_BYTES, Cfg<2, 256>::SMEM_BYTES,
                                       Cfg<2, 512>::SMEM_BYTES, Cfg<1, 128>::SMEM_BYTES,
-                                      Cfg<2, 256, 64>::SMEM_BYTES};
+                                      Cfg<2, 256, 64>::SMEM_BYTES, Cfg<2, 512, kBM, 8>::SMEM_BYTES};
+  static const int threads_of[6] = {Cfg<1, 256>::THREADS, Cfg<2, 256>::THREADS,
+                                    Cfg<2, 512>::THREADS, Cfg<1, 128>::THREADS,
+                                    Cfg<2, 256, 64>::THREADS, Cfg<2, 512, kBM, 8>::THREADS};
+  const int nthreads = threads_of[variant];
   const int e8 = esz == 1 ? 1 : 0;
   KernFn kern = table[e8][variant][bk][cm];
   const uint32_t smem = smem_of[variant];
@@ -862,7 +874,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
         qa[0].val.clusterDim.y = 1;
         qa[0].val.clusterDim.z = 1;
         qc.gridDim = dim3(2 * (ds->sm_count / 2), 1, 1);
-        qc.blockDim = dim3(kThreads, 1, 1);
+        qc.blockDim = dim3((unsigned)nthreads, 1, 1);
         qc.dynamicSmemBytes = smem;
         qc.attrs = qa;
         qc.numAttrs = 1;
@@ -918,7 +930,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
         qa[0].val.clusterDim.y = 1;
         qa[0].val.clusterDim.z = 1;
         qc.gridDim = dim3((unsigned)(cg * S * (ds->sm_count / (cg * S))), 1, 1);
-        qc.blockDim = dim3(kThreads, 1, 1);
+        qc.blockDim = dim3((unsigned)nthreads, 1, 1);
         qc.dynamicSmemBytes = smem;
         qc.attrs = qa;
         qc.numAttrs = 1;
@@ -1012,7 +1024,7 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
   cfg.gridDim = dim3((unsigned)(groups * cg), 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3((unsigned)nthreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
@@ -1333,6 +1345,9 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_comm_timeout_ms = value;
   } else if (!strcmp(key, "comm_nonblocking")) {
     opt_comm_nonblocking = value ? 1 : 0;
+  } else if (!strcmp(key, "epi_warps")) {
+    if (value != 4 && value != 8) return B2G_ERR_INVALID_ARG;
+    opt_epi_warps = value;
   } else if (!strcmp(key, "pair_rows")) {
     if (value != 0 && value != 64 && value != 128) return B2G_ERR_INVALID_ARG;
     opt_pair_rows = value;
@@ -1366,6 +1381,7 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "serial_fixup")) return opt_serial_fixup;
   if (!strcmp(key, "ring_slots")) return opt_ring_slots;
   if (!strcmp(key, "pair_rows")) return opt_pair_rows;
+  if (!strcmp(key, "epi_warps")) return opt_epi_warps;
   if (!strcmp(key, "comm_timeout_ms")) return opt_comm_timeout_ms;
   if (!strcmp(key, "comm_nonblocking")) return opt_comm_nonblocking;
   return -1;

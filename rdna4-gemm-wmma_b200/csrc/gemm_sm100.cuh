@@ -115,9 +115,14 @@ constexpr uint32_t kSmemLimit = 232448;  // max dynamic shared memory per CTA on
 // lanes 0-63 and columns [128, 256) in lanes 64-127 (the "2x2" data-path layout of M = 128
 // with cta_group::2).  It halves the partial tile a CTA holds when K is split, which is what
 // bounds the split-K reduction of skinny problems.
-template <int CG, int BN, int BMC = kBM>
+// EW: epilogue warps, 4, or 8 for the 256 x 512 pair tile.  With one accumulator filling TMEM
+// the MMA of the next tile waits for the epilogue to hand back each N-half.  Eight warps pull a
+// whole N-half into registers (each warp 32 rows x 128 columns) and hand it back before they
+// store it, instead of after storing 7/8 of it.
+template <int CG, int BN, int BMC = kBM, int EW = 4>
 struct Cfg {
   static_assert(CG == 1 || CG == 2, "CTA group");
+  static_assert(EW == 4 || (EW == 8 && CG == 2 && BN == 512 && BMC == kBM), "epilogue warps");
   static_assert(BN == 256 || BN == 512 || (BN == 128 && CG == 1), "tile width");
   static_assert(BMC == kBM || (BMC == 64 && CG == 2 && BN == 256), "half-height pair tile");
   static constexpr int UN = BN < kUN ? BN : kUN;      // N of one UMMA instruction
@@ -130,7 +135,10 @@ struct Cfg {
   static constexpr uint32_t A_BYTES = BMC * kRowBytes;  // 16 KiB (8 KiB for BMC = 64)
   static constexpr uint32_t B_BYTES = BN_CTA * kRowBytes;
   static constexpr uint32_t HALF_BYTES = BPH * kRowBytes;  // one N-half of B in shared memory
-  static constexpr uint32_t EPI_BYTES = kEpiWarps * 2 * kCBuf;
+  static constexpr int EPI_WARPS = EW;
+  static constexpr int EPI_BUFS = EW == 8 ? 1 : 2;  // 32x32 staging buffers per epilogue warp
+  static constexpr int THREADS = 64 + 32 * EW;
+  static constexpr uint32_t EPI_BYTES = EW * EPI_BUFS * kCBuf;
   static constexpr int NUM_BARS_FIXED = 2 + 2 + 1 + 1;
   static constexpr int STAGES =
       (int)((kSmemLimit - 1024 - EPI_BYTES - 256) / (A_BYTES + B_BYTES)) > 8
@@ -150,6 +158,8 @@ struct Cfg {
 static_assert(Cfg<1, 256>::SMEM_BYTES <= kSmemLimit && Cfg<1, 256>::STAGES >= 4, "CG=1 shared-memory fit");
 static_assert(Cfg<2, 256>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256>::STAGES >= 6, "CG=2 shared-memory fit");
 static_assert(Cfg<2, 512>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512>::STAGES >= 4, "BN=512 shared-memory fit");
+static_assert(Cfg<2, 512, kBM, 8>::SMEM_BYTES <= kSmemLimit && Cfg<2, 512, kBM, 8>::STAGES >= 4,
+              "BN=512 eight-warp shared-memory fit");
 static_assert(Cfg<1, 128>::SMEM_BYTES <= kSmemLimit && Cfg<1, 128>::STAGES >= 6, "BN=128 shared-memory fit");
 static_assert(Cfg<2, 256, 64>::SMEM_BYTES <= kSmemLimit && Cfg<2, 256, 64>::STAGES >= 8, "half-pair shared-memory fit");
 // the cluster fix-up keeps a CTA's 128 x BN fp32 partial in its (then idle) operand stages
@@ -198,11 +208,11 @@ __device__ __forceinline__ void m_tile_origin(const GemmParams& p, int mt, int& 
 
 // ESZ: operand element size in bytes (2 = fp16/bf16 via kind::f16, 1 = fp8 via kind::f8f6f4).
 // A K block is 128 bytes of K (64 or 128 elements), consumed by 4 UMMAs of 32 bytes of K each.
-template <int CG, int BN, bool B_KMAJOR, bool C_MCONTIG, int ESZ, int BMC = kBM>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int CG, int BN, bool B_KMAJOR, bool C_MCONTIG, int ESZ, int BMC = kBM, int EW = 4>
+__global__ void __launch_bounds__(Cfg<CG, BN, BMC, EW>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using C = Cfg<CG, BN, BMC>;
+  using C = Cfg<CG, BN, BMC, EW>;
   constexpr int KB = kRowBytes / ESZ;                 // K elements per stage
   constexpr int ATOM = kRowBytes / ESZ;               // MN-major swizzle atom width (elements)
   constexpr uint32_t ATOM_BYTES = (uint32_t)kRowBytes * KB;  // one atom: ATOM x KB elements
@@ -241,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(tfull_bar(a), 1);
-      ptx::mbar_init(tempty_bar(a), kEpiWarps * CG);
+      ptx::mbar_init(tempty_bar(a), C::EPI_WARPS * CG);
     }
     ptx::mbar_init(mma_done_bar, 1);
     ptx::mbar_init(ready_bar, p.cluster_fixup ? (uint32_t)p.k_splits : 1u);
@@ -428,7 +438,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter
-    const uint32_t cbuf = base + C::OFF_C + (uint32_t)(warp - 2) * 2u * kCBuf;
+    // EW = 8: warps 2-5 and 6-9 cover the four lane quarters twice; `part` picks the 128
+    // columns of each N-half this warp handles.  EW = 4: one warp per quarter, every column.
+    const int part = (warp - 2) >> 2;
+    auto mine = [&](int ch) { return C::EPI_WARPS == 4 || ((ch >> 2) & 1) == part; };
+    const uint32_t cbuf = base + C::OFF_C + (uint32_t)(warp - 2) * (uint32_t)C::EPI_BUFS * kCBuf;
     // This warp's 32-row sub-box inside the CTA's BMC-row tile (flattened (a, b, i) order) and
     // its columns: BMC = 128, all BN columns of rows 32q..32q+31; BMC = 64 (folded
     // accumulator), columns [(q/2)*BN/2, (q/2+1)*BN/2) of rows 32(q%2)..32(q%2)+31.
@@ -460,8 +474,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto store_chunk = [&](const uint32_t (&v)[32], int ch) {
         const int gcol = n0 + 32 * ch;
         if (!rows_valid || gcol >= p.n_size) return;
-        const uint32_t buf = cbuf + (uint32_t)(nstore & 1) * kCBuf;
-        if (lane == 0) ptx::bulk_wait_read<1>();
+        const uint32_t buf = cbuf + (uint32_t)(C::EPI_BUFS == 2 ? (nstore & 1) : 0) * kCBuf;
+        if (lane == 0) {
+          if constexpr (C::EPI_BUFS == 2)
+            ptx::bulk_wait_read<1>();
+          else
+            ptx::bulk_wait_read<0>();
+        }
         __syncwarp();
         uint32_t w[32];
 #pragma unroll
@@ -581,14 +600,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Publish: after the epilogue warps' barrier one thread arrives (release, cluster
         // scope) on the ready barrier of every CTA of the cluster, then waits (acquire) until
         // all ns partials of the tile are in place.
-        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        ptx::named_barrier_sync(1, C::EPI_WARPS * 32);
         volatile int* ready_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
         if (threadIdx.x == 64) {
           for (int r = 0; r < ns; ++r) ptx::mbar_arrive_cluster(ready_bar, split_cta(r));
           *ready_flag = ptx::mbar_wait_cluster(ready_bar, 0u, abort_flag, err, ERR_WAIT_FIXUP, lim)
                             ? 1 : 0;
         }
-        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        ptx::named_barrier_sync(1, C::EPI_WARPS * 32);
         if (*ready_flag) {
 #pragma unroll 1
           for (int ch = sp; ch < C::CHUNKS; ch += ns) {
@@ -642,26 +661,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         const size_t blk = (size_t)128 * BN;
         const int v = u - p.num_full;   // split unit index
         const int st = t - p.num_full;  // split tile index
-        float4* mine = reinterpret_cast<float4*>(p.ws + ((size_t)v * CG + cta_rank) * blk) +
-                       (size_t)q * 8 * 32 + lane;
+        float4* mine_ws = reinterpret_cast<float4*>(p.ws + ((size_t)v * CG + cta_rank) * blk) +
+                          (size_t)q * 8 * 32 + lane;
         uint32_t w0[32], w1[32];
+        if constexpr (C::EPI_WARPS == 8) {
+          // this warp's chunks only, two at a time (no loads in flight across iterations)
+#pragma unroll 1
+          for (int ch = 0; ch < C::CHUNKS; ch += 2) {
+            if (!mine(ch)) continue;
+            ptx::tmem_ld_32x32b_x32(tbase + 32u * ch, w0);
+            ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 1), w1);
+            ptx::tmem_ld_wait();
+            float4* d0 = mine_ws + (size_t)ch * 4 * 8 * 32;
+            float4* d1 = mine_ws + (size_t)(ch + 1) * 4 * 8 * 32;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              __stcg(d0 + 32 * j, make_float4(__uint_as_float(w0[4 * j]), __uint_as_float(w0[4 * j + 1]),
+                                              __uint_as_float(w0[4 * j + 2]), __uint_as_float(w0[4 * j + 3])));
+              __stcg(d1 + 32 * j, make_float4(__uint_as_float(w1[4 * j]), __uint_as_float(w1[4 * j + 1]),
+                                              __uint_as_float(w1[4 * j + 2]), __uint_as_float(w1[4 * j + 3])));
+            }
+          }
+        } else {
         ptx::tmem_ld_32x32b_x32(tbase, w0);
 #pragma unroll 1
         for (int ch = 0; ch < C::CHUNKS; ch += 2) {
           ptx::tmem_ld_wait();
           ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 1), w1);
-          float4* d0 = mine + (size_t)ch * 4 * 8 * 32;
+          float4* d0 = mine_ws + (size_t)ch * 4 * 8 * 32;
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             __stcg(d0 + 32 * j, make_float4(__uint_as_float(w0[4 * j]), __uint_as_float(w0[4 * j + 1]),
                                             __uint_as_float(w0[4 * j + 2]), __uint_as_float(w0[4 * j + 3])));
           ptx::tmem_ld_wait();
           if (ch + 2 < C::CHUNKS) ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 2), w0);
-          float4* d1 = mine + (size_t)(ch + 1) * 4 * 8 * 32;
+          float4* d1 = mine_ws + (size_t)(ch + 1) * 4 * 8 * 32;
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             __stcg(d1 + 32 * j, make_float4(__uint_as_float(w1[4 * j]), __uint_as_float(w1[4 * j + 1]),
                                             __uint_as_float(w1[4 * j + 2]), __uint_as_float(w1[4 * j + 3])));
+        }
         }
         if constexpr (C::ACC_BUFS == 2) {
           release(acc);
@@ -672,7 +711,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // One thread publishes the partial: the barrier orders the epilogue threads' stores
         // before its acq_rel (gpu scope) atomic, and its acquire, followed by the second
         // barrier, orders the siblings' partials before every thread's loads below.
-        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        ptx::named_barrier_sync(1, C::EPI_WARPS * 32);
         volatile int* last_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 8);
         int* ctr = p.counters + (size_t)st * CG + cta_rank;
         int ch_first = 0, ch_step = 1;
@@ -690,7 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (last) *ctr = 0;  // every split has arrived: ready for the next call
           *last_flag = last;
         }
-        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        ptx::named_barrier_sync(1, C::EPI_WARPS * 32);
         if (*last_flag) {
           const float4* tile4 = reinterpret_cast<const float4*>(
                                     p.ws + ((size_t)st * p.k_splits * CG + cta_rank) * blk) +
@@ -698,6 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const size_t split_stride = (size_t)CG * blk / 4;  // float4s between splits
 #pragma unroll 1
           for (int ch = ch_first; ch < C::CHUNKS; ch += ch_step) {
+            if (!mine(ch)) continue;
             const float4* src = tile4 + (size_t)ch * 4 * 8 * 32;
             float a[32];
 #pragma unroll
@@ -743,7 +783,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_chunk(vv, ch);
           }
         }
-        ptx::named_barrier_sync(1, kEpiWarps * 32);
+        ptx::named_barrier_sync(1, C::EPI_WARPS * 32);
         if (p.fixup_parallel && threadIdx.x == 64) {
           // done reading the partials; the last split to get here resets the counter
           if (ptx::atom_add_acq_rel_gpu(ctr, 1) == 2 * ns - 1) *ctr = 0;
@@ -751,6 +791,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
 
+      if constexpr (C::EPI_WARPS == 8) {
+        // N-half h: this warp's four chunks (h*8 + part*4 + c) into registers, hand the half
+        // back to the MMA warp as soon as all eight warps have loaded theirs, then store them.
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          const int ch0 = h * 8 + part * 4;
+          uint32_t v[4][32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch0 + c), v[c]);
+          ptx::tmem_ld_wait();
+          release(h);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) store_chunk(v[c], ch0 + c);
+        }
+        continue;
+      }
       // TMEM loads are software-pipelined: chunk ch+1 is in flight while chunk ch is stored.
       uint32_t v0[32], v1[32];
       ptx::tmem_ld_32x32b_x32(tbase, v0);

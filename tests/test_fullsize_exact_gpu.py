@@ -90,3 +90,15 @@ def test_contraction_full_size_exact(b2g, cuda):
     ref = torch.mm(A.reshape(8 * 16 * 64, 64 * 128).to(torch.float64),
                    B.reshape(64 * 128, 4096).to(torch.float64)).reshape(sc)
     assert int((C.to(torch.float64) != ref).sum().item()) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(8192, 8192, 8192), (8192, 28672, 8192), (8192, 4096, 8192)],
+                         ids=["configs1", "configs3_wide", "configs2_view"])
+@pytest.mark.parametrize("epi_warps", [4, 8])
+def test_gemm_full_size_exact_epilogue_warps(b2g, cuda, M, N, K, epi_warps):
+    """The 256 x 512 pair tile with four or eight epilogue warps (eight: each warp pulls 128
+    columns of an N-half into registers before storing them); 8192 x 28672 x 8192 and the
+    configs[2] GEMM view also split their tail wave over the global workspace.  Every element
+    exact."""
+    with options(b2g, epi_warps=epi_warps, tile_n=512):
+        assert _exact_gemm(b2g, cuda, M, N, K, seed=M + N + K + epi_warps) == 0

@@ -8,12 +8,12 @@ identical bits (this also shows the per-tile counters are reset for the next cal
 import numpy as np
 import pytest
 
-from gpu_util import VARIANT_IDS, VARIANTS, assert_close, options, to_dev
+from gpu_util import VARIANT_W8_IDS, VARIANTS_W8, assert_close, options, to_dev
 
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_W8, ids=VARIANT_W8_IDS)
 @pytest.mark.parametrize("splits", [2, 3, 5])
 def test_split_k_forced(b2g, cuda, orc, cg, tn, splits):
     torch = cuda
@@ -94,7 +94,7 @@ def test_split_k_auto_skinny(b2g, cuda, orc):
         assert_close(orc, dC[r:r + 1].cpu().numpy(), orc.gemm_f64(a, B), K, what="row %d" % r)
 
 
-@pytest.mark.parametrize("cg,tn", VARIANTS, ids=VARIANT_IDS)
+@pytest.mark.parametrize("cg,tn", VARIANTS_W8, ids=VARIANT_W8_IDS)
 def test_split_k_parallel_and_serial_fixup_agree(b2g, cuda, orc, cg, tn):
     """Both fix-up schedules sum the same partials in split order: identical bits."""
     torch = cuda
