@@ -364,6 +364,9 @@ int b2g_device_status(int clear);
  *   "force_generic" 1 = run the generic kernel for every call (testing)
  *   "tile_n"       0 = choose by shape (default); 128 (one CTA, 128x128 tiles), 256 or 512
  *                  columns per tile (512 needs CTA pairs)
+ *   "epi_warps"    8 (default) or 4: epilogue warps of the 256 x 512 CTA-pair tile.  With 8,
+ *                  each warp pulls 128 columns of an accumulator N-half into registers and
+ *                  hands the half back to the MMA before storing it
  *   "pair_rows"    64 = half-height pair tiles (128 x 256 over a CTA pair, UMMA M = 128 with
  *                  cta_group::2, 64 A rows per CTA) whenever the call allows them; 0 (default)
  *                  or 128 = the planner's tiles, which never include them (measured slower on

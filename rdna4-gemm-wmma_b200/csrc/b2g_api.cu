@@ -67,7 +67,7 @@ static std::atomic<int64_t> opt_split_k{0};  // 0 = choose by shape, else the sp
 static std::atomic<int64_t> opt_tail_split{1};  // split the tail wave's tiles (auto mode)
 static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream serialization
 static std::atomic<int64_t> opt_pair_rows{0};  // 0 = choose, 64 = half-height pair tiles, 128 = never
-static std::atomic<int64_t> opt_epi_warps{4};  // epilogue warps of the 256 x 512 pair tile (4 or 8)
+static std::atomic<int64_t> opt_epi_warps{8};  // epilogue warps of the 256 x 512 pair tile (4 or 8)
 // Kernels this library has launched (every GEMM, scale and fill kernel), for callers that
 // count launches (b2g_get_option("launches")).
 static std::atomic<int64_t> g_launches{0};
