@@ -364,9 +364,6 @@ int b2g_device_status(int clear);
  *   "force_generic" 1 = run the generic kernel for every call (testing)
  *   "tile_n"       0 = choose by shape (default); 128 (one CTA, 128x128 tiles), 256 or 512
  *                  columns per tile (512 needs CTA pairs)
- *   "l2_prefetch"  0 (default) = off; d in [1, 64]: the TMA producer also prefetches the
- *                  operand boxes of the K block d blocks ahead into L2 (takes effect for d
- *                  above the pipeline depth; unbatched calls)
  *   "epi_warps"    8 (default) or 4: epilogue warps of the 256 x 512 CTA-pair tile.  With 8,
  *                  each warp pulls 128 columns of an accumulator N-half into registers and
  *                  hands the half back to the MMA before storing it

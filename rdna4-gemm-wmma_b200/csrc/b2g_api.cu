@@ -68,7 +68,6 @@ static std::atomic<int64_t> opt_tail_split{1};  // split the tail wave's tiles (
 static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream serialization
 static std::atomic<int64_t> opt_pair_rows{0};  // 0 = choose, 64 = half-height pair tiles, 128 = never
 static std::atomic<int64_t> opt_epi_warps{8};  // epilogue warps of the 256 x 512 pair tile (4 or 8)
-static std::atomic<int64_t> opt_l2_prefetch{0};  // K blocks ahead to prefetch into L2 (0 = off)
 // Kernels this library has launched (every GEMM, scale and fill kernel), for callers that
 // count launches (b2g_get_option("launches")).
 static std::atomic<int64_t> g_launches{0};
@@ -819,7 +818,6 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.accumulate = beta != 0.0f ? 1 : 0;
   p.timeout_ns = (unsigned long long)opt_timeout_ns.load();
   p.fault_flags = (int)opt_fault_flags.load();
-  p.l2_prefetch = (int)opt_l2_prefetch.load();
 
   // ---- launch
   using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
@@ -1347,9 +1345,6 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_comm_timeout_ms = value;
   } else if (!strcmp(key, "comm_nonblocking")) {
     opt_comm_nonblocking = value ? 1 : 0;
-  } else if (!strcmp(key, "l2_prefetch")) {
-    if (value < 0 || value > 64) return B2G_ERR_INVALID_ARG;
-    opt_l2_prefetch = value;
   } else if (!strcmp(key, "epi_warps")) {
     if (value != 4 && value != 8) return B2G_ERR_INVALID_ARG;
     opt_epi_warps = value;
@@ -1387,7 +1382,6 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "ring_slots")) return opt_ring_slots;
   if (!strcmp(key, "pair_rows")) return opt_pair_rows;
   if (!strcmp(key, "epi_warps")) return opt_epi_warps;
-  if (!strcmp(key, "l2_prefetch")) return opt_l2_prefetch;
   if (!strcmp(key, "comm_timeout_ms")) return opt_comm_timeout_ms;
   if (!strcmp(key, "comm_nonblocking")) return opt_comm_nonblocking;
   return -1;

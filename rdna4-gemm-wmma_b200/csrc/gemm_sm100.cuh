@@ -93,8 +93,6 @@ struct GemmParams {
   int ab_format;               // UMMA operand format code (see make_idesc)
   unsigned long long timeout_ns;
   int fault_flags;             // test-only: bit 0 = producer issues no loads (forces a timeout)
-  int l2_prefetch;             // > 0: the producer also prefetches the operand boxes of the K
-                               // block this many blocks ahead into L2 (unbatched calls only)
 };
 
 constexpr int kBM = 128;  // rows per CTA (UMMA M per CTA)
@@ -323,25 +321,6 @@ __global__ void __launch_bounds__(Cfg<CG, BN, BMC, EW>::THREADS, 1)
         int i0, b0, a0;
         m_tile_origin(p, mt, i0, b0, a0);
         const int n0 = tn * BN;
-        // L2 prefetch of K block kb (its A box and this CTA's B boxes); nothing waits for it
-        auto prefetch = [&](int kb) {
-          const int jj = kb / p.k_blocks_per_j;
-          const int kc = (kb - jj * p.k_blocks_per_j) * KB;
-          ptx::tma_prefetch_l2_5d(&tmA, kc, jj, i0, b0, a0);
-#pragma unroll
-          for (int h = 0; h < C::NH; ++h) {
-            const int nh = n0 + h * C::UN + (int)cta_rank * C::BPH;
-            if constexpr (B_KMAJOR) {
-              ptx::tma_prefetch_l2_3d(&tmB, kc, jj, nh);
-            } else {
-#pragma unroll
-              for (int c = 0; c < C::BPH / ATOM; ++c) ptx::tma_prefetch_l2_3d(&tmB, nh + ATOM * c, kc, jj);
-            }
-          }
-        };
-        const int pfd = p.b_batched ? 0 : p.l2_prefetch;
-        if (pfd > C::STAGES && !(p.fault_flags & 1))
-          for (int kb = kb_lo + C::STAGES; kb < kb_lo + pfd && kb < kb_hi; ++kb) prefetch(kb);
         for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (uint32_t)(it / C::STAGES) & 1u;
@@ -356,7 +335,6 @@ __global__ void __launch_bounds__(Cfg<CG, BN, BMC, EW>::THREADS, 1)
           const int kc = (kb - jj * p.k_blocks_per_j) * KB;
           ptx::tma_load_5d<CG>(base + s * C::A_BYTES, &tmA, fb, kc, jj, i0, b0, a0);
           issue_b(base + C::OFF_B + s * C::B_BYTES, fb, n0, kc, jj, a0);
-          if (pfd > C::STAGES && kb + pfd < kb_hi) prefetch(kb + pfd);
         }
       }
       // Teardown: every load this thread issued must land before the CTA can exit.  With

@@ -265,22 +265,6 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const void* tmap, uint
   }
 }
 
-// Prefetch a tensor box into L2 (no shared memory, no completion to wait for).
-__device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
-                   reinterpret_cast<uint64_t>(tmap)),
-               "r"(c0), "r"(c1), "r"(c2)
-               : "memory");
-}
-
-__device__ __forceinline__ void tma_prefetch_l2_5d(const void* tmap, int c0, int c1, int c2, int c3,
-                                                   int c4) {
-  asm volatile("cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(
-                   reinterpret_cast<uint64_t>(tmap)),
-               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
-               : "memory");
-}
-
 __device__ __forceinline__ void tma_store_4d(const void* tmap, uint32_t src, int c0, int c1, int c2,
                                              int c3) {
   asm volatile(

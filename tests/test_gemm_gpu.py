@@ -236,49 +236,3 @@ def test_launch_counter(b2g, cuda):
     torch.cuda.synchronize()
     assert b2g.get_option("launches") - n0 == 5
 
-
-@pytest.mark.parametrize("cg,tn", [(1, 128), (1, 256), (2, 256), (2, 512)], ids=["cta1_n128", "cta1_n256", "cta2_n256", "cta2_n512"])
-@pytest.mark.parametrize("MNK", [(128, 2048, 8192), (640, 1000, 3000), (1024, 1536, 4096)])
-def test_l2_prefetch_gives_identical_bits(b2g, cuda, orc, cg, tn, MNK):
-    """The producer's L2 prefetch of the operand boxes ahead of the pipeline (option
-    l2_prefetch) changes no result: identical bits with and without it, and within tolerance
-    of the oracle; split-K shapes included."""
-    torch = cuda
-    M, N, K = MNK
-    r8 = lambda x: (x + 7) // 8 * 8
-    A, dA = padded_f16(torch, orc, M, K, r8(K), 91)
-    B, dB = padded_f16(torch, orc, K, N, r8(N), 92)
-    outs = []
-    for pf in (0, 12):
-        with options(b2g, cta_group=cg, tile_n=tn, l2_prefetch=pf):
-            dC = torch.full((M, r8(N)), float("nan"), dtype=torch.float32, device="cuda")
-            b2g.gemm(dA, dB, dC, M, N, K, r8(K), r8(N), r8(N))
-            torch.cuda.synchronize()
-            assert b2g.device_status() == 0
-            outs.append(dC[:, :N].clone())
-    assert torch.equal(outs[0], outs[1])
-    assert_close(orc, outs[1].cpu().numpy(), orc.gemm_f64(A, B), K)
-
-
-def test_l2_prefetch_contraction_reference_form(b2g, cuda, orc):
-    """The same with the 5-D A map and K-major B of the reference's contraction layout."""
-    torch = cuda
-    mt, rt, nt, rt_l, bt = 4, 64, 3, 128, 512
-    G = orc.uniform_f16((rt * nt * mt * rt_l,), 93)
-    In = orc.uniform_f16((bt * nt * rt_l,), 94)
-    dG, dIn = to_dev(torch, G), to_dev(torch, In)
-    outs = []
-    for pf in (0, 10):
-        with options(b2g, l2_prefetch=pf):
-            dOut = torch.full((mt * bt * rt,), float("nan"), dtype=torch.float32, device="cuda")
-            b2g.contract5d(dG, (mt, 1, rt, nt, rt_l), (rt_l, 0, nt * mt * rt_l, mt * rt_l, 1), dIn,
-                           (nt, rt_l, bt), (rt_l, 1, nt * rt_l), dOut, (mt, 1, rt, bt),
-                           (bt * rt, 0, 1, rt))
-            torch.cuda.synchronize()
-            assert b2g.device_status() == 0
-            outs.append(dOut.clone())
-    assert torch.equal(outs[0], outs[1])
-    ref = orc.contract5d_f64(G, (mt, 1, rt, nt, rt_l), (rt_l, 0, nt * mt * rt_l, mt * rt_l, 1), In,
-                             (nt, rt_l, bt), (rt_l, 1, nt * rt_l), (mt, 1, rt, bt),
-                             (bt * rt, 0, 1, rt), c_size=mt * bt * rt)
-    assert_close(orc, outs[0].cpu().numpy(), ref, nt * rt_l)
