@@ -312,6 +312,11 @@ def main():
     ap.add_argument("--tp", default="p2p", choices=["p2p", "nccl"],
                     help="tp_k: reduce-scatter fused into the GEMMs over peer memory, or "
                          "ncclReduceScatter after the GEMM")
+    ap.add_argument("--rs-form", default="staged", choices=["staged", "direct", "fused"],
+                    help="tp_k --tp p2p: staged = peers' partials computed locally and pushed "
+                         "by the copy engine during the next GEMM; direct = the GEMMs store into "
+                         "the peers' slots; fused = direct, with the slots summed in the own "
+                         "slab's GEMM epilogue (all three give the same bits)")
     ap.add_argument("--shape", default=None,
                     help="M,N,K: time this row-major GEMM instead of 8192^3 (device-resident "
                          "kernel loop only; used for the other BASELINE shapes and for profiling)")
@@ -739,6 +744,8 @@ def run_tp_k(args, torch, dist, b2g, ws, rank, local, dev):
     dA = A[:, k0:k0 + kr].contiguous()
     dB = B[k0:k0 + kr].contiguous()
     dC = torch.empty((rows, N), dtype=torch.float32, device=dev)
+    b2g.set_option("rs_stage", 1 if args.rs_form == "staged" else 0)
+    b2g.set_option("rs_fused", 1 if args.rs_form == "fused" else 0)
     plan = b2g.rs_plan_create(comm, M, N) if args.tp == "p2p" else None
 
     def step():
@@ -800,9 +807,14 @@ def run_tp_k(args, torch, dist, b2g, ws, rank, local, dev):
             "data": "synthetic: seeded U[-1,1] fp16 generated on the device",
             "config": {"workload": "tensor-parallel K-split gemm %dx%dx%d, K slabs over N GPUs, "
                                    "partials reduce-scattered every step" % (M, N, K),
-                       "reduce_scatter": ("fused into the GEMMs over peer memory "
-                                          "(b2g_gemm_sharded_k_p2p)" if plan is not None
+                       "reduce_scatter": ({"staged": "partials pushed to the peers' slots by "
+                                                     "the copy engine during the next GEMM",
+                                           "direct": "GEMMs store into the peers' slots",
+                                           "fused": "GEMMs store into the peers' slots, own "
+                                                    "slab's epilogue sums the slots"}[args.rs_form]
+                                          + " (b2g_gemm_sharded_k_p2p)" if plan is not None
                                           else "ncclReduceScatter after the GEMM (b2g_gemm_sharded_k)"),
+                       "p2p_form": args.rs_form if plan is not None else None,
                        "rows_per_rank": rows},
             "roofline": {"bound": "tensor" if t_gemm >= t_link else "nvlink",
                          "target_ms": target * 1e3, "frac": target * 1e3 / (ms / args.steps),

@@ -237,13 +237,21 @@ int b2g_gemm_sharded_k(const void* A_kslab, const void* B_kslab, float* C_slab, 
                        void* stream);
 
 /*
- * The same K-split GEMM with the reduce-scatter fused into the GEMMs over peer memory (no
- * NCCL kernel).  b2g_rs_plan_create (collective, once per M x N) allocates every rank's
- * receive slots (world x M/world x N fp32) and maps every peer's through CUDA IPC.  In
- * b2g_gemm_sharded_k_p2p, rank r's GEMM of row slab q stores its tiles straight into rank q's
- * slot r over NVLink, and rank r sums its slots in rank order into C_slab.  Epoch flags
- * written and waited for by stream memory operations order the ranks.  Every rank of the
- * plan calls it with the same M, N, K, in the same order.  b2g_rs_plan_destroy is collective.
+ * The same K-split GEMM with the reduce-scatter done over peer memory (no NCCL kernel).
+ * b2g_rs_plan_create (collective, once per M x N) allocates every rank's receive slots
+ * (world x M/world x N fp32) and maps every peer's through CUDA IPC; in the staged form also
+ * min(2, world-1) local staging buffers of M/world x N fp32 and a copy stream.  In
+ * b2g_gemm_sharded_k_p2p, rank r's partial of row slab q reaches rank q's slot r, and C_slab
+ * is the sum of rank r's slots in rank order.  Three forms, all giving the same bits:
+ * staged (option "rs_stage", default 1, read when the plan is created and at each call): the
+ * peers' partials are computed into local staging buffers and the copy engine pushes each to
+ * its peer over NVLink while the next GEMM runs; direct ("rs_stage" 0): the GEMMs store their
+ * tiles straight into the peers' slots; fused ("rs_stage" 0, "rs_fused" 1): direct, and rank
+ * r computes its own slab last, after the peers' partials have landed, with a GEMM whose
+ * epilogue adds the slots in rank order and stores C_slab (no separate reduction kernel).
+ * Staged is the fastest measured.  Epoch flags written and waited for by stream memory
+ * operations order the ranks.  Every rank of the plan calls it with the same M, N, K, in the
+ * same order.  b2g_rs_plan_destroy is collective.
  * The ranks are processes on one node with CUDA IPC between their GPUs.  No reference
  * counterpart.
  */
@@ -252,6 +260,21 @@ int b2g_rs_plan_destroy(void* plan);
 int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const void* B_kslab, float* C_slab,
                            int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
                            void* stream);
+
+/*
+ * The fused form's epilogue on its own, for callers that run their own exchange:
+ * C (M x N, ldc) = sum over s = 0 .. count-1, in that order, of term s, where term `self` is
+ * A.B (fp16 A M x K and B K x N, row-major, fp32 accumulation) and every other term is the fp32
+ * M x N block slots + s * slot_stride (row pitch N).  With status != NULL, status[s] must equal
+ * `epoch` for every s != self, else C is NaN and b2g_device_status reports 7 (a peer's part
+ * failed).  On the tensor-core path the sum happens in the GEMM's epilogue; elsewhere a
+ * separate pass gives the same bits.  slots is 16-byte aligned and slot_stride (elements) a
+ * multiple of 4, at least M * N; count is at most 1024.  No reference counterpart.
+ */
+int b2g_gemm_sum_slots(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K,
+                       int64_t lda, int64_t ldb, int64_t ldc, const float* slots,
+                       int64_t slot_stride, int count, int self, const uint32_t* status,
+                       uint32_t epoch, void* stream);
 
 /*
  * N-slabs with all-gather: rank r holds the column slab b2g_slab_rows(N, world, r) of B
@@ -383,6 +406,10 @@ int b2g_device_status(int clear);
  *                  kernel's set-up overlaps the previous kernel in the stream); 0 = plain launch
  *   "comm_timeout_ms" bound of every NCCL wait of the multi-GPU entry points (default 60000)
  *   "comm_nonblocking" 1 (default) = b2g_comm_init makes a non-blocking NCCL communicator
+ *   "rs_stage"     1 (default) = b2g_gemm_sharded_k_p2p computes the peers' partials locally
+ *                  and pushes them with the copy engine; 0 = its GEMMs store into peer memory
+ *   "rs_fused"     with "rs_stage" 0: 1 = sum the slots in the own slab's GEMM epilogue; 0
+ *                  (default) = a separate reduction kernel (same bits)
  *   "ring_slots"   split-K arrival counters usable in the per-device ring (default and
  *                  maximum 1048576, a multiple of 64, at least 512): a small ring makes tests
  *                  wrap it often

@@ -101,6 +101,9 @@ def load(path=None):
     L.b2g_rs_plan_destroy.argtypes = [vp]
     L.b2g_gemm_sharded_k_p2p.restype = ctypes.c_int
     L.b2g_gemm_sharded_k_p2p.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, vp]
+    L.b2g_gemm_sum_slots.restype = ctypes.c_int
+    L.b2g_gemm_sum_slots.argtypes = [vp, vp, vp, i64, i64, i64, i64, i64, i64, vp, i64,
+                                     ctypes.c_int, ctypes.c_int, vp, ctypes.c_uint32, vp]
     L.b2g_chain_plan_create.restype = ctypes.c_int
     L.b2g_chain_plan_create.argtypes = [vp, vp, i64, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
     L.b2g_chain_plan_destroy.restype = ctypes.c_int
@@ -343,6 +346,18 @@ def gemm_sharded_k_p2p(plan, A_kslab, B_kslab, C_slab, M, N, K, lda=None, ldb=No
     _check(load().b2g_gemm_sharded_k_p2p(plan, _ptr(A_kslab), _ptr(B_kslab), _ptr(C_slab), M, N, K,
                                          _ld(A_kslab, lda, "lda"), _ld(B_kslab, ldb, "ldb"),
                                          _ld(C_slab, ldc, "ldc"), _stream(stream)))
+
+
+def gemm_sum_slots(A, B, C, M, N, K, slots, slot_stride, count, self_index, status=None,
+                   epoch=0, lda=None, ldb=None, ldc=None, stream=None):
+    """C = sum over s < count, in order, of term s: A.B for s == self_index, else the fp32
+    M x N block at slots + s * slot_stride (the peer-memory K-split's epilogue on its own)."""
+    _check(load().b2g_gemm_sum_slots(_ptr(A), _ptr(B), _ptr(C), M, N, K,
+                                     K if lda is None else lda, N if ldb is None else ldb,
+                                     N if ldc is None else ldc,
+                                     None if slots is None else _ptr(slots), slot_stride, count,
+                                     self_index, None if status is None else _ptr(status),
+                                     epoch, _stream(stream)))
 
 
 def chain_plan_create(comm, B, nbytes, root=0):

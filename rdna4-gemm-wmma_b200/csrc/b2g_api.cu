@@ -68,6 +68,8 @@ static std::atomic<int64_t> opt_tail_split{1};  // split the tail wave's tiles (
 static std::atomic<int64_t> opt_pdl{1};  // launch with programmatic stream serialization
 static std::atomic<int64_t> opt_pair_rows{0};  // 0 = choose, 64 = half-height pair tiles, 128 = never
 static std::atomic<int64_t> opt_epi_warps{8};  // epilogue warps of the 256 x 512 pair tile (4 or 8)
+static std::atomic<int64_t> opt_rs_fused{0};  // peer-memory K-split: rank-order sum in the own GEMM
+static std::atomic<int64_t> opt_rs_stage{1};  // peer-memory K-split: partials pushed by the copy engine
 // Kernels this library has launched (every GEMM, scale and fill kernel), for callers that
 // count launches (b2g_get_option("launches")).
 static std::atomic<int64_t> g_launches{0};
@@ -150,11 +152,12 @@ static CUresult encode_cached(CUtensorMap* out, CUtensorMapDataType dt, cuuint32
 struct DevState {
   int sm_count = 0;
   int cc_major = 0, cc_minor = 0;
-  bool attr_set[2][6][2][2] = {};  // [fp8][variant][b_kmajor][c_mcontig]
-  int max_clusters[2][6][2][2] = {};
+  // [kind: 0 fp16, 1 fp8, 2 fp16 with the epilogue rank-order sum][variant][b_kmajor][c_mcontig]
+  bool attr_set[3][6][2][2] = {};
+  int max_clusters[3][6][2][2] = {};
   // clusters of s split units resident at once (cluster fix-up): one-CTA tiles, or s CTA pairs
   // of half-height pair tiles
-  int max_clusters_cg1[2][6][2][2][9] = {};
+  int max_clusters_cg1[3][6][2][2][9] = {};
 };
 static std::mutex g_dev_mu;
 static DevState g_dev[64];
@@ -504,13 +507,23 @@ static inline CUtensorMapDataType dt_map(int dt) {
 }
 
 // ------------------------------------------------------------------ core dispatch
+// Rank-order sum in the epilogue (see GemmParams::add_*): the stored C is the sum, in slot
+// order, of `count` terms, term `self` being A.B and term s the fp32 slot base + s * slot.
+struct AddendSpec {
+  const float* base;
+  int64_t slot;
+  int count, self;
+  const uint32_t* status;
+  uint32_t epoch;
+};
+
 // c_type: 0 = fp32 C, 1 = fp16 C, 2 = bf16 C (16-bit C requires beta == 0); bias: optional
 // per-column fp32 vector of N elements added once to every row of alpha*A.B.
 static int run(const void* A, const int64_t as[5], const int64_t ast[5], const void* B,
                const int64_t bs[3], const int64_t bst[3], void* Cv, const int64_t cs[4],
                const int64_t cst[4], int dtype, float alpha, float beta, cudaStream_t stream,
                const FixedScratch* fixed = nullptr, const float* bias = nullptr, int c_type = 0,
-               int64_t b_batch = -1) {
+               int64_t b_batch = -1, const AddendSpec* add = nullptr) {
   // b_batch >= 0: mode a is a batch mode, B[a][j][k][n] with stride b_batch along a
   if (dtype < B2G_DTYPE_F16 || dtype > B2G_DTYPE_E5M2)
     return fail(B2G_ERR_INVALID_ARG, "unknown operand type code %d", dtype);
@@ -564,6 +577,8 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   const unsigned eblocks =
       (unsigned)std::min<int64_t>((total + eth - 1) / eth, (int64_t)ds->sm_count * 32);
   auto launch_generic = [&](int path) -> int {
+    if (add)  // the rank-order sum exists on the tensor-core path only
+      return fail(B2G_ERR_UNSUPPORTED, "the epilogue rank-order sum needs the tensor-core path");
     const Geo g = make_geo();
     switch (dtype) {
       case B2G_DTYPE_F16:
@@ -818,6 +833,16 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   p.accumulate = beta != 0.0f ? 1 : 0;
   p.timeout_ns = (unsigned long long)opt_timeout_ns.load();
   p.fault_flags = (int)opt_fault_flags.load();
+  if (add) {
+    if (batched || !c_n || c_type != 0 || beta != 0.0f || as[0] * as[1] != 1 || bias)
+      return fail(B2G_ERR_UNSUPPORTED, "the epilogue rank-order sum takes a plain row-major fp32 C");
+    p.add_base = add->base;
+    p.add_slot = (long long)add->slot;
+    p.add_count = add->count;
+    p.add_self = add->self;
+    p.add_status = add->status;
+    p.add_epoch = add->epoch;
+  }
 
   // ---- launch
   using KernFn = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const GemmParams);
@@ -857,9 +882,25 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   static const int threads_of[6] = {Cfg<1, 256>::THREADS, Cfg<2, 256>::THREADS,
                                     Cfg<2, 512>::THREADS, Cfg<1, 128>::THREADS,
                                     Cfg<2, 256, 64>::THREADS, Cfg<2, 512, kBM, 8>::THREADS};
+  // the epilogue rank-order sum: fp16 operands, row-major C (the ADD instances)
+  static const KernFn table_add[6][2] = {
+      {gemm_tc_kernel<1, 256, false, false, 2, kBM, 4, true>,
+       gemm_tc_kernel<1, 256, true, false, 2, kBM, 4, true>},
+      {gemm_tc_kernel<2, 256, false, false, 2, kBM, 4, true>,
+       gemm_tc_kernel<2, 256, true, false, 2, kBM, 4, true>},
+      {gemm_tc_kernel<2, 512, false, false, 2, kBM, 4, true>,
+       gemm_tc_kernel<2, 512, true, false, 2, kBM, 4, true>},
+      {gemm_tc_kernel<1, 128, false, false, 2, kBM, 4, true>,
+       gemm_tc_kernel<1, 128, true, false, 2, kBM, 4, true>},
+      {gemm_tc_kernel<2, 256, false, false, 2, 64, 4, true>,
+       gemm_tc_kernel<2, 256, true, false, 2, 64, 4, true>},
+      {gemm_tc_kernel<2, 512, false, false, 2, kBM, 8, true>,
+       gemm_tc_kernel<2, 512, true, false, 2, kBM, 8, true>}};
   const int nthreads = threads_of[variant];
-  const int e8 = esz == 1 ? 1 : 0;
-  KernFn kern = table[e8][variant][bk][cm];
+  if (add && (esz != 2 || cm != 0))
+    return fail(B2G_ERR_UNSUPPORTED, "the epilogue rank-order sum takes 16-bit operands and a row-major C");
+  const int e8 = add ? 2 : esz == 1 ? 1 : 0;
+  KernFn kern = add ? table_add[variant][bk] : table[e8][variant][bk][cm];
   const uint32_t smem = smem_of[variant];
   {
     std::lock_guard<std::mutex> lk(g_dev_mu);
@@ -1036,9 +1077,10 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
     attr[cfg.numAttrs].val.clusterDim.z = 1;
     ++cfg.numAttrs;
   }
-  if (opt_pdl.load()) {
+  if (opt_pdl.load() && !add) {
     // programmatic dependent launch: the kernel's set-up overlaps the previous kernel's tail
-    // (the kernel waits with griddepcontrol.wait before it touches global memory)
+    // (the kernel waits with griddepcontrol.wait before it touches global memory).  Not for
+    // the rank-order sum, whose launch follows a stream wait on the peers' flags.
     attr[cfg.numAttrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[cfg.numAttrs].val.programmaticStreamSerializationAllowed = 1;
     ++cfg.numAttrs;
@@ -1059,6 +1101,50 @@ static int run(const void* A, const int64_t as[5], const int64_t ast[5], const v
   g_launches.fetch_add(1, std::memory_order_relaxed);
   t_path = cg == 1 ? B2G_PATH_TC_1CTA : B2G_PATH_TC_2CTA;
   return B2G_OK;
+}
+
+int gemm_rank_sum(const void* A, const void* B, float* C, int64_t M, int64_t N, int64_t K,
+                  int64_t lda, int64_t ldb, int64_t ldc, const float* add_base, int64_t add_slot,
+                  int add_count, int add_self, const uint32_t* status, uint32_t epoch,
+                  void* stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
+  if (lda < std::max<int64_t>(K, 1) || ldb < std::max<int64_t>(N, 1) || ldc < std::max<int64_t>(N, 1))
+    return fail(B2G_ERR_INVALID_ARG, "leading dimension smaller than the row length");
+  if (M == 0 || N == 0) return B2G_OK;  // nothing to store (run() would return before adding)
+  if (K == 0) return fail(B2G_ERR_UNSUPPORTED, "the epilogue rank-order sum needs K > 0");
+  const int64_t as[5] = {1, 1, M, 1, K}, ast[5] = {0, 0, lda, 0, 1};
+  const int64_t bs[3] = {1, K, N}, bst[3] = {0, ldb, 1};
+  const int64_t cs[4] = {1, 1, M, N}, cst[4] = {0, 0, ldc, 1};
+  const AddendSpec add = {add_base, add_slot, add_count, add_self, status, epoch};
+  return run(A, as, ast, B, bs, bst, C, cs, cst, B2G_DTYPE_F16, 1.0f, 0.0f,
+             static_cast<cudaStream_t>(stream), nullptr, nullptr, 0, -1, &add);
+}
+
+bool rs_fused() { return opt_rs_fused.load() != 0; }
+bool rs_stage() { return opt_rs_stage.load() != 0; }
+
+// The rank-order sum as a separate pass, for calls the tensor-core epilogue does not take:
+// C (holding A.B) becomes the sum over s of term s in order, term `self` being C itself and
+// the others slots[s * slot_stride + i * N + j].  Failed status words give NaN, as in the
+// kernel's epilogue.
+__global__ void slot_sum_kernel(float* __restrict__ C, int64_t M, int64_t N, int64_t ldc,
+                                const float* __restrict__ slots, int64_t slot_stride, int count,
+                                int self, const uint32_t* status, uint32_t epoch) {
+  bool failed = false;
+  if (status)
+    for (int s = 0; s < count; ++s)
+      if (s != self && __ldcg(status + s) != epoch) failed = true;
+  if (failed && blockIdx.x == 0 && threadIdx.x == 0) atomicCAS(&g_device_error, 0, ERR_PEER_FAILED);
+  const int64_t total = M * N, stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < total; v += stride) {
+    const int64_t i = v / N, j = v - i * N;
+    float a = 0.0f;
+    for (int s = 0; s < count; ++s) {
+      const float t = s == self ? C[i * ldc + j] : __ldcg(slots + s * slot_stride + v);
+      a = s == 0 ? t : a + t;
+    }
+    C[i * ldc + j] = failed ? __int_as_float(0x7fc00000) : a;
+  }
 }
 
 }  // namespace b2g
@@ -1083,6 +1169,38 @@ extern "C" int b2g_gemm_ex(const void* A, const void* B, float* C, int64_t M, in
 extern "C" int b2g_gemm_f16_f32(const void* A, const void* B, float* C, int64_t M, int64_t N,
                                 int64_t K, int64_t lda, int64_t ldb, int64_t ldc, void* stream) {
   return b2g_gemm_ex(A, B, C, M, N, K, lda, ldb, ldc, 1.0f, 0.0f, stream);
+}
+
+extern "C" int b2g_gemm_sum_slots(const void* A, const void* B, float* C, int64_t M, int64_t N,
+                                  int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                                  const float* slots, int64_t slot_stride, int count, int self,
+                                  const uint32_t* status, uint32_t epoch, void* stream) {
+  t_err.clear();
+  if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_INVALID_ARG, "negative dimension");
+  if (lda < std::max<int64_t>(K, 1) || ldb < std::max<int64_t>(N, 1) || ldc < std::max<int64_t>(N, 1))
+    return fail(B2G_ERR_INVALID_ARG, "leading dimension smaller than the row length");
+  if (count < 1 || count > 1024 || self < 0 || self >= count)
+    return fail(B2G_ERR_INVALID_ARG, "count outside [1, 1024] or self outside [0, count)");
+  if (count > 1 && (!slots || slot_stride < M * N || slot_stride % 4 != 0 ||
+                    (reinterpret_cast<uintptr_t>(slots) & 15) != 0))
+    return fail(B2G_ERR_INVALID_ARG,
+                "slots must be 16-byte aligned, slot_stride >= M * N and a multiple of 4");
+  if (M == 0 || N == 0) return B2G_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = K > 0 ? gemm_rank_sum(A, B, C, M, N, K, lda, ldb, ldc, slots, slot_stride, count, self,
+                                 status, epoch, stream)
+                 : (int)B2G_ERR_UNSUPPORTED;
+  if (rc != B2G_ERR_UNSUPPORTED) return rc;
+  // no tensor-core launch for this call: the GEMM, then the sum as its own pass
+  rc = b2g_gemm_ex(A, B, C, M, N, K, lda, ldb, ldc, 1.0f, 0.0f, stream);
+  if (rc != B2G_OK || count == 1) return rc;
+  const int64_t blocks = std::min<int64_t>((M * N + 255) / 256, 148 * 8);
+  slot_sum_kernel<<<(unsigned)blocks, 256, 0, s>>>(C, M, N, ldc, slots, slot_stride, count, self,
+                                                   status, epoch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "slot_sum_kernel");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return B2G_OK;
 }
 
 extern "C" int b2g_gemm_f16_f32_noalloc(const void* A, const void* B, float* C, int64_t M,
@@ -1345,6 +1463,10 @@ extern "C" int b2g_set_option(const char* key, int64_t value) {
     opt_comm_timeout_ms = value;
   } else if (!strcmp(key, "comm_nonblocking")) {
     opt_comm_nonblocking = value ? 1 : 0;
+  } else if (!strcmp(key, "rs_fused")) {
+    opt_rs_fused = value ? 1 : 0;
+  } else if (!strcmp(key, "rs_stage")) {
+    opt_rs_stage = value ? 1 : 0;
   } else if (!strcmp(key, "epi_warps")) {
     if (value != 4 && value != 8) return B2G_ERR_INVALID_ARG;
     opt_epi_warps = value;
@@ -1382,6 +1504,8 @@ extern "C" int64_t b2g_get_option(const char* key) {
   if (!strcmp(key, "ring_slots")) return opt_ring_slots;
   if (!strcmp(key, "pair_rows")) return opt_pair_rows;
   if (!strcmp(key, "epi_warps")) return opt_epi_warps;
+  if (!strcmp(key, "rs_fused")) return opt_rs_fused;
+  if (!strcmp(key, "rs_stage")) return opt_rs_stage;
   if (!strcmp(key, "comm_timeout_ms")) return opt_comm_timeout_ms;
   if (!strcmp(key, "comm_nonblocking")) return opt_comm_nonblocking;
   return -1;

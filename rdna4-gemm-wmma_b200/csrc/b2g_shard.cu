@@ -975,6 +975,14 @@ struct b2g_rs_plan {
   std::vector<uint32_t*> peer_flags;   // rank q's flag array, mapped here
   std::vector<void*> opened;
   uint32_t epoch = 0;
+  // Staged form (option "rs_stage" at plan creation): the partials of the peers' slabs are
+  // computed into local buffers and pushed to the peers' slots by the copy engine on `copy`,
+  // while the next GEMM runs.  min(2, world - 1) buffers of rows x N fp32.
+  float* stage[2] = {nullptr, nullptr};
+  int nstage = 0;
+  cudaStream_t copy = nullptr;
+  cudaEvent_t gemm_done[2] = {nullptr, nullptr}, copy_done[2] = {nullptr, nullptr};
+  cudaEvent_t copies_done = nullptr;  // the last call's copies (the buffers may be rewritten)
 };
 
 namespace {
@@ -991,6 +999,13 @@ void rs_plan_free(b2g_rs_plan* p) {
     if (o) cudaIpcCloseMemHandle(o);
   if (p->recv) cudaFree(p->recv);
   if (p->flags) cudaFree(p->flags);
+  for (int b = 0; b < 2; ++b) {
+    if (p->stage[b]) cudaFree(p->stage[b]);
+    if (p->gemm_done[b]) cudaEventDestroy(p->gemm_done[b]);
+    if (p->copy_done[b]) cudaEventDestroy(p->copy_done[b]);
+  }
+  if (p->copies_done) cudaEventDestroy(p->copies_done);
+  if (p->copy) cudaStreamDestroy(p->copy);
   delete p;
 }
 
@@ -1071,6 +1086,18 @@ extern "C" int b2g_rs_plan_create(void* comm, int64_t M, int64_t N, void** plan_
   cudaError_t e = cudaMalloc(&p->recv, rbytes);
   if (e == cudaSuccess) e = cudaMalloc(&p->flags, 3 * p->world * sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMemset(p->flags, 0, 3 * p->world * sizeof(uint32_t));
+  if (e == cudaSuccess && p->world > 1 && b2g::rs_stage()) {
+    p->nstage = std::min(2, p->world - 1);
+    const size_t sbytes = std::max<size_t>(16, (size_t)p->rows * N * sizeof(float));
+    for (int b = 0; b < p->nstage && e == cudaSuccess; ++b) {
+      e = cudaMalloc(&p->stage[b], sbytes);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->gemm_done[b], cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->copy_done[b], cudaEventDisableTiming);
+    }
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&p->copy, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&p->copies_done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(p->copies_done, p->copy);
+  }
   int rc = e == cudaSuccess ? B2G_OK : cuda_sfail(e, "reduce-scatter plan set-up");
   p->peer_recv.assign(p->world, nullptr);
   p->peer_flags.assign(p->world, nullptr);
@@ -1232,16 +1259,73 @@ extern "C" int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const voi
     if (r != CUDA_SUCCESS && rc == B2G_OK)
       rc = sfail(B2G_ERR_CUDA, std::string(what) + " failed (CUresult " + std::to_string((int)r) + ")");
   };
+  // Three forms, all giving the same bits (slot s of rank q holds rank s's partial of q's rows
+  // and C_slab is the sum of the slots in rank order):
+  //  - staged (option "rs_stage", default): the peers' partials are computed into local
+  //    buffers, and the copy engine pushes each to its peer's slot on the plan's copy stream
+  //    while the next GEMM runs, so no GEMM stores over NVLink (measured: a GEMM whose C is a
+  //    peer's memory runs 8-40% slower, its epilogue stalled on the link); the own partial
+  //    goes to slot R and rs_reduce_kernel sums the slots;
+  //  - direct: the GEMMs of the peers' slabs store their tiles straight into the peers' slots;
+  //  - direct and fused (option "rs_fused"): as direct, but the own slab is computed last,
+  //    after every peer's partial of it has landed, by a GEMM whose epilogue adds the peers'
+  //    slots in rank order (its own product standing in for slot R) and stores C_slab; it
+  //    needs the tensor-core path (16-byte aligned operands and pitches), and where the
+  //    planner finds no tensor-core launch the own partial goes to slot R as in the others.
+  const char* A_base = static_cast<const char*>(A_kslab);
+  const int64_t lda_e = kr > 0 ? lda : 1;
+  const bool stage = W > 1 && b2g::rs_stage() && p->nstage > 0;
+  const bool fused = !stage && W > 1 && b2g::rs_fused() && rc == B2G_OK && rows > 0 && N > 0 &&
+                     kr > 0 && N % 4 == 0 && ldc % 4 == 0 && lda % 8 == 0 && ldb % 8 == 0 &&
+                     (reinterpret_cast<uintptr_t>(C_slab) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(A_base) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(B_kslab) & 15) == 0 &&
+                     b2g_get_option("force_generic") == 0;
+  const bool work = rows > 0 && N > 0;
+  auto ce = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && rc == B2G_OK) rc = cuda_sfail(e, what);
+  };
+  CUstream ccs = reinterpret_cast<CUstream>(p->copy);
+  // staged: the previous call's pushes out of the staging buffers finish before they are
+  // rewritten (whatever stream that call ran on)
+  if (stage) ce(cudaStreamWaitEvent(s, p->copies_done, 0), "cudaStreamWaitEvent(previous pushes)");
   // the partial of rows [q*rows, (q+1)*rows) goes to rank q's slot R; the other ranks first
   for (int t = 1; t <= W; ++t) {
     const int q = (R + t) % W;
-    if (q != R)  // rank q has reduced the previous call's slots
+    const char* A_q = A_base + (size_t)(q * rows) * lda_e * 2;
+    if (q == R) {
+      if (!fused && rc == B2G_OK && work)
+        rc = b2g_gemm_ex(A_q, B_kslab, p->recv + (size_t)R * rows * N, rows, N, kr, lda_e, ldb, N,
+                         1.0f, 0.0f, s);
+      continue;
+    }
+    if (!stage) {
+      // rank q has reduced the previous call's slots
       cu(d->wait32(cs, flag(p->flags, W + q), ep - 1, CU_STREAM_WAIT_VALUE_GEQ),
          "cuStreamWaitValue32(slots free)");
-    if (rc != B2G_OK || rows == 0 || N == 0) continue;
-    rc = b2g_gemm_ex(static_cast<const char*>(A_kslab) + (size_t)(q * rows) * (kr > 0 ? lda : 1) * 2,
-                     B_kslab, p->peer_recv[q] + (size_t)R * rows * N, rows, N, kr,
-                     kr > 0 ? lda : 1, ldb, N, 1.0f, 0.0f, s);
+      if (rc == B2G_OK && work)
+        rc = b2g_gemm_ex(A_q, B_kslab, p->peer_recv[q] + (size_t)R * rows * N, rows, N, kr, lda_e,
+                         ldb, N, 1.0f, 0.0f, s);
+      continue;
+    }
+    const int b = (t - 1) % p->nstage;
+    if (t - 1 >= p->nstage)  // buffer b's earlier push in this call is done
+      ce(cudaStreamWaitEvent(s, p->copy_done[b], 0), "cudaStreamWaitEvent(push done)");
+    if (rc == B2G_OK && work)
+      rc = b2g_gemm_ex(A_q, B_kslab, p->stage[b], rows, N, kr, lda_e, ldb, N, 1.0f, 0.0f, s);
+    ce(cudaEventRecord(p->gemm_done[b], s), "cudaEventRecord(partial)");
+    ce(cudaStreamWaitEvent(p->copy, p->gemm_done[b], 0), "cudaStreamWaitEvent(partial)");
+    cu(d->wait32(ccs, flag(p->flags, W + q), ep - 1, CU_STREAM_WAIT_VALUE_GEQ),
+       "cuStreamWaitValue32(slots free)");
+    if (rc == B2G_OK && work)
+      ce(cudaMemcpyAsync(p->peer_recv[q] + (size_t)R * rows * N, p->stage[b],
+                         (size_t)rows * N * sizeof(float), cudaMemcpyDeviceToDevice, p->copy),
+         "cudaMemcpyAsync(push partial)");
+    ce(cudaEventRecord(p->copy_done[b], p->copy), "cudaEventRecord(push)");
+  }
+  if (stage) {  // the flags below announce partials that have arrived
+    ce(cudaEventRecord(p->copies_done, p->copy), "cudaEventRecord(pushes)");
+    ce(cudaStreamWaitEvent(s, p->copies_done, 0), "cudaStreamWaitEvent(pushes)");
   }
   // announce this rank's partials (the default write orders the GEMMs' stores before it), then
   // wait for every peer's.  The status word goes first: the epoch if this rank's part
@@ -1255,12 +1339,23 @@ extern "C" int b2g_gemm_sharded_k_p2p(void* plan, const void* A_kslab, const voi
   for (int q = 0; q < W; ++q)
     if (q != R)
       cu(d->wait32(cs, flag(p->flags, q), ep, CU_STREAM_WAIT_VALUE_GEQ), "cuStreamWaitValue32(landed)");
-  if (rc == B2G_OK && rows > 0 && N > 0) {
+  bool reduce = !fused;
+  if (fused && rc == B2G_OK && work) {
+    const char* A_own = A_base + (size_t)(R * rows) * lda_e * 2;
+    rc = b2g::gemm_rank_sum(A_own, B_kslab, C_slab, rows, N, kr, lda_e, ldb, ldc, p->recv,
+                            rows * N, W, R, p->flags + 2 * W, ep, s);
+    if (rc == B2G_ERR_UNSUPPORTED) {  // no tensor-core launch: the unfused form
+      rc = b2g_gemm_ex(A_own, B_kslab, p->recv + (size_t)R * rows * N, rows, N, kr, lda_e, ldb,
+                       N, 1.0f, 0.0f, s);
+      reduce = true;
+    }
+  }
+  if (reduce && rc == B2G_OK && work) {
     const int vec = (N % 4 == 0 && ldc % 4 == 0 && (reinterpret_cast<uintptr_t>(C_slab) & 15) == 0);
-    const int64_t work = vec ? rows * (N / 4) : rows * N;
+    const int64_t items = vec ? rows * (N / 4) : rows * N;
     int sms = 148;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p->dev);
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)sms * 8));
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, (int64_t)sms * 8));
     rs_reduce_kernel<<<grid, 256, 0, s>>>(p->recv, C_slab, rows, N, ldc, W, vec, p->flags + 2 * W,
                                           ep, R);
     cudaError_t e = cudaGetLastError();

@@ -41,6 +41,7 @@ enum : int {
   ERR_WAIT_TFULL = 4,   // epilogue waiting for an accumulator
   ERR_WAIT_DRAIN = 5,   // teardown waiting for copies / MMAs in flight
   ERR_WAIT_FIXUP = 6,   // split-K unit waiting for the partial tiles of its siblings
+  ERR_PEER_FAILED = 7,  // a peer's part of a peer-memory reduce-scatter failed (its status word)
 };
 
 // Problem description computed on the host (b2g_api.cu) and passed by value.
@@ -93,6 +94,19 @@ struct GemmParams {
   int ab_format;               // UMMA operand format code (see make_idesc)
   unsigned long long timeout_ns;
   int fault_flags;             // test-only: bit 0 = producer issues no loads (forces a timeout)
+  // Rank-order sum in the epilogue (the own row slab of the peer-memory K-split; the kernel
+  // instances with ADD = true only): with add_count > 0 every stored element is the sum over
+  // s = 0 .. add_count-1, in that order, of term s, where term add_self is this launch's A.B
+  // and every other term is add_base[s * add_slot + row * n_size + col] (fp32 slots, e.g.
+  // written by the peers).  Plain row-major C only (one M mode).  With add_status set,
+  // add_status[s] must equal add_epoch for every s other than add_self, else the result is
+  // NaN and the device error word records ERR_PEER_FAILED.
+  const float* add_base;
+  long long add_slot;
+  int add_count;
+  int add_self;
+  const unsigned* add_status;
+  unsigned add_epoch;
 };
 
 constexpr int kBM = 128;  // rows per CTA (UMMA M per CTA)
@@ -208,7 +222,8 @@ __device__ __forceinline__ void m_tile_origin(const GemmParams& p, int mt, int& 
 
 // ESZ: operand element size in bytes (2 = fp16/bf16 via kind::f16, 1 = fp8 via kind::f8f6f4).
 // A K block is 128 bytes of K (64 or 128 elements), consumed by 4 UMMAs of 32 bytes of K each.
-template <int CG, int BN, bool B_KMAJOR, bool C_MCONTIG, int ESZ, int BMC = kBM, int EW = 4>
+template <int CG, int BN, bool B_KMAJOR, bool C_MCONTIG, int ESZ, int BMC = kBM, int EW = 4,
+          bool ADD = false>
 __global__ void __launch_bounds__(Cfg<CG, BN, BMC, EW>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
@@ -447,6 +462,16 @@ __global__ void __launch_bounds__(Cfg<CG, BN, BMC, EW>::THREADS, 1)
     // its columns: BMC = 128, all BN columns of rows 32q..32q+31; BMC = 64 (folded
     // accumulator), columns [(q/2)*BN/2, (q/2+1)*BN/2) of rows 32(q%2)..32(q%2)+31.
     const int r0 = BMC == kBM ? 32 * q : 32 * (q & 1);
+    // rank-order sum: the peers' status words are final before the launch (the stream waited
+    // for their flags), so each warp reads them once
+    bool add_failed = false;
+    if constexpr (ADD) {
+      if (p.add_count > 0 && p.add_status != nullptr) {
+        for (int s2 = 0; s2 < p.add_count; ++s2)
+          if (s2 != p.add_self && __ldcg(p.add_status + s2) != p.add_epoch) add_failed = true;
+        if (add_failed && lane == 0) atomicCAS(err, 0, ERR_PEER_FAILED);
+      }
+    }
     const int col_off = BMC == kBM ? 0 : (q >> 1) * C::WARP_COLS;
     const int a_l = r0 / (p.bi * p.bb);
     const int b_l = (r0 / p.bi) % p.bb;
@@ -464,6 +489,27 @@ __global__ void __launch_bounds__(Cfg<CG, BN, BMC, EW>::THREADS, 1)
       const bool rows_valid = mt < p.num_m_tiles && ci < p.i_size && cb < p.b_size && ca < p.a_size;
       const int acc = (C::ACC_BUFS == 2) ? (tc & 1) : 0;
       const uint32_t aph = (uint32_t)(C::ACC_BUFS == 2 ? (tc >> 1) : tc) & 1u;
+      if constexpr (ADD) {
+        // rank-order sum: while the tile's MMAs run, bring this lane's row of every other
+        // term (the columns this warp stores) into L2, so that the epilogue's reads hit there
+        const int row = ci + lane;
+        if (p.add_count > 1 && !add_failed && rows_valid && row < p.i_size && ns == 1) {
+          const int nb = tn * BN + col_off;
+          for (int s2 = 0; s2 < p.add_count; ++s2) {
+            if (s2 == p.add_self) continue;
+            const float* rp = p.add_base + (size_t)s2 * (size_t)p.add_slot +
+                              (size_t)row * (size_t)p.n_size;
+#pragma unroll
+            for (int ch = 0; ch < C::CHUNKS; ++ch) {
+              const int gc = nb + 32 * ch;
+              if (!mine(ch) || gc >= p.n_size) continue;
+              const uint32_t bytes = (uint32_t)min(32, p.n_size - gc) * 4u & ~15u;
+              if (bytes && (reinterpret_cast<uintptr_t>(rp + gc) & 15) == 0)
+                ptx::bulk_prefetch_l2(rp + gc, bytes);
+            }
+          }
+        }
+      }
       const bool got = ptx::mbar_wait(tfull_bar(acc), aph, abort_flag, err, ERR_WAIT_TFULL, lim);
       if (!__all_sync(0xffffffffu, got)) break;
       ptx::tc_fence_after();
@@ -483,9 +529,60 @@ __global__ void __launch_bounds__(Cfg<CG, BN, BMC, EW>::THREADS, 1)
         }
         __syncwarp();
         uint32_t w[32];
+        if (ADD && p.add_count > 0) {
+          // rank-order sum (compiled only into the ADD instances, so that the plain kernels
+          // keep their registers): term add_self is v, the others come from the peers' slots
+          // (row = this lane's row of the plain row-major C)
+          const int row = ci + lane;
+          if (add_failed) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = 0x7fc00000u;  // NaN
+          } else {
+            float a[32];
+            const bool vec = gcol + 32 <= p.n_size && (p.n_size & 3) == 0;
+            // each term is added straight into a (the first one assigned), so no second
+            // 32-value array is live
+#pragma unroll 1
+            for (int s2 = 0; s2 < p.add_count; ++s2) {
+              const bool first = s2 == 0;
+              if (s2 == p.add_self) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  a[j] = first ? __uint_as_float(v[j]) : a[j] + __uint_as_float(v[j]);
+              } else if (row < p.i_size) {
+                const float* src = p.add_base + (size_t)s2 * (size_t)p.add_slot +
+                                   (size_t)row * (size_t)p.n_size + gcol;
+                if (vec) {
+#pragma unroll
+                  for (int j = 0; j < 8; ++j) {
+                    const float4 x = __ldcg(reinterpret_cast<const float4*>(src) + j);
+                    a[4 * j] = first ? x.x : a[4 * j] + x.x;
+                    a[4 * j + 1] = first ? x.y : a[4 * j + 1] + x.y;
+                    a[4 * j + 2] = first ? x.z : a[4 * j + 2] + x.z;
+                    a[4 * j + 3] = first ? x.w : a[4 * j + 3] + x.w;
+                  }
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) {
+                    const float x = gcol + j < p.n_size ? __ldcg(src + j) : 0.0f;
+                    a[j] = first ? x : a[j] + x;
+                  }
+                }
+              } else if (first) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) a[j] = 0.0f;  // a row past M: clipped by the store
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(a[j]);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) w[j] = v[j];
+        }
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          w[j] = p.alpha == 1.0f ? v[j] : __float_as_uint(__uint_as_float(v[j]) * p.alpha);
+          w[j] = p.alpha == 1.0f ? w[j] : __float_as_uint(__uint_as_float(w[j]) * p.alpha);
         if (p.bias) {
           // the same 32 bias values for every lane (broadcast loads); columns past N are not
           // read (the store clips them)

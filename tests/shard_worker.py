@@ -299,6 +299,60 @@ def nccl_p2p_rs_rank(rank, world, uid_path, M, N, K, calls, out_q):
         out_q.put((rank, -1, -1, False, traceback.format_exc()))
 
 
+def nccl_p2p_rs_forms_rank(rank, world, uid_path, M, N, K, ldc, out_q):
+    """b2g_gemm_sharded_k_p2p in its three forms on the same operands: staged (partials pushed
+    by the copy engine; option rs_stage 1), direct (GEMMs store into the peers' slots; rs_stage
+    0, rs_fused 0) and direct with the slots summed in the own slab's GEMM epilogue (rs_stage
+    0, rs_fused 1).  C must be the same bits in all three and correct on sampled rows; the
+    fused form launches one kernel fewer (no reduction kernel).  Reports (rank, C equal,
+    {form: launches}, failing sampled elements, device status, traceback)."""
+    try:
+        import torch
+        from oracle import orc
+        b2g = _load_pkg("b2g")
+        torch.cuda.set_device(rank)
+        comm = _nccl_comm(b2g, rank, world, uid_path)
+        plan = b2g.rs_plan_create(comm, M, N)  # rs_stage is on by default: staging buffers
+        k0, kr = b2g.slab_rows(K, world, rank)
+        rows = M // world
+        dA = torch.empty((M, K), dtype=torch.float16, device="cuda")
+        dB = torch.empty((K, N), dtype=torch.float16, device="cuda")
+        b2g.fill_uniform(dA, M * K, 31)
+        b2g.fill_uniform(dB, K * N, 32)
+        Ak, Bk = dA[:, k0:k0 + kr].contiguous(), dB[k0:k0 + kr].contiguous()
+        forms = {"staged": (1, 0), "direct": (0, 0), "fused": (0, 1)}
+        outs, launches = {}, {}
+        old = {k: b2g.get_option(k) for k in ("rs_stage", "rs_fused")}
+        try:
+            for name, (stage, fused) in forms.items():
+                b2g.set_option("rs_stage", stage)
+                b2g.set_option("rs_fused", fused)
+                dC = torch.full((rows, ldc), float("nan"), dtype=torch.float32, device="cuda")
+                torch.cuda.synchronize()
+                n0 = b2g.get_option("launches")
+                b2g.gemm_sharded_k_p2p(plan, Ak, Bk, dC, M, N, K, lda=max(kr, 1), ldb=N, ldc=ldc)
+                launches[name] = b2g.get_option("launches") - n0
+                torch.cuda.synchronize()
+                outs[name] = dC
+        finally:
+            for k, v in old.items():
+                b2g.set_option(k, v)
+        ref = outs["staged"]
+        same = all(bool(torch.equal(o[:, :N].view(torch.int32), ref[:, :N].view(torch.int32)))
+                   and bool(torch.isnan(o[:, N:]).all()) for o in outs.values())
+        B = orc.uniform_f16((K, N), 32)
+        bad = 0
+        for r in sorted(set([0, rows - 1, rows // 2, rows // 3])):
+            a = orc.uniform_f16((1, K), 31, (rank * rows + r) * K)
+            bad += orc.check(ref[r:r + 1, :N].cpu().numpy(), orc.gemm_f64(a, B), K, 1.0, 1.0)[0]
+        status = b2g.device_status()
+        b2g.rs_plan_destroy(plan)
+        b2g.comm_destroy(comm)
+        out_q.put((rank, same, launches, bad, status, None))
+    except Exception:
+        out_q.put((rank, False, {}, -1, -1, traceback.format_exc()))
+
+
 def nccl_chain_rank(rank, world, uid_path, M, N, K, panels, calls, out_q):
     """b2g_gemm_sharded_chain on `world` GPUs: `calls` calls in a row, the root writing a new B
     (another seed) before each; every call checked on sampled rows, and B bit-exact."""

@@ -76,6 +76,20 @@ def test_invalid_arguments_rejected_without_gpu(b2g):
                             None) == b2g.ERR_INVALID_ARG
     assert L.b2g_gemm_batched(None, None, None, -1, 4, 4, 4, 4, 4, 4, 16, 16, 16,
                               None) == b2g.ERR_INVALID_ARG
+    # the slot sum: count, self and slot alignment are checked first; an empty C needs nothing
+    assert L.b2g_gemm_sum_slots(None, None, None, 4, 4, 4, 4, 4, 4, None, 16, 0, 0, None, 0,
+                                None) == b2g.ERR_INVALID_ARG
+    assert L.b2g_gemm_sum_slots(None, None, None, 4, 4, 4, 4, 4, 4, None, 16, 2, 2, None, 0,
+                                None) == b2g.ERR_INVALID_ARG
+    assert L.b2g_gemm_sum_slots(None, None, None, 4, 4, 4, 4, 4, 4, None, 16, 2, 0, None, 0,
+                                None) == b2g.ERR_INVALID_ARG
+    assert L.b2g_gemm_sum_slots(None, None, None, 4, 4, 4, 4, 4, 4, 4096 + 4, 16, 2, 0, None,
+                                0, None) == b2g.ERR_INVALID_ARG
+    assert b"16-byte aligned" in L.b2g_last_error_string()
+    assert L.b2g_gemm_sum_slots(None, None, None, 4, 4, 4, 4, 4, 4, 4096, 12, 2, 0, None, 0,
+                                None) == b2g.ERR_INVALID_ARG
+    assert L.b2g_gemm_sum_slots(None, None, None, 0, 4, 4, 4, 4, 4, 4096, 16, 2, 0, None, 0,
+                                None) == b2g.OK
     # multi-GPU plans: null plan / communicator rejected, destroying a null plan is a no-op
     assert L.b2g_gemm_sharded_k_p2p(None, None, None, None, 4, 4, 4, 4, 4, 4,
                                     None) == b2g.ERR_INVALID_ARG

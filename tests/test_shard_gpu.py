@@ -158,6 +158,33 @@ def test_p2p_rs_multi_rank(b2g, cuda, world, M, N, K):
         assert bad == 0 and status == 0 and pad_ok, (rank, bad, status, pad_ok)
 
 
+@pytest.mark.parametrize("world,M,N,K,ldc", [(2, 2048, 1536, 4096, 1536), (2, 4096, 8192, 8192, 8200),
+                                             (2, 520, 1000, 784, 1004), (4, 4096, 2048, 4096, 2048),
+                                             (8, 8192, 4096, 8192, 4096)])
+def test_p2p_rs_forms_give_the_same_bits(b2g, cuda, world, M, N, K, ldc):
+    """Staged (copy-engine pushes), direct (remote stores) and fused (slot sum in the own
+    slab's GEMM epilogue, one launch fewer) give the same C bits; 520 x 1000 x 784 has 260-row
+    slabs (partial tiles) and 392-element K slabs (not a multiple of the 64-element stage);
+    ldc > N leaves the pad alone."""
+    if cuda.cuda.device_count() < world:
+        pytest.skip("needs %d GPUs" % world)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as d:
+        procs = [ctx.Process(target=shard_worker.nccl_p2p_rs_forms_rank,
+                             args=(r, world, os.path.join(d, "id"), M, N, K, ldc, q))
+                 for r in range(world)]
+        for p in procs:
+            p.start()
+        res = sorted(q.get(timeout=300) for _ in procs)
+        for p in procs:
+            p.join(timeout=120)
+    for rank, same, launches, bad, status, tb in res:
+        assert tb is None, tb
+        assert same and bad == 0 and status == 0, (rank, same, bad, status)
+        assert launches["fused"] == launches["direct"] - 1 == launches["staged"] - 1, launches
+
+
 def test_chain_single_rank(b2g, cuda):
     with tempfile.TemporaryDirectory() as d:
         q = _ListQueue()
