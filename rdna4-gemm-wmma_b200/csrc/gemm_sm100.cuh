@@ -676,22 +676,20 @@ __global__ void __launch_bounds__(Cfg<CG, BN, BMC, EW>::THREADS, 1)
         };
         const uint32_t part = base + (uint32_t)(q * 8 * 32 + lane) * 16u;
         ptx::fence_proxy_async_smem();
-        uint32_t w0[32], w1[32];
-        ptx::tmem_ld_32x32b_x32(tbase, w0);
+        // four chunks of TMEM loads in flight per wait (the wait is the cost here)
+        static_assert(C::CHUNKS % 4 == 0, "fix-up copies four chunks per TMEM wait");
 #pragma unroll 1
-        for (int ch = 0; ch < C::CHUNKS; ch += 2) {
-          ptx::tmem_ld_wait();
-          ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 1), w1);
+        for (int ch0 = 0; ch0 < C::CHUNKS; ch0 += 4) {
+          uint32_t w4[4][32];
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            ptx::st_shared_v4(part + (uint32_t)((ch * 4 * 8 + j) * 32) * 16u, w0[4 * j],
-                              w0[4 * j + 1], w0[4 * j + 2], w0[4 * j + 3]);
+          for (int c = 0; c < 4; ++c) ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch0 + c), w4[c]);
           ptx::tmem_ld_wait();
-          if (ch + 2 < C::CHUNKS) ptx::tmem_ld_32x32b_x32(tbase + 32u * (ch + 2), w0);
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            ptx::st_shared_v4(part + (uint32_t)(((ch + 1) * 4 * 8 + j) * 32) * 16u, w1[4 * j],
-                              w1[4 * j + 1], w1[4 * j + 2], w1[4 * j + 3]);
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              ptx::st_shared_v4(part + (uint32_t)(((ch0 + c) * 4 * 8 + j) * 32) * 16u,
+                                w4[c][4 * j], w4[c][4 * j + 1], w4[c][4 * j + 2], w4[c][4 * j + 3]);
         }
         release(acc);
         // Publish: after the epilogue warps' barrier one thread arrives (release, cluster
@@ -711,29 +709,29 @@ __global__ void __launch_bounds__(Cfg<CG, BN, BMC, EW>::THREADS, 1)
             float a[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) a[j] = 0.0f;
-            // Splits in order (deterministic sums); split r+1's loads are in flight while
-            // split r is added.
+            // Splits in order (deterministic sums), four splits' loads in flight at a time.
             const uint32_t off = part + (uint32_t)(ch * 4 * 8 * 32) * 16u;
-            float4 x[8], y[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              x[j] = ptx::ld_shared_cluster_v4(ptx::mapa(off, split_cta(0)) + (uint32_t)(j * 32) * 16u);
 #pragma unroll 1
-            for (int r = 0; r < ns; ++r) {
-              if (r + 1 < ns) {
-                const uint32_t src = ptx::mapa(off, split_cta(r + 1));
+            for (int r0 = 0; r0 < ns; r0 += 4) {
+              float4 x[4][8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) y[j] = ptx::ld_shared_cluster_v4(src + (uint32_t)(j * 32) * 16u);
+              for (int c = 0; c < 4; ++c) {
+                if (r0 + c >= ns) break;
+                const uint32_t src = ptx::mapa(off, split_cta(r0 + c));
+#pragma unroll
+                for (int j = 0; j < 8; ++j) x[c][j] = ptx::ld_shared_cluster_v4(src + (uint32_t)(j * 32) * 16u);
               }
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                a[4 * j] += x[j].x;
-                a[4 * j + 1] += x[j].y;
-                a[4 * j + 2] += x[j].z;
-                a[4 * j + 3] += x[j].w;
-              }
+              for (int c = 0; c < 4; ++c) {
+                if (r0 + c >= ns) break;
 #pragma unroll
-              for (int j = 0; j < 8; ++j) x[j] = y[j];
+                for (int j = 0; j < 8; ++j) {
+                  a[4 * j] += x[c][j].x;
+                  a[4 * j + 1] += x[c][j].y;
+                  a[4 * j + 2] += x[c][j].z;
+                  a[4 * j + 3] += x[c][j].w;
+                }
+              }
             }
             uint32_t vv[32];
 #pragma unroll
