@@ -628,6 +628,11 @@ def main():
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if clocks and clocks.get("sm_mhz"):
+        # clock-normalised rate: the per-GPU value per GHz of the median SM clock under load
+        clocks["tflops_per_ghz_per_gpu"] = value / ws / (clocks["sm_mhz"] / 1000.0)
+    if cublas and cublas.get("value") and (cublas.get("clocks") or {}).get("sm_mhz"):
+        cublas["clocks"]["tflops_per_ghz"] = cublas["value"] / (cublas["clocks"]["sm_mhz"] / 1000.0)
     print(json.dumps(line), flush=True)
     return 0
 
