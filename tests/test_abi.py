@@ -181,14 +181,22 @@ int main() {
     ((8192, 28672, 8192), (2, 512, 4, 1776)),       # configs[3]: 16 tail tiles split 4 ways
     ((16384, 16384, 4096), (2, 512, 1, 2048)),      # configs[3]: whole waves
     ((128, 8192, 8192), (1, 256, 4, 0)),            # configs[3] skinny: 32 tiles x 4 splits
-    ((1024, 1024, 1024), (1, 128, 1, 64)),          # configs[0]: 64 tiles, K too short to split
+    ((1024, 1024, 1024), (1, 128, 2, 0)),           # configs[0]: 64 tiles x 2 splits of 8 blocks
     ((256, 8192, 8192), (1, 256, 2, 0)),
     ((128, 2048, 8192), (1, 128, 8, 0)),
-    ((2048, 2048, 2048), (1, 256, 1, 128)),
+    ((512, 512, 2048), (1, 128, 4, 0)),             # four splits of 8 K blocks
+    ((256, 512, 1024), (1, 128, 2, 0)),
+    ((4096, 512, 1024), (1, 128, 1, 128)),          # tie: no 8-block splits
+    ((2048, 2048, 2048), (2, 256, 1, 64)),          # no split: 256x256 pairs, same CTAs
+    ((1024, 4096, 4096), (2, 256, 1, 64)),
+    ((2048, 4096, 4096), (2, 512, 1, 64)),          # one wave of 512-wide pair tiles
+    ((3072, 3072, 3072), (2, 512, 1, 72)),
 ])
 def test_plan_preview_choices(b2g, shape, plan):
-    """The launch plan for the BASELINE shapes and the small shapes whose choice was measured
-    (the width whose split units fill the SMs best; ties to 128x256)."""
+    """The launch plan for the BASELINE shapes and the small and mid shapes whose choice was
+    measured: split-K units of the width that fills the SMs best (ties to 128x256), else
+    256x256 pair tiles when no width splits, and 512-wide pair tiles whenever their waves fill
+    the pairs as well as 256-wide ones."""
     assert b2g.plan_preview(*shape) == plan
 
 
@@ -219,7 +227,8 @@ def test_plan_preview_follows_options(b2g):
 def test_plan_preview_invariants(b2g):
     """Random shapes, operand types and SM counts: the launch plan is always one the kernel can
     run.  Legal tile shapes; one-CTA tiles split at most 8 ways (the largest cluster of the
-    cluster fix-up), pairs at most 16; every split keeps at least 16 K blocks; the split units
+    cluster fix-up), pairs at most 16; every split keeps at least 16 K blocks (8 when one-CTA
+    tiles split every tile); the split units
     of one launch fit in the resident CTA groups; unsplit plans run every tile whole."""
     from hypothesis import given, settings, strategies as st
 
@@ -242,7 +251,7 @@ def test_plan_preview_invariants(b2g):
         if splits == 1:
             assert full == tiles
         else:
-            assert -(-k_iters // splits) >= 16
+            assert -(-k_iters // splits) >= (8 if (cg == 1 and rows == 128 and full == 0) else 16)
             groups = sms if cg == 1 else max(1, sms // 2)
             assert (tiles - full) * splits <= groups
 
