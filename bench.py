@@ -273,7 +273,7 @@ def run_all_configs(args):
     for label, extra in ALL_CONFIGS:
         steps = args.steps if "32768" not in extra[-1] else min(args.steps, 20)
         cmd = [sys.executable, os.path.abspath(__file__)] + extra + [
-            "--steps", str(steps), "--warmup", str(args.warmup)]
+            "--steps", str(steps), "--warmup", str(args.warmup)] + (["--graph"] if args.graph else [])
         res = subprocess.run(cmd, capture_output=True, text=True)
         lines = [l for l in res.stdout.splitlines() if l.startswith("{")]
         if res.returncode != 0 or not lines:
@@ -329,6 +329,11 @@ def main():
     ap.add_argument("--kernel-only", action="store_true",
                     help="device-resident GEMM steps only (no e2e, CPU baseline or clock "
                          "sampling): the command profiled with ncu")
+    ap.add_argument("--graph", action="store_true",
+                    help="one GPU: also time the step replayed from a CUDA graph (device time "
+                         "per step without host launch gaps), this library's and cuBLAS's")
+    ap.add_argument("--option", action="append", default=[], metavar="KEY=VALUE",
+                    help="set a library option (b2g_set_option) before timing; repeatable")
     ap.add_argument("--all-configs", action="store_true",
                     help="one JSON line per BASELINE config on one GPU (1024^3, 8192^3, the "
                          "configs[2] contraction, the three configs[3] shapes, 32768^3), each "
@@ -352,6 +357,9 @@ def main():
     if ws > 1:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     b2g = load_b2g()
+    for opt in args.option:
+        key, _, val = opt.partition("=")
+        b2g.set_option(key, int(val))
     if args.workload == "sharded32768":
         return run_sharded(args, torch, dist, b2g, ws, rank, local, dev)
     if args.workload == "tp_k":
@@ -423,25 +431,26 @@ def main():
         sys.stderr.write("rank %d/%d: B (%d MiB) along a copy-engine chain of %d ranks every "
                          "step\n" % (rank, ws, chain["bytes"] >> 20, ws))
 
-    def step():
+    def step(st=None):
+        st = stream if st is None else st
         if chain is not None:
             i = chain["n"]
             b = i % 2
             bcast(i + 1)
-            stream.wait_event(chain["bdone"][b])
-            b2g.gemm(dA, chain["bufs"][b], dC, M, N, K, K, N, N, stream)
-            chain["gdone"][b].record(stream)
+            st.wait_event(chain["bdone"][b])
+            b2g.gemm(dA, chain["bufs"][b], dC, M, N, K, K, N, N, st)
+            chain["gdone"][b].record(st)
             chain["n"] = i + 1
         elif contraction:
             b2g.contract5d(dA, a_shape, rowmajor(a_shape), dB, b_shape, rowmajor(b_shape), dC,
-                           c_shape, rowmajor(c_shape), stream)
+                           c_shape, rowmajor(c_shape), st)
         elif epilogue:
             b2g.gemm_epilogue(dA, dB, dC, M, N, K, dtype=dt, bias=dBias, c_dtype=c_dt,
-                              stream=stream)
+                              stream=st)
         elif dt:
-            b2g.gemm_typed(dA, dB, dC, M, N, K, dt, stream=stream)
+            b2g.gemm_typed(dA, dB, dC, M, N, K, dt, stream=st)
         else:
-            b2g.gemm(dA, dB, dC, M, N, K, K, N, N, stream)
+            b2g.gemm(dA, dB, dC, M, N, K, K, N, N, st)
 
     for _ in range(args.warmup):
         step()
@@ -519,6 +528,19 @@ def main():
     value = flops * ws * args.steps / (elapsed_ms * 1e-3) / 1e12
     avg_launch_ms = statistics.mean(launch_ms)
     achieved = flops / (avg_launch_ms * 1e-3) / 1e12
+
+    # ---- device time per step from CUDA graph replay (no host launch gaps), ours and cuBLAS's
+    graph = None
+    if args.graph and ws == 1:
+        calls = max(1, min(args.steps, 20 if flops < 2 ** 37 else 5))
+        us = graph_us_per_call(torch, lambda: step(torch.cuda.current_stream()), calls)
+        graph = {"us_per_step": us, "value": flops / (us * 1e-6) / 1e12, "unit": "TFLOP/s",
+                 "calls_per_graph": calls, "replays": 10}
+        if dt == 0 and not epilogue and not args.no_cublas:
+            cub = graph_us_per_call(torch, lambda: torch.mm(dA, dB, out_dtype=torch.float32),
+                                    calls)
+            graph["cublas_us_per_step"] = cub
+            graph["cublas_value"] = flops / (cub * 1e-6) / 1e12
 
     # ---- end to end through the C ABI with host buffers (pipelined over 3 streams)
     e2e = None
@@ -628,6 +650,10 @@ def main():
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if graph is not None:
+        line["graph"] = graph
+    if args.option:
+        line["config"]["options"] = dict(o.partition("=")[::2] for o in args.option)
     if clocks and clocks.get("sm_mhz"):
         # clock-normalised rate: the per-GPU value per GHz of the median SM clock under load
         clocks["tflops_per_ghz_per_gpu"] = value / ws / (clocks["sm_mhz"] / 1000.0)
@@ -829,6 +855,34 @@ def run_tp_k(args, torch, dist, b2g, ws, rank, local, dev):
             "row0_out_of_tolerance": bad, "device_status": status,
             "gpu_launches": launches}), flush=True)
     return 0
+
+
+def graph_us_per_call(torch, fn, calls, replays=10):
+    """Microseconds per call of `fn`, `calls` calls captured in one CUDA graph and the graph
+    replayed `replays` times between two events: device time with no host launch gaps (the
+    host cost of a call, about 10 us through Python, hides small kernels otherwise)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for _ in range(calls):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(replays):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) / (replays * calls) * 1000.0
 
 
 def cublas_side_by_side(torch, dA, dB, dC, gpu, steps):
