@@ -52,6 +52,19 @@ def test_gemm_full_size_exact(b2g, cuda, M, N, K):
     assert _exact_gemm(b2g, cuda, M, N, K, seed=M + N + K) == 0
 
 
+@pytest.mark.parametrize("M,N,K", [(512, 512, 2048), (1024, 1024, 1024), (2048, 2048, 2048),
+                                   (1024, 4096, 4096), (3072, 3072, 3072), (4096, 4096, 4096),
+                                   (4096, 512, 1024)],
+                         ids=["split4x8blocks", "configs0_split2", "pairs256_unsplit",
+                              "pairs256_wide", "pairs512_72tiles", "pairs512_128tiles",
+                              "n128_unsplit"])
+def test_gemm_planner_small_and_mid_shapes_exact(b2g, cuda, M, N, K):
+    """The plans the planner picks for small and mid-size shapes (one-CTA tiles split in 8-block
+    pieces, unsplit 256x256 pair tiles, one or two waves of 512-wide pair tiles), every element
+    exact."""
+    assert _exact_gemm(b2g, cuda, M, N, K, seed=M * 3 + N * 5 + K) == 0
+
+
 def test_gemm_32768_cubed_single_gpu_exact(b2g, cuda):
     """BASELINE configs[4]'s whole problem, 32768^3 (C is 4 GiB: 64-bit offsets in every
     address), on one GPU; every element exact."""
