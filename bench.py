@@ -529,18 +529,20 @@ def main():
     avg_launch_ms = statistics.mean(launch_ms)
     achieved = flops / (avg_launch_ms * 1e-3) / 1e12
 
-    # ---- device time per step from CUDA graph replay (no host launch gaps), ours and cuBLAS's
+    # ---- device time per step from CUDA graph replay (no host launch gaps), ours and cuBLAS's,
+    # their replays interleaved so that both see the same clocks under the power cap
     graph = None
     if args.graph and ws == 1:
         calls = max(1, min(args.steps, 20 if flops < 2 ** 37 else 5))
-        us = graph_us_per_call(torch, lambda: step(torch.cuda.current_stream()), calls)
-        graph = {"us_per_step": us, "value": flops / (us * 1e-6) / 1e12, "unit": "TFLOP/s",
-                 "calls_per_graph": calls, "replays": 10}
+        fns = [lambda: step(torch.cuda.current_stream())]
         if dt == 0 and not epilogue and not args.no_cublas:
-            cub = graph_us_per_call(torch, lambda: torch.mm(dA, dB, out_dtype=torch.float32),
-                                    calls)
-            graph["cublas_us_per_step"] = cub
-            graph["cublas_value"] = flops / (cub * 1e-6) / 1e12
+            fns.append(lambda: torch.mm(dA, dB, out_dtype=torch.float32))
+        us = graph_us_per_call(torch, fns, calls)
+        graph = {"us_per_step": us[0], "value": flops / (us[0] * 1e-6) / 1e12, "unit": "TFLOP/s",
+                 "calls_per_graph": calls, "replays": 10, "interleaved": len(us) > 1}
+        if len(us) > 1:
+            graph["cublas_us_per_step"] = us[1]
+            graph["cublas_value"] = flops / (us[1] * 1e-6) / 1e12
 
     # ---- end to end through the C ABI with host buffers (pipelined over 3 streams)
     e2e = None
@@ -857,32 +859,39 @@ def run_tp_k(args, torch, dist, b2g, ws, rank, local, dev):
     return 0
 
 
-def graph_us_per_call(torch, fn, calls, replays=10):
-    """Microseconds per call of `fn`, `calls` calls captured in one CUDA graph and the graph
-    replayed `replays` times between two events: device time with no host launch gaps (the
-    host cost of a call, about 10 us through Python, hides small kernels otherwise)."""
+def graph_us_per_call(torch, fns, calls, replays=10):
+    """Microseconds per call of each function in `fns`: `calls` calls of it captured in one CUDA
+    graph, the graphs replayed in turn (A, B, A, B, ...) `replays` times, each replay between
+    two events.  Device time with no host launch gaps (the host cost of a call, about 10 us
+    through Python, hides small kernels otherwise); taking turns gives every function the same
+    clocks under the power cap."""
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(s):
-        for _ in range(3):
-            fn()
-    torch.cuda.current_stream().wait_stream(s)
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=s):
-        for _ in range(calls):
-            fn()
-    g.replay()
-    torch.cuda.synchronize()
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(replays):
+    graphs = []
+    for fn in fns:
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(calls):
+                fn()
         g.replay()
-    b.record()
-    torch.cuda.synchronize()
-    del g
-    return a.elapsed_time(b) / (replays * calls) * 1000.0
+        torch.cuda.synchronize()
+        graphs.append(g)
+    total = [0.0] * len(fns)
+    for _ in range(replays):
+        for i, g in enumerate(graphs):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            total[i] += a.elapsed_time(b)
+    del graphs
+    return [t / (replays * calls) * 1000.0 for t in total]
 
 
 def cublas_side_by_side(torch, dA, dB, dC, gpu, steps):
