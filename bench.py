@@ -273,7 +273,7 @@ def run_all_configs(args):
     for label, extra in ALL_CONFIGS:
         steps = args.steps if "32768" not in extra[-1] else min(args.steps, 20)
         cmd = [sys.executable, os.path.abspath(__file__)] + extra + [
-            "--steps", str(steps), "--warmup", str(args.warmup)] + (["--graph"] if args.graph else [])
+            "--steps", str(steps), "--warmup", str(args.warmup)] + (["--no-graph"] if args.no_graph else [])
         res = subprocess.run(cmd, capture_output=True, text=True)
         lines = [l for l in res.stdout.splitlines() if l.startswith("{")]
         if res.returncode != 0 or not lines:
@@ -331,7 +331,9 @@ def main():
                          "sampling): the command profiled with ncu")
     ap.add_argument("--graph", action="store_true",
                     help="one GPU: also time the step replayed from a CUDA graph (device time "
-                         "per step without host launch gaps), this library's and cuBLAS's")
+                         "per step without host launch gaps), this library's and cuBLAS's in "
+                         "turn (on by default for one GPU; kept for older command lines)")
+    ap.add_argument("--no-graph", action="store_true", help="skip the CUDA graph timing")
     ap.add_argument("--option", action="append", default=[], metavar="KEY=VALUE",
                     help="set a library option (b2g_set_option) before timing; repeatable")
     ap.add_argument("--all-configs", action="store_true",
@@ -532,7 +534,7 @@ def main():
     # ---- device time per step from CUDA graph replay (no host launch gaps), ours and cuBLAS's,
     # their replays interleaved so that both see the same clocks under the power cap
     graph = None
-    if args.graph and ws == 1:
+    if not args.no_graph and ws == 1:
         calls = max(1, min(args.steps, 20 if flops < 2 ** 37 else 5))
         fns = [lambda: step(torch.cuda.current_stream())]
         if dt == 0 and not epilogue and not args.no_cublas:
